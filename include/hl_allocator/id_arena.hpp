@@ -1,0 +1,95 @@
+#pragma once
+// IdArena: per-sequence lists of block ids in one growable uint32 array, with
+// the dirty tracking that keeps a device copy current through patches.
+//
+// Drop-in for the reference's project1_allocator/include/hl_allocator/id_arena.hpp
+// (same public API, same observable results: offsets, capacities and patch
+// order).  A sequence owns one segment whose capacity is a power-of-two size
+// class (8 << k entries, 8 .. 2^31).  A full segment moves to one of the next
+// class, copying its entries; freed segments are kept per class (LIFO) and
+// reused; the array only grows.  Every write marks its entry; collect() turns
+// the marked entries into {offset, block_id} patches, each offset once, so a
+// device can apply them in any order.
+//
+// reserve() gives the strong guarantee: all allocation happens before any
+// state changes, so push_back(), release() and the dirty bookkeeping never
+// allocate and are noexcept.
+#include <array>
+#include <cstdint>
+#include <span>
+#include <string>
+#include <vector>
+
+#include "hl_allocator/status.hpp"
+
+namespace hl::alloc {
+
+/// arena[offset] = block_id on the device.
+struct IdPatch {
+  std::uint32_t offset;
+  std::uint32_t block_id;
+  friend constexpr bool operator==(IdPatch, IdPatch) noexcept = default;
+};
+
+/// What a kernel needs per sequence: block ids arena[offset .. offset + length).
+struct SequenceSegment {
+  std::uint32_t offset;
+  std::uint32_t length;
+  friend constexpr bool operator==(SequenceSegment, SequenceSegment) noexcept = default;
+};
+
+class IdArena {
+ public:
+  static constexpr std::uint32_t kMinSegment = 8;
+  static constexpr std::uint32_t kNumClasses = 29;  // 8 .. 2^31 entries
+  static constexpr std::uint32_t kMaxSegment = kMinSegment << (kNumClasses - 1);
+  /// Offsets are uint32 and 0xFFFFFFFF is reserved.
+  static constexpr std::uint64_t kMaxEntries = 0xFFFF'FFFFull;
+
+  /// A sequence's storage; capacity 0 = no storage yet.
+  struct Segment {
+    std::uint32_t offset = 0;
+    std::uint32_t capacity = 0;
+    std::uint32_t length = 0;
+  };
+
+  /// Makes seg.capacity >= needed, moving the segment if necessary.
+  /// kCapacityExceeded past kMaxSegment or kMaxEntries.  Strong guarantee.
+  [[nodiscard]] Status reserve(Segment& seg, std::uint32_t needed);
+  /// Appends one id.  Precondition: seg.length < seg.capacity.
+  void push_back(Segment& seg, std::uint32_t block_id) noexcept;
+  /// Returns the segment's storage to its class free list; seg becomes empty.
+  void release(Segment& seg) noexcept;
+
+  [[nodiscard]] std::span<const std::uint32_t> view(const Segment& seg) const noexcept;
+  [[nodiscard]] static SequenceSegment kernel_view(const Segment& seg) noexcept {
+    return seg.capacity == 0 ? SequenceSegment{0u, seg.length}
+                             : SequenceSegment{seg.offset, seg.length};
+  }
+
+  /// Replaces `out` with one patch per dirty entry (in marking order) and clears the marks.
+  void collect(std::vector<IdPatch>& out);
+
+  [[nodiscard]] std::uint32_t size() const noexcept {
+    return static_cast<std::uint32_t>(ids_.size());
+  }
+  [[nodiscard]] std::size_t pending_patches() const noexcept { return dirty_order_.size(); }
+  /// Total capacity parked on the free lists.
+  [[nodiscard]] std::uint64_t free_entries() const noexcept;
+
+  /// Checks that `live` plus the free lists tile the array exactly and that the
+  /// dirty bookkeeping is consistent; "" when it holds, else the first problem.
+  [[nodiscard]] std::string validate(std::span<const Segment> live) const;
+
+ private:
+  [[nodiscard]] Status carve_or_reuse(std::uint32_t size_class, std::uint32_t& offset);
+  void mark(std::uint32_t offset) noexcept;
+
+  std::vector<std::uint32_t> ids_;
+  std::vector<std::uint8_t> is_dirty_;       // per entry
+  std::vector<std::uint32_t> dirty_order_;   // offsets, unique; capacity >= ids_.size()
+  std::array<std::vector<std::uint32_t>, kNumClasses> parked_{};  // free offsets per class
+  std::array<std::uint32_t, kNumClasses> carved_{};               // segments created per class
+};
+
+}  // namespace hl::alloc
