@@ -1,0 +1,207 @@
+// Device-side element codecs shared by the sm_100a kernels.
+//
+// Decode contract (the reference's dequantize_reference_to_fp16,
+// project2_quant/src/cpu_dequant.cpp:93-141, on its x86-64 build):
+//   FP16  out = code, except NaN codes which become sign|0x7E00
+//   FP8   out = fp16_rn(fp32(decode(code)) * scale)             (two roundings)
+//         NaN codes -> sign|0x7E00; E5M2 +-Inf * 0 -> 0xFE00 (the SSE default NaN)
+//   INT4  out = fp16_rn(fmaf(float(q), scale, bias))            (one fused rounding)
+// Parameters must be finite, as the reference requires.  No fast-math anywhere:
+// products that are binary32 subnormals must not be flushed.
+//
+// Encode contract (quantize_reference, project2_quant/src/cpu_quant.cpp:27-170):
+// round-to-nearest-even with integer arithmetic, FP8 saturating, FP16 overflow to Inf.
+#pragma once
+
+#include <cuda_fp16.h>
+#include <cstdint>
+
+namespace hlkv {
+namespace dev {
+
+enum : uint32_t { kFp16 = 0, kE4M3 = 1, kE5M2 = 2, kInt4 = 3, kInvalidFormat = 15 };
+
+// Error bits (the HLKV_ERR_* values of include/hlkv.h).
+enum : uint32_t {
+  kErrNotExecutable = 1u << 0,
+  kErrBadFormat = 1u << 1,
+  kErrSlotRange = 1u << 2,
+  kErrArenaRange = 1u << 3,
+  kErrBlockIdRange = 1u << 4,
+  kErrValidTokens = 1u << 5,
+  kErrLayout = 1u << 6,
+  kErrScaleMode = 1u << 7,
+  kErrDescMismatch = 1u << 8,
+  kErrNonFinite = 1u << 9,
+  kErrTokenRange = 1u << 10,
+  kErrPatchRange = 1u << 11,
+  kErrOutAlign = 1u << 12,
+};
+
+__device__ __forceinline__ uint32_t f16_bits(float x) { return __half_as_ushort(__float2half_rn(x)); }
+
+// Two binary32 values -> two binary16 (RNE) packed lo | hi << 16.
+__device__ __forceinline__ uint32_t pack_f16x2(float lo, float hi) {
+  const __half2 h = __floats2half2_rn(lo, hi);
+  return *reinterpret_cast<const uint32_t*>(&h);
+}
+
+// ---- FP16 ------------------------------------------------------------------------------------
+
+// NaN halves (magnitude > 0x7C00) of a packed pair become sign|0x7E00.
+__device__ __forceinline__ uint32_t canon_f16x2(uint32_t w) {
+  const uint32_t nan = __vcmpgtu2(w & 0x7FFF7FFFu, 0x7C007C00u);  // 0xFFFF per NaN half
+  return (w & ~nan) | (nan & ((w & 0x80008000u) | 0x7E007E00u));
+}
+
+__device__ __forceinline__ uint4 canon_f16x8(uint4 v) {
+  return make_uint4(canon_f16x2(v.x), canon_f16x2(v.y), canon_f16x2(v.z), canon_f16x2(v.w));
+}
+
+// ---- FP8 decode ------------------------------------------------------------------------------
+
+// Exact value of a finite FP8 code: the code's exponent and mantissa bits are
+// placed in the binary32 exponent/mantissa fields (a binary32 normal or
+// subnormal) and rebiased by an exact power-of-two multiply.
+template <uint32_t kKind>
+__device__ __forceinline__ float fp8_finite_value(uint32_t b) {
+  if constexpr (kKind == kE4M3) {
+    return __fmul_rn(__uint_as_float(((b & 0x80u) << 24) | ((b & 0x7Fu) << 20)), 0x1p120f);
+  } else {
+    return __fmul_rn(__uint_as_float(((b & 0x80u) << 24) | ((b & 0x7Fu) << 21)), 0x1p112f);
+  }
+}
+
+// One element, including NaN and Inf codes.
+template <uint32_t kKind>
+__device__ __forceinline__ uint32_t fp8_to_f16(uint32_t b, float scale) {
+  if constexpr (kKind == kE4M3) {
+    if ((b & 0x7Fu) == 0x7Fu) return ((b & 0x80u) << 8) | 0x7E00u;
+  } else {
+    if ((b & 0x7Cu) == 0x7Cu) {
+      if (b & 3u) return ((b & 0x80u) << 8) | 0x7E00u;  // NaN
+      if (scale == 0.0f) return 0xFE00u;                // Inf * 0: SSE default NaN
+      const float inf = __int_as_float((b & 0x80u) ? 0xFF800000 : 0x7F800000);
+      return f16_bits(__fmul_rn(inf, scale));
+    }
+  }
+  return f16_bits(__fmul_rn(fp8_finite_value<kKind>(b), scale));
+}
+
+// True when any of the 4 codes of `w` is a NaN (E4M3) or an Inf/NaN (E5M2).
+template <uint32_t kKind>
+__device__ __forceinline__ bool fp8_has_special(uint32_t w) {
+  if constexpr (kKind == kE4M3) return __vcmpeq4(w & 0x7F7F7F7Fu, 0x7F7F7F7Fu) != 0;
+  else return __vcmpeq4(w & 0x7C7C7C7Cu, 0x7C7C7C7Cu) != 0;
+}
+
+// Per-element path for 8 codes that include a NaN or Inf code (rare): kept out
+// of line so the common path stays small in registers.
+template <uint32_t kKind>
+__device__ __noinline__ uint4 fp8x8_to_f16_special(uint2 c, float scale) {
+  uint32_t r[4];
+#pragma unroll
+  for (int k = 0; k < 4; ++k) {
+    const uint32_t w = k < 2 ? c.x : c.y;
+    const uint32_t sh = (k & 1) * 16;
+    r[k] = fp8_to_f16<kKind>((w >> sh) & 0xFFu, scale) |
+           (fp8_to_f16<kKind>((w >> (sh + 8)) & 0xFFu, scale) << 16);
+  }
+  return make_uint4(r[0], r[1], r[2], r[3]);
+}
+
+// Eight codes (little-endian in a uint2) -> eight binary16 in a uint4.
+template <uint32_t kKind>
+__device__ __forceinline__ uint4 fp8x8_to_f16(uint2 c, float scale) {
+  if (fp8_has_special<kKind>(c.x) | fp8_has_special<kKind>(c.y)) {
+    return fp8x8_to_f16_special<kKind>(c, scale);
+  }
+  uint32_t r[4];
+#pragma unroll
+  for (int k = 0; k < 4; ++k) {
+    const uint32_t w = k < 2 ? c.x : c.y;
+    const uint32_t sh = (k & 1) * 16;
+    const float lo = __fmul_rn(fp8_finite_value<kKind>((w >> sh) & 0xFFu), scale);
+    const float hi = __fmul_rn(fp8_finite_value<kKind>((w >> (sh + 8)) & 0xFFu), scale);
+    r[k] = pack_f16x2(lo, hi);
+  }
+  return make_uint4(r[0], r[1], r[2], r[3]);
+}
+
+// ---- INT4 decode -----------------------------------------------------------------------------
+
+// q (0..15) as binary32, exactly: (2^23 + q) - 2^23.
+__device__ __forceinline__ float nibble_value(uint32_t q) {
+  return __fsub_rn(__uint_as_float(0x4B000000u | q), 8388608.0f);
+}
+
+// Eight nibbles (element 2k in the low nibble of byte k) -> eight binary16.
+__device__ __forceinline__ uint4 int4x8_to_f16(uint32_t w, float scale, float bias) {
+  uint32_t r[4];
+#pragma unroll
+  for (int k = 0; k < 4; ++k) {
+    const float lo = __fmaf_rn(nibble_value((w >> (8 * k)) & 0xFu), scale, bias);
+    const float hi = __fmaf_rn(nibble_value((w >> (8 * k + 4)) & 0xFu), scale, bias);
+    r[k] = pack_f16x2(lo, hi);
+  }
+  return make_uint4(r[0], r[1], r[2], r[3]);
+}
+
+__device__ __forceinline__ uint32_t int4_to_f16(uint32_t q, float scale, float bias) {
+  return f16_bits(__fmaf_rn(nibble_value(q), scale, bias));
+}
+
+// ---- encoders --------------------------------------------------------------------------------
+
+// binary32 -> minifloat with round-to-nearest-even on the integer significand
+// (the method of project2_quant/src/cpu_quant.cpp:27-64).
+template <uint32_t kEBits, uint32_t kMBits, int kBias, bool kSaturate, uint32_t kMaxCode,
+          uint32_t kNanCode, uint32_t kInfCode>
+__device__ __forceinline__ uint32_t encode_minifloat(float x) {
+  const uint32_t bits = __float_as_uint(x);
+  const uint32_t sign = (bits >> 31) << (kEBits + kMBits);
+  const uint32_t mag = bits & 0x7FFFFFFFu;
+  constexpr uint32_t kOverflow = kSaturate ? kMaxCode : kInfCode;
+  if (mag > 0x7F800000u) return sign | kNanCode;
+  if (mag == 0x7F800000u) return sign | kOverflow;
+  constexpr int kEmin = 1 - kBias;
+  int binade, lsb_exp;
+  uint32_t sig;
+  if (mag >= 0x00800000u) {
+    const int e = static_cast<int>(mag >> 23) - 127;
+    sig = (mag & 0x007FFFFFu) | 0x00800000u;
+    lsb_exp = e - 23;
+    binade = e < kEmin ? kEmin : e;
+  } else {
+    sig = mag;
+    lsb_exp = -149;
+    binade = kEmin;
+  }
+  const int drop = (binade - static_cast<int>(kMBits)) - lsb_exp;  // >= 1
+  uint32_t kept = 0;  // drop >= 32: sig < 2^24 is below half a spacing, rounds to 0
+  if (drop < 32) {
+    kept = sig >> drop;
+    const uint32_t rest = sig & ((1u << drop) - 1u);
+    const uint32_t half = 1u << (drop - 1);
+    if (rest > half || (rest == half && (kept & 1u))) kept += 1u;
+  }
+  const uint32_t code = (static_cast<uint32_t>(binade - kEmin) << kMBits) + kept;
+  return sign | (code > kMaxCode ? kOverflow : code);
+}
+
+__device__ __forceinline__ uint32_t encode_e4m3(float x) {
+  return encode_minifloat<4, 3, 7, true, 0x7Eu, 0x7Fu, 0u>(x);
+}
+__device__ __forceinline__ uint32_t encode_e5m2(float x) {
+  return encode_minifloat<5, 2, 15, true, 0x7Bu, 0x7Fu, 0x7Cu>(x);
+}
+__device__ __forceinline__ uint32_t encode_f16(float x) {
+  return encode_minifloat<5, 10, 15, false, 0x7BFFu, 0x7E00u, 0x7C00u>(x);
+}
+
+__device__ __forceinline__ bool finite_f32(float x) {
+  return (__float_as_uint(x) & 0x7F800000u) != 0x7F800000u;
+}
+
+}  // namespace dev
+}  // namespace hlkv

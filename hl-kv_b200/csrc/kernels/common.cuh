@@ -1,0 +1,35 @@
+// Launch helpers shared by the kernels: device attributes cached per device,
+// the per-thread last CUDA error, and cache-hinted loads and stores.
+#pragma once
+
+#include <cuda_runtime.h>
+
+#include <cstdint>
+
+#include "hlkv.h"
+
+namespace hlkv {
+
+/// Records `e` as this thread's last CUDA error and maps it to an HLKV status.
+int cuda_status(cudaError_t e) noexcept;
+
+/// Number of SMs of the current device (cached per device).
+int sm_count() noexcept;
+
+/// Bytes of the code region of a layout slot (the parameters follow it).
+uint64_t layout_code_bytes(int format, uint64_t elems);
+/// A layout the kernels support (block_tokens 1..512, head_dim 64/128/256, ...).
+bool layout_ok(const HlkvLayout* l);
+
+namespace dev {
+
+// Streaming (evict-first) global loads and stores: the payload is read once and
+// the FP16 output is consumed by another kernel, so neither should displace
+// the descriptor table and arena from L2.
+__device__ __forceinline__ uint4 ld_stream(const uint4* p) { return __ldcs(p); }
+__device__ __forceinline__ uint2 ld_stream(const uint2* p) { return __ldcs(p); }
+__device__ __forceinline__ uint32_t ld_stream(const uint32_t* p) { return __ldcs(p); }
+__device__ __forceinline__ void st_stream(uint4* p, uint4 v) { __stcs(p, v); }
+
+}  // namespace dev
+}  // namespace hlkv

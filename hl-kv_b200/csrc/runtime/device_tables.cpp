@@ -1,0 +1,175 @@
+// hl::kv::DeviceTables (include/hl_kv/device_tables.hpp).
+#include "hl_kv/device_tables.hpp"
+
+#include <cuda_runtime_api.h>
+
+#include <cstring>
+
+#include "hlkv.h"
+
+namespace hlkv {
+int cuda_status(cudaError_t e) noexcept;
+}
+
+namespace hl::kv {
+namespace {
+
+using quant::QuantStatus;
+
+DeviceStatus from_cuda(cudaError_t e) {
+  (void)hlkv::cuda_status(e);
+  return e == cudaSuccess ? DeviceStatus{} : DeviceStatus{QuantStatus::kCudaError, e};
+}
+
+template <typename T>
+cudaError_t device_alloc(T** p, std::size_t bytes) {
+  return cudaMalloc(reinterpret_cast<void**>(p), bytes);
+}
+
+// Makes `device` current for the scope of one call.
+class DeviceGuard {
+ public:
+  explicit DeviceGuard(int device) {
+    if (cudaGetDevice(&prev_) == cudaSuccess && prev_ != device) {
+      ok_ = cudaSetDevice(device) == cudaSuccess;
+      restore_ = true;
+    }
+  }
+  ~DeviceGuard() {
+    if (restore_) (void)cudaSetDevice(prev_);
+  }
+  [[nodiscard]] bool ok() const noexcept { return ok_; }
+
+ private:
+  int prev_ = 0;
+  bool ok_ = true;
+  bool restore_ = false;
+};
+
+}  // namespace
+
+DeviceTables::DeviceTables() { (void)cudaGetDevice(&device_); }
+
+DeviceTables::~DeviceTables() {
+  DeviceGuard g(device_);
+  if (staging_free_ != nullptr) {
+    (void)cudaEventSynchronize(staging_free_);
+    (void)cudaEventDestroy(staging_free_);
+  }
+  // The owner must not destroy the tables while kernels that read them are
+  // queued; a device-wide sync makes the frees below safe regardless.
+  (void)cudaDeviceSynchronize();
+  if (d_table_ != nullptr) (void)cudaFree(d_table_);
+  if (d_arena_ != nullptr) (void)cudaFree(d_arena_);
+  if (d_err_ != nullptr) (void)cudaFree(d_err_);
+  if (d_staging_ != nullptr) (void)cudaFree(d_staging_);
+  if (h_staging_ != nullptr) (void)cudaFreeHost(h_staging_);
+}
+
+DeviceStatus DeviceTables::reserve_staging(std::size_t bytes, cudaStream_t stream) {
+  if (bytes <= staging_bytes_) {
+    // The previous upload must have read the pinned buffer before it is rewritten.
+    if (staging_free_ != nullptr) return from_cuda(cudaEventSynchronize(staging_free_));
+    return {};
+  }
+  std::size_t cap = staging_bytes_ == 0 ? std::size_t{64} << 10 : staging_bytes_;
+  while (cap < bytes) cap *= 2;
+  // The old buffers may still feed a queued upload / kernel.
+  if (const cudaError_t e = cudaStreamSynchronize(stream); e != cudaSuccess) return from_cuda(e);
+  if (d_staging_ != nullptr) (void)cudaFree(d_staging_);
+  if (h_staging_ != nullptr) (void)cudaFreeHost(h_staging_);
+  d_staging_ = nullptr;
+  h_staging_ = nullptr;
+  staging_bytes_ = 0;
+  if (const cudaError_t e = cudaMallocHost(&h_staging_, cap); e != cudaSuccess) return from_cuda(e);
+  if (const cudaError_t e = cudaMalloc(&d_staging_, cap); e != cudaSuccess) return from_cuda(e);
+  staging_bytes_ = cap;
+  return {};
+}
+
+DeviceStatus DeviceTables::sync(alloc::HeteroBlockTable& table, cudaStream_t stream) {
+  table.collect_delta(delta_);
+  return apply(delta_, stream);
+}
+
+DeviceStatus DeviceTables::apply(const alloc::ExecDelta& delta, cudaStream_t stream) {
+  DeviceGuard g(device_);
+  if (!g.ok()) return from_cuda(cudaErrorInvalidDevice);
+  if (d_err_ == nullptr) {
+    if (const cudaError_t e = device_alloc(&d_err_, sizeof(std::uint32_t)); e != cudaSuccess) {
+      d_err_ = nullptr;
+      return from_cuda(e);
+    }
+    if (const cudaError_t e = cudaMemsetAsync(d_err_, 0, sizeof(std::uint32_t), stream);
+        e != cudaSuccess) {
+      return from_cuda(e);
+    }
+    if (const cudaError_t e = cudaEventCreateWithFlags(&staging_free_, cudaEventDisableTiming);
+        e != cudaSuccess) {
+      staging_free_ = nullptr;
+      return from_cuda(e);
+    }
+  }
+  if (delta.descriptor_table_size != table_size_) {
+    // A table has a fixed size; this happens once, on the first delta.
+    if (const cudaError_t e = cudaStreamSynchronize(stream); e != cudaSuccess) return from_cuda(e);
+    if (d_table_ != nullptr) (void)cudaFree(d_table_);
+    d_table_ = nullptr;
+    table_size_ = 0;
+    if (delta.descriptor_table_size > 0) {
+      if (const cudaError_t e = device_alloc(&d_table_, std::size_t{delta.descriptor_table_size} * 16);
+          e != cudaSuccess) {
+        d_table_ = nullptr;
+        return from_cuda(e);
+      }
+    }
+    table_size_ = delta.descriptor_table_size;
+  }
+  if (delta.arena_size > arena_capacity_) {
+    std::uint64_t cap = arena_capacity_ == 0 ? 1024 : 2ull * arena_capacity_;
+    if (cap < delta.arena_size) cap = delta.arena_size;
+    if (cap > 0xFFFFFFFFull) cap = 0xFFFFFFFFull;
+    std::uint32_t* fresh = nullptr;
+    if (const cudaError_t e = device_alloc(&fresh, cap * 4); e != cudaSuccess) return from_cuda(e);
+    if (d_arena_ != nullptr) {
+      // Keep the contents (the protocol grows the arena, it never rewrites it).
+      if (const cudaError_t e = cudaMemcpyAsync(fresh, d_arena_, std::size_t{arena_size_} * 4,
+                                                cudaMemcpyDeviceToDevice, stream);
+          e != cudaSuccess) {
+        (void)cudaFree(fresh);
+        return from_cuda(e);
+      }
+      // The old buffer may still be read by queued kernels on this stream.
+      if (const cudaError_t e = cudaStreamSynchronize(stream); e != cudaSuccess) return from_cuda(e);
+      (void)cudaFree(d_arena_);
+    }
+    d_arena_ = fresh;
+    arena_capacity_ = static_cast<std::uint32_t>(cap);
+  }
+  arena_size_ = delta.arena_size;
+
+  const std::size_t n_desc = delta.descriptor_patches.size(), n_id = delta.id_patches.size();
+  const std::size_t bytes = 16 * n_desc + 8 * n_id;
+  if (bytes == 0) return {};
+  if (DeviceStatus s = reserve_staging(bytes, stream); !s.ok()) return s;
+  auto* h = static_cast<unsigned char*>(h_staging_);
+  if (n_desc > 0) std::memcpy(h, delta.descriptor_patches.data(), 16 * n_desc);
+  if (n_id > 0) std::memcpy(h + 16 * n_desc, delta.id_patches.data(), 8 * n_id);
+  if (const cudaError_t e = cudaMemcpyAsync(d_staging_, h_staging_, bytes, cudaMemcpyHostToDevice, stream);
+      e != cudaSuccess) {
+    return from_cuda(e);
+  }
+  if (const cudaError_t e = cudaEventRecord(staging_free_, stream); e != cudaSuccess) return from_cuda(e);
+  auto* d = static_cast<unsigned char*>(d_staging_);
+  const int st = hlkv_apply_delta(
+      reinterpret_cast<HlkvExecDescriptor*>(d_table_), table_size_, d_arena_, arena_size_,
+      reinterpret_cast<const HlkvExecDescriptor*>(d), static_cast<std::uint32_t>(n_desc),
+      reinterpret_cast<const HlkvIdPatch*>(d + 16 * n_desc), static_cast<std::uint32_t>(n_id), d_err_,
+      reinterpret_cast<hlkv_stream_t>(stream));
+  if (st != HLKV_OK) {
+    return DeviceStatus{static_cast<QuantStatus>(st), static_cast<cudaError_t>(hlkv_last_cuda_error())};
+  }
+  return {};
+}
+
+}  // namespace hl::kv

@@ -1,0 +1,67 @@
+#pragma once
+// hl::kv::DeviceTables -- the GPU-resident copy of a HeteroBlockTable's
+// device-facing state (descriptor table + id arena), kept current with deltas.
+//
+// The reference defines the protocol (hetero_block_table.hpp:100-114,
+// hl_allocator_abi.md section 5) but only simulates the device side on the
+// host (tests/project1/exec_mirror.hpp).  Here sync() runs it for real, in
+// stream order on the caller's stream:
+//   1. table.collect_delta() on the host;
+//   2. grow the device arena when delta.arena_size exceeds its capacity (a
+//      larger allocation, the old contents copied device-to-device, then the
+//      old buffer freed after the stream drains); the descriptor table is
+//      allocated once at max_blocks entries;
+//   3. copy the patches into pinned staging and upload them;
+//   4. run kernel (3) (hlkv_apply_delta).
+// Kernels issued later on the same stream see the updated tables.  One
+// DeviceTables per table and device, used from the table's first delta on;
+// not thread-safe (like the table).
+#include <cuda_runtime_api.h>
+
+#include <cstdint>
+
+#include "hl_allocator/hetero_block_table.hpp"
+#include "hl_quant/cuda_dequant.hpp"
+
+namespace hl::kv {
+
+using hl::quant::cuda::DeviceStatus;
+
+class DeviceTables {
+ public:
+  /// Binds to the current CUDA device.  Nothing is allocated before sync().
+  DeviceTables();
+  ~DeviceTables();
+  DeviceTables(const DeviceTables&) = delete;
+  DeviceTables& operator=(const DeviceTables&) = delete;
+
+  /// collect_delta() + upload + apply on `stream`.
+  [[nodiscard]] DeviceStatus sync(alloc::HeteroBlockTable& table, cudaStream_t stream);
+  /// Uploads and applies an already collected delta.
+  [[nodiscard]] DeviceStatus apply(const alloc::ExecDelta& delta, cudaStream_t stream);
+
+  [[nodiscard]] const alloc::BlockExecDescriptor* table() const noexcept { return d_table_; }
+  [[nodiscard]] std::uint32_t table_size() const noexcept { return table_size_; }
+  [[nodiscard]] const std::uint32_t* arena() const noexcept { return d_arena_; }
+  [[nodiscard]] std::uint32_t arena_size() const noexcept { return arena_size_; }
+  /// Device word that kernel (3) reports HLKV_ERR_PATCH_RANGE into.
+  [[nodiscard]] std::uint32_t* error_word() const noexcept { return d_err_; }
+
+ private:
+  [[nodiscard]] DeviceStatus reserve_staging(std::size_t bytes, cudaStream_t stream);
+
+  int device_ = 0;
+  alloc::BlockExecDescriptor* d_table_ = nullptr;
+  std::uint32_t table_size_ = 0;
+  std::uint32_t* d_arena_ = nullptr;
+  std::uint32_t arena_size_ = 0;
+  std::uint32_t arena_capacity_ = 0;
+  std::uint32_t* d_err_ = nullptr;
+  void* h_staging_ = nullptr;   // pinned
+  void* d_staging_ = nullptr;
+  std::size_t staging_bytes_ = 0;
+  cudaEvent_t staging_free_ = nullptr;  // recorded after the upload that reads h_staging_
+  alloc::ExecDelta delta_;
+};
+
+}  // namespace hl::kv

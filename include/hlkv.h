@@ -1,0 +1,333 @@
+/*
+ * hlkv.h -- C ABI of the HL-KV quantized KV-block path on NVIDIA B200 (sm_100a).
+ *
+ * One shared library, libhlkv.so, behind plain C types: pointers, sizes and a
+ * CUDA stream handle.  It binds from any FFI (ctypes, cgo, JNI, N-API).  The
+ * C++20 API that the reference exposes (hl::alloc::HeteroBlockTable,
+ * hl::alloc::IdArena, hl::quant::cuda::dequantize_fp8_to_fp16) is in
+ * include/hl_allocator/ and include/hl_quant/; this header is the flat view
+ * of the same objects, and the only way into the CUDA kernels.
+ *
+ * Conventions
+ *  - Device entry points are asynchronous on `stream`, launch nothing on an
+ *    argument error (outputs untouched), and treat n == 0 as a no-op.
+ *    They return an HLKV_* status; HLKV_CUDA_ERROR carries the cudaError_t in
+ *    hlkv_last_cuda_error() (per thread).
+ *  - Per-block problems found on the device (a non-executable descriptor, an
+ *    index out of range, ...) never fault: the block is skipped and its
+ *    HLKV_ERR_* bit is OR-ed into *d_err (device memory, one uint32_t the
+ *    caller owns and clears).
+ *  - Table entry points return an hl::alloc::Status value (HLKV_STATUS_*).
+ *  - The caller owns every device buffer; no entry point allocates device
+ *    memory except hlkv_device_tables_* (the persistent table mirror).
+ */
+#ifndef HLKV_H_
+#define HLKV_H_
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+#define HLKV_ABI_VERSION 1 /* == hl::alloc::kAbiVersion */
+
+/* A CUDA stream (the same type as cudaStream_t / CUstream). NULL = legacy default stream. */
+typedef struct CUstream_st* hlkv_stream_t;
+
+/* ---- device status (== hl::quant::QuantStatus, quant_types.hpp:54-60) ------------------- */
+enum {
+  HLKV_OK = 0,
+  HLKV_INVALID_ARGUMENT = 1,
+  HLKV_BUFFER_TOO_SMALL = 2,
+  HLKV_UNSUPPORTED_FORMAT = 3,
+  HLKV_CUDA_ERROR = 4
+};
+
+/* ---- table status (== hl::alloc::Status, status.hpp:17-30) ---------------------------- */
+enum {
+  HLKV_STATUS_OK = 0,
+  HLKV_STATUS_OUT_OF_BLOCKS = 1,
+  HLKV_STATUS_OUT_OF_SLOTS = 2,
+  HLKV_STATUS_INVALID_HANDLE = 3,
+  HLKV_STATUS_STALE_HANDLE = 4,
+  HLKV_STATUS_INVALID_STATE = 5,
+  HLKV_STATUS_INVALID_ARGUMENT = 6,
+  HLKV_STATUS_UNKNOWN_FORMAT = 7,
+  HLKV_STATUS_NOT_DEVICE_RESIDENT = 8,
+  HLKV_STATUS_REFCOUNT_OVERFLOW = 9,
+  HLKV_STATUS_CORRUPT = 10,
+  HLKV_STATUS_CAPACITY_EXCEEDED = 11
+};
+
+/* ---- formats (== hl::quant::QuantFormat, quant_types.hpp:40-46) --------------------- */
+enum { HLKV_FP16 = 0, HLKV_FP8_E4M3 = 1, HLKV_FP8_E5M2 = 2, HLKV_INT4 = 3, HLKV_INVALID_FORMAT = 15 };
+
+/* ---- per-block error bits written to *d_err ------------------------------------------ */
+enum {
+  HLKV_ERR_NOT_EXECUTABLE = 1u << 0,  /* descriptor format 15 (free / not resident)    */
+  HLKV_ERR_BAD_FORMAT = 1u << 1,      /* no pool for the format, or not decodable     */
+  HLKV_ERR_SLOT_RANGE = 1u << 2,      /* slot >= num_slots of its pool                */
+  HLKV_ERR_ARENA_RANGE = 1u << 3,     /* segment offset + j >= arena_size             */
+  HLKV_ERR_BLOCK_ID_RANGE = 1u << 4,  /* arena entry / target id >= table_size        */
+  HLKV_ERR_VALID_TOKENS = 1u << 5,    /* valid_tokens > block_tokens                  */
+  HLKV_ERR_LAYOUT = 1u << 6,          /* descriptor layout tag != layout->layout_id   */
+  HLKV_ERR_SCALE_MODE = 1u << 7,      /* quantized block with scale_mode != kNone     */
+  HLKV_ERR_DESC_MISMATCH = 1u << 8,   /* table[id].block_id != id                     */
+  HLKV_ERR_NONFINITE = 1u << 9,       /* a group with a non-finite value was skipped  */
+  HLKV_ERR_TOKEN_RANGE = 1u << 10,    /* append target token >= block_tokens          */
+  HLKV_ERR_PATCH_RANGE = 1u << 11,    /* delta patch target out of range              */
+  HLKV_ERR_OUT_ALIGN = 1u << 12       /* output offset not a multiple of 8 elements   */
+};
+
+/* ---- ABI records (byte-identical to hl::alloc, block_descriptor.hpp:137-150 and
+ *      id_arena.hpp:315-326) -------------------------------------------------------------- */
+typedef struct {
+  uint32_t slot;
+  uint32_t info; /* format:4 | scale_mode:2 | layout:4 | valid_tokens:10 | 0:12 */
+  uint32_t scale_ref;
+  uint32_t block_id;
+} HlkvExecDescriptor;
+
+typedef struct {
+  uint32_t offset;
+  uint32_t block_id;
+} HlkvIdPatch;
+
+typedef struct {
+  uint32_t offset;
+  uint32_t length;
+} HlkvSegment;
+
+/* ---- payload pools and layout -------------------------------------------------------- */
+/* Pool of one format: slot s starts at base + s * slot_bytes (block_descriptor.hpp:144).  */
+typedef struct {
+  void* base;          /* device pointer, 16-byte aligned; NULL = no pool for this format */
+  uint64_t slot_bytes; /* multiple of 16, >= hlkv_layout_slot_bytes(format, layout)      */
+  uint32_t num_slots;
+  uint32_t reserved;   /* 0 */
+} HlkvPool;
+
+typedef struct {
+  HlkvPool pool[15]; /* indexed by format code */
+} HlkvPools;
+
+/*
+ * Payload layout of a block (the "layout" tag of the descriptor):
+ * 2 (K, V) x block_tokens x kv_heads rows of head_dim elements, row-major in
+ * that order, one parameter group per row.  A slot holds the codes of all rows
+ * (packed_bytes(format, rows * head_dim)) followed by the row parameters:
+ * nothing for FP16, one binary32 scale per row for FP8, one {scale, bias}
+ * binary32 pair per row for INT4.  head_dim is 64, 128 or 256.
+ */
+typedef struct {
+  uint32_t block_tokens; /* 1 .. 512 */
+  uint32_t kv_heads;     /* >= 1 */
+  uint32_t head_dim;     /* 64, 128 or 256 */
+  uint32_t layout_id;    /* descriptors must carry this tag (0 .. 15) */
+} HlkvLayout;
+
+/* Bytes one slot of `format` needs under `layout` (0 for an unsupported format/layout). */
+uint64_t hlkv_layout_slot_bytes(int format, const HlkvLayout* layout);
+
+/* The cudaError_t of this thread's last HLKV_CUDA_ERROR (cudaSuccess otherwise). */
+int hlkv_last_cuda_error(void);
+
+/* ---- kernel (1): heterogeneous gather-dequant ------------------------------------------ */
+/*
+ * For every sequence i < nseq and block j < d_segs[i].length:
+ *   d = d_table[d_arena[d_segs[i].offset + j]]          (hetero_block_table.hpp:22-25)
+ *   payload = pools->pool[d.format].base + d.slot * slot_bytes
+ *   out block = d_out + off_i + j * block_elems,  block_elems = 2*T*H*D,
+ *   off_i = d_out_offsets[i] (elements, multiple of 8), or the packed prefix
+ *           sum of the lengths * block_elems when d_out_offsets is NULL.
+ * Rows of tokens < valid_tokens are decoded per hl::quant's
+ * dequantize_reference_to_fp16 (cpu_dequant.cpp:127-141), bit for bit; rows of
+ * later tokens are written as +0.  A block failing a check is skipped and its
+ * bit set in *d_err.  The reference has no gather; its per-block semantics are
+ * the reference's CPU decoder.
+ */
+int hlkv_gather_dequant(const HlkvPools* pools, const HlkvLayout* layout,
+                        const HlkvExecDescriptor* d_table, uint32_t table_size,
+                        const uint32_t* d_arena, uint32_t arena_size, const HlkvSegment* d_segs,
+                        uint32_t nseq, uint16_t* d_out, const uint64_t* d_out_offsets,
+                        uint32_t* d_err, hlkv_stream_t stream);
+
+/* ---- kernel (2): append-encode ---------------------------------------------------------- */
+typedef struct {
+  uint32_t block_id; /* resolved through d_table */
+  uint32_t token;    /* token slot inside the block, < block_tokens */
+} HlkvAppendTarget;
+
+/*
+ * Encodes d_tokens[k] (binary16, [2][kv_heads][head_dim]) into token slot
+ * d_targets[k].token of block d_targets[k].block_id, in the block's format:
+ * each row is one group of quantize_reference (cpu_quant.cpp:97-170) on the
+ * binary32 values of the inputs -- FP8 scale = max(amax/max_finite, FLT_MIN)
+ * (1 when amax == 0), INT4 {scale = (max-min)/15, bias = min} -- codes and
+ * parameters bit-exact.  A row with a non-finite input is skipped
+ * (HLKV_ERR_NONFINITE), as quantize_reference rejects it.  Targets must be
+ * distinct (block, token) pairs.  valid_tokens is not changed here: the host
+ * table's set_valid_tokens + delta (kernel 3) does that.
+ */
+int hlkv_append_encode(const HlkvPools* pools, const HlkvLayout* layout,
+                       const HlkvExecDescriptor* d_table, uint32_t table_size,
+                       const HlkvAppendTarget* d_targets, uint32_t n, const uint16_t* d_tokens,
+                       uint32_t* d_err, hlkv_stream_t stream);
+
+/* ---- kernel (3): delta apply ------------------------------------------------------------ */
+/*
+ * Applies one hl::alloc::ExecDelta (hetero_block_table.hpp:100-114) to device
+ * tables that already have room for it:
+ *   d_table[p.block_id] = p  for each descriptor patch,
+ *   d_arena[p.offset] = p.block_id  for each id patch.
+ * Targets are unique per list, so all patches go in parallel.  Out-of-range
+ * targets are skipped with HLKV_ERR_PATCH_RANGE.  The device restatement of
+ * the reference's ExecMirror::apply (tests/project1/exec_mirror.hpp:23-49).
+ */
+int hlkv_apply_delta(HlkvExecDescriptor* d_table, uint32_t table_size, uint32_t* d_arena,
+                     uint32_t arena_size, const HlkvExecDescriptor* d_desc_patches,
+                     uint32_t n_desc, const HlkvIdPatch* d_id_patches, uint32_t n_id,
+                     uint32_t* d_err, hlkv_stream_t stream);
+
+/* ---- flat codecs ------------------------------------------------------------------------ */
+/*
+ * Drop-in for hl::quant::cuda::dequantize_fp8_to_fp16 (cuda_dequant.hpp:47-50,
+ * dequant_kernel.cu:244-264): out[i] = fp16_rn(decode_fp8(in[i]) * params[i/group].scale),
+ * any alignment, any group size >= 1.  d_params holds {scale, bias} binary32
+ * pairs (AffineParams); only scale is read.
+ */
+int hlkv_dequantize_fp8_to_fp16(int format, const void* d_in, size_t n, const float* d_params,
+                                size_t group_size, uint16_t* d_out, hlkv_stream_t stream);
+
+/*
+ * Device counterpart of hl::quant::dequantize_reference_to_fp16
+ * (cpu_dequant.hpp:267-278) for every format, with the same argument rules
+ * checked on the host (format, group size, parameter count, buffer sizes).
+ * Parameter values are checked per group on the device: a group with a
+ * non-finite parameter (or a non-zero FP8 bias) is skipped, its outputs left
+ * untouched, and HLKV_ERR_NONFINITE is set in *d_err.
+ */
+int hlkv_dequantize_to_fp16(int format, const void* d_packed, size_t packed_size, size_t n,
+                            const float* d_params, size_t n_params, size_t group_size,
+                            uint16_t* d_out, size_t out_size, uint32_t* d_err,
+                            hlkv_stream_t stream);
+
+/*
+ * Device counterpart of hl::quant::quantize_reference (cpu_quant.hpp:209-222):
+ * same argument rules on the host; codes and parameters bit-exact.  A group
+ * with a non-finite input (or an INT4 range that overflows) is skipped, its
+ * codes and parameters left untouched, and HLKV_ERR_NONFINITE is set.
+ */
+int hlkv_quantize(int format, const float* d_in, size_t n, size_t group_size, float* d_params,
+                  size_t n_params, void* d_packed, size_t packed_size, uint32_t* d_err,
+                  hlkv_stream_t stream);
+
+/* ---- host table (hl::alloc::HeteroBlockTable, hetero_block_table.hpp:141-245) ----------- */
+typedef struct hlkv_table hlkv_table;
+
+typedef struct {
+  uint32_t format;
+  uint32_t slot_bytes;
+  uint32_t num_slots;
+} HlkvPoolConfig;
+
+typedef struct {
+  uint32_t max_blocks;
+  uint32_t block_tokens;
+  uint32_t num_pools;
+  const HlkvPoolConfig* pools;
+} HlkvTableConfig;
+
+typedef struct {
+  uint32_t format;
+  uint32_t valid_tokens;
+  uint32_t layout;
+  uint32_t scale_mode;
+  uint32_t scale_ref;
+} HlkvAllocRequest;
+
+typedef struct {
+  uint32_t id;
+  uint32_t generation;
+} HlkvHandle; /* BlockHandle and SequenceHandle; {0xFFFFFFFF, 0} is invalid */
+
+int hlkv_table_validate_config(const HlkvTableConfig* config);
+int hlkv_table_create(const HlkvTableConfig* config, hlkv_table** out);
+void hlkv_table_destroy(hlkv_table* table);
+
+int hlkv_table_allocate(hlkv_table* t, const HlkvAllocRequest* req, HlkvHandle* out);
+int hlkv_table_retain(hlkv_table* t, HlkvHandle block);
+int hlkv_table_release(hlkv_table* t, HlkvHandle block);
+int hlkv_table_set_valid_tokens(hlkv_table* t, HlkvHandle block, uint32_t valid_tokens);
+int hlkv_table_seal(hlkv_table* t, HlkvHandle block);
+int hlkv_table_set_residency(hlkv_table* t, HlkvHandle block, uint32_t residency);
+int hlkv_table_set_scale(hlkv_table* t, HlkvHandle block, uint32_t scale_mode, uint32_t scale_ref);
+/* out[4] = {from_format, from_slot, to_format, to_slot} */
+int hlkv_table_begin_format_change(hlkv_table* t, HlkvHandle block, uint32_t target, uint32_t out[4]);
+int hlkv_table_commit_format_change(hlkv_table* t, HlkvHandle block, uint32_t scale_mode,
+                                    uint32_t scale_ref);
+int hlkv_table_abort_format_change(hlkv_table* t, HlkvHandle block);
+/* out = the 32-byte host record (hl::alloc::BlockDescriptor) */
+int hlkv_table_lookup(const hlkv_table* t, HlkvHandle block, void* out32);
+int hlkv_table_lookup_batch(const hlkv_table* t, const HlkvHandle* blocks, size_t n,
+                            HlkvExecDescriptor* out, size_t out_n);
+HlkvHandle hlkv_table_handle_of(const hlkv_table* t, uint32_t block_id);
+
+int hlkv_table_create_sequence(hlkv_table* t, HlkvHandle* out);
+int hlkv_table_append_block(hlkv_table* t, HlkvHandle seq, const HlkvAllocRequest* req,
+                            HlkvHandle* out);
+int hlkv_table_append_shared_block(hlkv_table* t, HlkvHandle seq, HlkvHandle block);
+int hlkv_table_release_sequence(hlkv_table* t, HlkvHandle seq);
+/* Copies up to cap ids; *len = the sequence length (HLKV_STATUS_INVALID_ARGUMENT if cap < len). */
+int hlkv_table_sequence_block_ids(const hlkv_table* t, HlkvHandle seq, uint32_t* out, size_t cap,
+                                  size_t* len);
+int hlkv_table_batch_segments(const hlkv_table* t, const HlkvHandle* seqs, size_t n,
+                              HlkvSegment* out);
+/* CSR reference path: indptr[n+1], blocks[cap]; *total = number of blocks. */
+int hlkv_table_build_exec_table(const hlkv_table* t, const HlkvHandle* seqs, size_t n,
+                                uint32_t* indptr, HlkvExecDescriptor* blocks, size_t cap,
+                                size_t* total);
+void hlkv_table_pending(const hlkv_table* t, size_t* n_desc, size_t* n_id);
+/* Moves the pending delta out (HLKV_STATUS_INVALID_ARGUMENT, nothing moved, if a cap is short). */
+int hlkv_table_collect_delta(hlkv_table* t, HlkvExecDescriptor* desc, size_t desc_cap,
+                             HlkvIdPatch* ids, size_t id_cap, size_t* n_desc, size_t* n_id,
+                             uint32_t* table_size, uint32_t* arena_size);
+HlkvExecDescriptor hlkv_table_device_descriptor(const hlkv_table* t, uint32_t block_id);
+uint32_t hlkv_table_block_tokens(const hlkv_table* t);
+uint32_t hlkv_table_max_blocks(const hlkv_table* t);
+uint32_t hlkv_table_blocks_in_use(const hlkv_table* t);
+int hlkv_table_has_pool(const hlkv_table* t, uint32_t format);
+uint32_t hlkv_table_free_slots(const hlkv_table* t, uint32_t format);
+uint32_t hlkv_table_pool_slots(const hlkv_table* t, uint32_t format);
+uint32_t hlkv_table_slot_bytes(const hlkv_table* t, uint32_t format);
+/* TableStats flattened: 3 + 15 + 4 + 4 counters, then 10 uint64 totals (36 values). */
+void hlkv_table_stats(const hlkv_table* t, uint64_t out[36]);
+/* Returns the status of validate(); the message (NUL-terminated, truncated) goes to msg. */
+int hlkv_table_validate(const hlkv_table* t, char* msg, size_t cap);
+
+/* ---- persistent device tables (the mirror of the table's device-facing state) ---------- */
+typedef struct hlkv_device_tables hlkv_device_tables;
+
+/* Binds to the current CUDA device; allocates lazily on the first sync. */
+int hlkv_device_tables_create(hlkv_device_tables** out);
+void hlkv_device_tables_destroy(hlkv_device_tables* dt);
+/*
+ * collect_delta() on the host table, then on `stream`: grow the device arena
+ * (keeping contents), upload the patches (pinned staging) and run kernel (3).
+ * Returns an HLKV_* device status.
+ */
+int hlkv_device_tables_sync(hlkv_device_tables* dt, hlkv_table* t, hlkv_stream_t stream);
+const HlkvExecDescriptor* hlkv_device_tables_table(const hlkv_device_tables* dt);
+uint32_t hlkv_device_tables_table_size(const hlkv_device_tables* dt);
+const uint32_t* hlkv_device_tables_arena(const hlkv_device_tables* dt);
+uint32_t hlkv_device_tables_arena_size(const hlkv_device_tables* dt);
+/* Device word the sync's kernel (3) reports into (zeroed at creation). */
+uint32_t* hlkv_device_tables_error_word(const hlkv_device_tables* dt);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* HLKV_H_ */
