@@ -182,3 +182,183 @@ REF_API std::uint32_t ref_gather_dequant(const RefPool* pools, std::uint32_t T, 
   for (const std::uint32_t e : errs) err |= e;
   return err;
 }
+
+// ---- a CPU-built workload for the reference arm of bench.py --------------------------------
+// Built entirely with the reference's own code: its HeteroBlockTable (scrambled
+// free lists, sequences, collect_delta/batch_segments for the device view) and
+// its quantize_reference (one group per row) on seeded N(0,1) FP16 values.
+#include <algorithm>
+#include <cmath>
+#include <memory>
+
+#include "hl_allocator/hetero_block_table.hpp"
+
+namespace {
+
+struct SplitMix {
+  std::uint64_t s;
+  std::uint64_t next() {
+    std::uint64_t z = (s += 0x9E3779B97F4A7C15ull);
+    z = (z ^ (z >> 30)) * 0xBF58476D1CE4E5B9ull;
+    z = (z ^ (z >> 27)) * 0x94D049BB133111EBull;
+    return z ^ (z >> 31);
+  }
+  float normal() {
+    const double u1 = 1.0 - static_cast<double>(next() >> 11) * 0x1.0p-53;
+    const double u2 = static_cast<double>(next() >> 11) * 0x1.0p-53;
+    return static_cast<float>(std::sqrt(-2.0 * std::log(u1)) * std::cos(6.283185307179586 * u2));
+  }
+};
+
+struct RefWorkload {
+  std::uint32_t T, H, D, layout_id;
+  std::vector<std::uint32_t> table_words, arena, segs;
+  RefPool pools[15]{};
+  std::vector<std::vector<std::uint8_t>> pool_bytes = std::vector<std::vector<std::uint8_t>>(4);
+  std::uint64_t info[16]{};  // table_size, arena_size, nseq, total_blocks, slots[4], slot_bytes[4]
+};
+
+}  // namespace
+
+REF_API void* ref_workload_build(const std::uint8_t* fmts, const std::uint32_t* lens,
+                                 std::uint32_t nseq, std::uint32_t T, std::uint32_t H,
+                                 std::uint32_t D, std::uint32_t layout_id, std::uint64_t seed,
+                                 std::uint32_t outlier_channels, float outlier_scale, int threads) {
+  auto w = std::make_unique<RefWorkload>();
+  w->T = T; w->H = H; w->D = D; w->layout_id = layout_id;
+  const std::size_t rows = std::size_t{2} * T * H, elems = rows * D;
+  std::uint32_t counts[4] = {0, 0, 0, 0};
+  std::size_t total = 0;
+  for (std::uint32_t i = 0; i < nseq; ++i) {
+    for (std::uint32_t j = 0; j < lens[i]; ++j) counts[fmts[total + j] & 3]++;
+    total += lens[i];
+  }
+  std::size_t slot_bytes[4];
+  for (int f = 0; f < 4; ++f) {
+    const auto qf = static_cast<q::QuantFormat>(f);
+    const std::size_t params = f == 0 ? 0 : (f == 3 ? 8 * rows : 4 * rows);
+    slot_bytes[f] = (q::packed_bytes(qf, elems) + params + 15) / 16 * 16;
+  }
+  a::TableConfig cfg;
+  cfg.max_blocks = static_cast<std::uint32_t>(std::max<std::size_t>(total, 1));
+  cfg.block_tokens = T;
+  for (int f = 0; f < 4; ++f) {
+    if (counts[f] > 0) {
+      cfg.pools.push_back({a::FormatId{static_cast<std::uint8_t>(f)},
+                           static_cast<std::uint32_t>(slot_bytes[f]), counts[f]});
+    }
+  }
+  if (cfg.pools.empty()) cfg.pools.push_back({a::FormatId{0}, static_cast<std::uint32_t>(slot_bytes[0]), 1});
+  a::HeteroBlockTable table(cfg);
+  SplitMix rng{seed};
+  {  // scramble: allocate every slot, release in a seeded order
+    std::vector<a::BlockHandle> hs;
+    for (const a::PoolConfig& p : cfg.pools) {
+      for (std::uint32_t k = 0; k < p.num_slots; ++k) {
+        a::AllocRequest r;
+        r.format = p.format;
+        r.layout = layout_id;
+        hs.push_back(table.allocate(r).value());
+      }
+    }
+    for (std::size_t i = hs.size(); i > 1; --i) std::swap(hs[i - 1], hs[rng.next() % i]);
+    for (const a::BlockHandle h : hs) (void)table.release(h);
+  }
+  std::vector<a::SequenceHandle> seqs;
+  total = 0;
+  for (std::uint32_t i = 0; i < nseq; ++i) {
+    seqs.push_back(table.create_sequence().value());
+    for (std::uint32_t j = 0; j < lens[i]; ++j) {
+      a::AllocRequest r;
+      r.format = a::FormatId{static_cast<std::uint8_t>(fmts[total + j] & 3)};
+      r.valid_tokens = T;
+      r.layout = layout_id;
+      (void)table.append_block(seqs.back(), r).value();
+    }
+    total += lens[i];
+  }
+  a::ExecDelta delta;
+  table.collect_delta(delta);
+  w->table_words.resize(std::size_t{delta.descriptor_table_size} * 4);
+  for (const a::BlockExecDescriptor& p : delta.descriptor_patches) {
+    std::memcpy(&w->table_words[std::size_t{p.block_id} * 4], &p, 16);
+  }
+  w->arena.assign(std::max<std::size_t>(delta.arena_size, 1), 0xFFFFFFFFu);
+  for (const a::IdPatch& p : delta.id_patches) w->arena[p.offset] = p.block_id;
+  w->arena.resize(delta.arena_size);
+  std::vector<a::SequenceSegment> segs;
+  (void)table.batch_segments(seqs, segs);
+  for (const a::SequenceSegment& s : segs) {
+    w->segs.push_back(s.offset);
+    w->segs.push_back(s.length);
+  }
+  // Payloads: per slot, seeded N(0,1) values (outlier channels scaled), rounded to
+  // FP16, then quantize_reference per row.
+  std::vector<std::uint32_t> outlier(std::size_t{H} * D, 0);
+  for (std::uint32_t h = 0; h < H; ++h) {
+    for (std::uint32_t k = 0; k < outlier_channels && k < D; ++k) outlier[h * D + rng.next() % D] = 1;
+  }
+  for (int f = 0; f < 4; ++f) {
+    if (counts[f] == 0) continue;
+    const auto qf = static_cast<q::QuantFormat>(f);
+    std::vector<std::uint8_t>& bytes = w->pool_bytes[f];
+    bytes.assign(std::size_t{counts[f]} * slot_bytes[f], 0);
+    auto fill = [&](std::uint32_t s0, std::uint32_t s1) {
+      std::vector<float> x(elems);
+      std::vector<q::AffineParams> prm(rows);
+      for (std::uint32_t s = s0; s < s1; ++s) {
+        SplitMix g{seed * 0x100000001B3ull + static_cast<std::uint64_t>(f) * 0x1000003ull + s};
+        for (std::size_t e = 0; e < elems; ++e) {
+          float v = g.normal();
+          if (outlier[e % (std::size_t{H} * D)]) v *= outlier_scale;
+          x[e] = q::decode_fp16(q::encode_fp16(v));
+        }
+        std::uint8_t* dst = bytes.data() + std::size_t{s} * slot_bytes[f];
+        const std::size_t cb = q::packed_bytes(qf, elems);
+        (void)q::quantize_reference(qf, x, f == 0 ? 0 : D,
+                                    std::span<q::AffineParams>(prm.data(), f == 0 ? 0 : rows),
+                                    std::span<std::byte>(reinterpret_cast<std::byte*>(dst), cb));
+        for (std::size_t r = 0; r < rows && f != 0; ++r) {
+          if (f == 3) std::memcpy(dst + cb + 8 * r, &prm[r], 8);
+          else std::memcpy(dst + cb + 4 * r, &prm[r].scale, 4);
+        }
+      }
+    };
+    const int nt = std::max(1, threads);
+    std::vector<std::thread> pool;
+    for (int t = 0; t < nt; ++t) {
+      pool.emplace_back(fill, static_cast<std::uint32_t>(std::uint64_t{counts[f]} * t / nt),
+                        static_cast<std::uint32_t>(std::uint64_t{counts[f]} * (t + 1) / nt));
+    }
+    for (std::thread& th : pool) th.join();
+    w->pools[f] = RefPool{bytes.data(), slot_bytes[f], counts[f], 0};
+    w->info[4 + f] = counts[f];
+    w->info[8 + f] = slot_bytes[f];
+  }
+  w->info[0] = delta.descriptor_table_size;
+  w->info[1] = delta.arena_size;
+  w->info[2] = nseq;
+  w->info[3] = total;
+  return w.release();
+}
+
+REF_API const std::uint64_t* ref_workload_info(void* w) { return static_cast<RefWorkload*>(w)->info; }
+REF_API const std::uint32_t* ref_workload_table(void* w) { return static_cast<RefWorkload*>(w)->table_words.data(); }
+REF_API const std::uint32_t* ref_workload_arena(void* w) { return static_cast<RefWorkload*>(w)->arena.data(); }
+REF_API const std::uint32_t* ref_workload_segs(void* w) { return static_cast<RefWorkload*>(w)->segs.data(); }
+REF_API const std::uint8_t* ref_workload_pool(void* w, int f) {
+  return static_cast<RefWorkload*>(w)->pool_bytes[f & 3].data();
+}
+
+REF_API std::uint32_t ref_workload_gather(void* wp, std::uint16_t* out, int threads) {
+  auto* w = static_cast<RefWorkload*>(wp);
+  const std::uint32_t nseq = static_cast<std::uint32_t>(w->info[2]);
+  std::vector<std::uint64_t> prefix(nseq + 1, 0);
+  for (std::uint32_t i = 0; i < nseq; ++i) prefix[i + 1] = prefix[i] + w->segs[2 * i + 1];
+  return ref_gather_dequant(w->pools, w->T, w->H, w->D, w->layout_id, w->table_words.data(),
+                            static_cast<std::uint32_t>(w->info[0]), w->arena.data(),
+                            static_cast<std::uint32_t>(w->info[1]), w->segs.data(), nseq, nullptr,
+                            out, prefix.data(), threads);
+}
+
+REF_API void ref_workload_free(void* w) { delete static_cast<RefWorkload*>(w); }

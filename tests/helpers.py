@@ -1,0 +1,58 @@
+"""Shared test helpers: device copies, oracle views of a workload, comparisons."""
+from __future__ import annotations
+
+import numpy as np
+
+
+def d2h(ptr: int, nbytes: int) -> np.ndarray:
+    """Copies raw device memory to a host uint8 array (for pointers torch does not own)."""
+    from cuda.bindings import runtime as rt
+    import torch
+    torch.cuda.synchronize()
+    out = np.empty(max(nbytes, 1), dtype=np.uint8)
+    if nbytes:
+        err, = rt.cudaMemcpy(out.ctypes.data, ptr, nbytes, rt.cudaMemcpyKind.cudaMemcpyDeviceToHost)
+        assert err == rt.cudaError_t.cudaSuccess, err
+    return out[:nbytes]
+
+
+def host_pools(wl) -> dict:
+    """{fmt: (uint8 numpy array, slot_bytes, num_slots)} copies of a workload's device pools."""
+    return {f: (buf.cpu().numpy().reshape(-1), sb, ns) for f, (buf, sb, ns) in wl.pools.items()}
+
+
+def device_table_words(wl) -> np.ndarray:
+    return d2h(wl.dt.table_ptr, wl.dt.table_size * 16).view(np.uint32).reshape(-1, 4)
+
+
+def device_arena(wl) -> np.ndarray:
+    return d2h(wl.dt.arena_ptr, wl.dt.arena_size * 4).view(np.uint32)
+
+
+def oracle_gather(oracle, wl, out_elems: int | None = None, out_offsets=None, table=None,
+                  arena=None, segs=None, fill: int = 0xABCD, threads: int = 8):
+    """Runs the CPU oracle on the exact bytes the kernel reads."""
+    table = device_table_words(wl) if table is None else table
+    arena = device_arena(wl) if arena is None else arena
+    segs = wl.segs_host if segs is None else segs
+    n = out_elems if out_elems is not None else wl.total_blocks * wl.block_elems
+    out = np.full(max(n, 1), fill, dtype=np.uint16)
+    err = oracle.gather_dequant(host_pools(wl), wl.T, wl.H, wl.D, wl.layout.layout_id, table,
+                                arena, segs, out, out_offsets, threads)
+    return out[:n], err
+
+
+def fp16_nan(h: np.ndarray) -> np.ndarray:
+    h = h.astype(np.uint16)
+    return ((h & 0x7C00) == 0x7C00) & ((h & 0x03FF) != 0)
+
+
+def assert_bits_equal(got: np.ndarray, want: np.ndarray, what: str = "") -> None:
+    got = np.asarray(got).view(np.uint16).reshape(-1)
+    want = np.asarray(want).view(np.uint16).reshape(-1)
+    assert got.shape == want.shape, (got.shape, want.shape)
+    bad = np.nonzero(got != want)[0]
+    if bad.size:
+        i = bad[0]
+        raise AssertionError(f"{what}: {bad.size} of {got.size} differ; first at {i}: "
+                             f"got {got[i]:#06x} want {want[i]:#06x}")
