@@ -54,7 +54,15 @@ __device__ __forceinline__ uint32_t canon_f16x2(uint32_t w) {
   return (w & ~nan) | (nan & ((w & 0x80008000u) | 0x7E007E00u));
 }
 
+// Any NaN half among 8: magnitude + 0x3FF reaches bit 15 exactly for magnitudes > 0x7C00.
+__device__ __forceinline__ bool f16x8_has_nan(uint4 v) {
+  const uint32_t any = ((v.x & 0x7FFF7FFFu) + 0x03FF03FFu) | ((v.y & 0x7FFF7FFFu) + 0x03FF03FFu) |
+                       ((v.z & 0x7FFF7FFFu) + 0x03FF03FFu) | ((v.w & 0x7FFF7FFFu) + 0x03FF03FFu);
+  return (any & 0x80008000u) != 0;
+}
+
 __device__ __forceinline__ uint4 canon_f16x8(uint4 v) {
+  if (!f16x8_has_nan(v)) return v;
   return make_uint4(canon_f16x2(v.x), canon_f16x2(v.y), canon_f16x2(v.z), canon_f16x2(v.w));
 }
 
@@ -88,11 +96,14 @@ __device__ __forceinline__ uint32_t fp8_to_f16(uint32_t b, float scale) {
   return f16_bits(__fmul_rn(fp8_finite_value<kKind>(b), scale));
 }
 
-// True when any of the 4 codes of `w` is a NaN (E4M3) or an Inf/NaN (E5M2).
+// True when any of the 4 codes of `w` is a NaN (E4M3: magnitude 0x7F) or an
+// Inf/NaN (E5M2: exponent bits 0x7C all set).  With the magnitude masked to
+// 7 bits, adding 1 (E4M3) or 4 (E5M2) per byte carries into bit 7 exactly for
+// those codes, and no byte carries into its neighbour.
 template <uint32_t kKind>
 __device__ __forceinline__ bool fp8_has_special(uint32_t w) {
-  if constexpr (kKind == kE4M3) return __vcmpeq4(w & 0x7F7F7F7Fu, 0x7F7F7F7Fu) != 0;
-  else return __vcmpeq4(w & 0x7C7C7C7Cu, 0x7C7C7C7Cu) != 0;
+  if constexpr (kKind == kE4M3) return (((w & 0x7F7F7F7Fu) + 0x01010101u) & 0x80808080u) != 0;
+  else return (((w & 0x7C7C7C7Cu) + 0x04040404u) & 0x80808080u) != 0;
 }
 
 // Per-element path for 8 codes that include a NaN or Inf code (rare): kept out
@@ -111,19 +122,45 @@ __device__ __noinline__ uint4 fp8x8_to_f16_special(uint2 c, float scale) {
 }
 
 // Eight codes (little-endian in a uint2) -> eight binary16 in a uint4.
+//
+// fp8_finite_value(b) = bits(b) * 2^k exactly (k = 120 for E4M3, 112 for
+// E5M2), so decode(b) * scale = bits(b) * (scale * 2^k) as real numbers, and
+// one rounding of the same real gives the same binary32 -- provided
+// scale * 2^k is itself exact, i.e. |scale| < 2^(128-k).  That folds the
+// rebias into one multiply per row; larger scales take the two-multiply form.
+template <uint32_t kKind>
+__device__ __forceinline__ float fp8_fold_bits(uint32_t b) {
+  if constexpr (kKind == kE4M3) return __uint_as_float(((b & 0x80u) << 24) | ((b & 0x7Fu) << 20));
+  else return __uint_as_float(((b & 0x80u) << 24) | ((b & 0x7Fu) << 21));
+}
+
 template <uint32_t kKind>
 __device__ __forceinline__ uint4 fp8x8_to_f16(uint2 c, float scale) {
   if (fp8_has_special<kKind>(c.x) | fp8_has_special<kKind>(c.y)) {
     return fp8x8_to_f16_special<kKind>(c, scale);
   }
+  constexpr float kRebias = kKind == kE4M3 ? 0x1p120f : 0x1p112f;
+  constexpr float kFoldLimit = kKind == kE4M3 ? 0x1p8f : 0x1p16f;
   uint32_t r[4];
+  if (fabsf(scale) < kFoldLimit) {
+    const float folded = __fmul_rn(scale, kRebias);  // exact
 #pragma unroll
-  for (int k = 0; k < 4; ++k) {
-    const uint32_t w = k < 2 ? c.x : c.y;
-    const uint32_t sh = (k & 1) * 16;
-    const float lo = __fmul_rn(fp8_finite_value<kKind>((w >> sh) & 0xFFu), scale);
-    const float hi = __fmul_rn(fp8_finite_value<kKind>((w >> (sh + 8)) & 0xFFu), scale);
-    r[k] = pack_f16x2(lo, hi);
+    for (int k = 0; k < 4; ++k) {
+      const uint32_t w = k < 2 ? c.x : c.y;
+      const uint32_t sh = (k & 1) * 16;
+      const float lo = __fmul_rn(fp8_fold_bits<kKind>((w >> sh) & 0xFFu), folded);
+      const float hi = __fmul_rn(fp8_fold_bits<kKind>((w >> (sh + 8)) & 0xFFu), folded);
+      r[k] = pack_f16x2(lo, hi);
+    }
+  } else {
+#pragma unroll
+    for (int k = 0; k < 4; ++k) {
+      const uint32_t w = k < 2 ? c.x : c.y;
+      const uint32_t sh = (k & 1) * 16;
+      const float lo = __fmul_rn(fp8_finite_value<kKind>((w >> sh) & 0xFFu), scale);
+      const float hi = __fmul_rn(fp8_finite_value<kKind>((w >> (sh + 8)) & 0xFFu), scale);
+      r[k] = pack_f16x2(lo, hi);
+    }
   }
   return make_uint4(r[0], r[1], r[2], r[3]);
 }
@@ -136,13 +173,20 @@ __device__ __forceinline__ float nibble_value(uint32_t q) {
 }
 
 // Eight nibbles (element 2k in the low nibble of byte k) -> eight binary16.
+// The low and high nibbles are split into two byte vectors; a byte permute
+// then places one code in the low byte of the binary32 pattern of 2^23, so
+// (2^23 + q) - 2^23 recovers q exactly.
 __device__ __forceinline__ uint4 int4x8_to_f16(uint32_t w, float scale, float bias) {
+  const uint32_t lo4 = w & 0x0F0F0F0Fu;         // elements 0, 2, 4, 6
+  const uint32_t hi4 = (w >> 4) & 0x0F0F0F0Fu;  // elements 1, 3, 5, 7
   uint32_t r[4];
 #pragma unroll
   for (int k = 0; k < 4; ++k) {
-    const float lo = __fmaf_rn(nibble_value((w >> (8 * k)) & 0xFu), scale, bias);
-    const float hi = __fmaf_rn(nibble_value((w >> (8 * k + 4)) & 0xFu), scale, bias);
-    r[k] = pack_f16x2(lo, hi);
+    // selector: byte k of the first operand, then bytes 1..3 of 0x4B000000 (= 0x4B, 0, 0 high).
+    const uint32_t sel = static_cast<uint32_t>(k) | 0x7650u;
+    const float qlo = __fsub_rn(__uint_as_float(__byte_perm(lo4, 0x4B000000u, sel)), 8388608.0f);
+    const float qhi = __fsub_rn(__uint_as_float(__byte_perm(hi4, 0x4B000000u, sel)), 8388608.0f);
+    r[k] = pack_f16x2(__fmaf_rn(qlo, scale, bias), __fmaf_rn(qhi, scale, bias));
   }
   return make_uint4(r[0], r[1], r[2], r[3]);
 }

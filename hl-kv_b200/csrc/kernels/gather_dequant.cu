@@ -23,6 +23,7 @@
 #include <cuda_runtime.h>
 
 #include <cstdint>
+#include <cstdlib>
 
 #include "codec.cuh"
 #include "common.cuh"
@@ -34,6 +35,7 @@ namespace {
 constexpr int kThreads = 256;
 constexpr int kMinCtasPerSm = 4;  // 64 registers per thread
 constexpr int kUnroll = 8;
+constexpr int kDefaultWaves = 1;
 
 struct DevPool {
   const uint8_t* base;
@@ -105,8 +107,11 @@ __device__ Item resolve(const Params& p, uint32_t seq, uint64_t j, uint64_t bloc
 }
 
 // Streams one block.  kD = head_dim; 8-element chunk v covers row v / (kD/8).
-// One register set serves every format (raw chunk words + row parameters), so
-// the format switch does not multiply the register footprint.
+// One register set serves every format (raw chunk words + row parameters) and
+// the format test is CTA-uniform, so the compiler keeps one 64-register
+// allocation instead of one per format.  Per unrolled step every thread issues
+// its kUnroll loads first (codes plus, for FP8/INT4, the row parameters
+// through the read-only path; 16 threads share a row), then converts and stores.
 template <int kD>
 __device__ __forceinline__ void stream_block(const Params& p, const Item& it) {
   constexpr uint32_t kChunksPerRowLog2 = kD == 64 ? 3 : (kD == 128 ? 4 : 5);
@@ -230,6 +235,19 @@ __global__ void __launch_bounds__(kThreads, kMinCtasPerSm) gather_dequant_kernel
   }
 }
 
+// Grid = waves x (SMs x resident CTAs).  With more than one wave the hardware
+// block scheduler hands freed SM slots to the next CTA, which evens out the
+// per-CTA work (blocks of different formats carry different byte counts).
+// HLKV_GATHER_WAVES overrides the default for tuning.
+int gather_waves() {
+  static const int waves = [] {
+    const char* e = std::getenv("HLKV_GATHER_WAVES");
+    const int v = e != nullptr ? std::atoi(e) : 0;
+    return v >= 1 && v <= 64 ? v : kDefaultWaves;
+  }();
+  return waves;
+}
+
 template <int kD>
 int grid_for() {
   static thread_local int cached_device = -1;
@@ -242,7 +260,7 @@ int grid_for() {
                                                       0) != cudaSuccess) {
       return 0;
     }
-    cached_grid = sm_count() * (per_sm > 0 ? per_sm : 1);
+    cached_grid = sm_count() * (per_sm > 0 ? per_sm : 1) * gather_waves();
     cached_device = device;
   }
   return cached_grid;

@@ -1,0 +1,115 @@
+"""Kernel (3), hlkv_apply_delta, and hl::kv::DeviceTables: the device tables track the host
+table through the delta protocol (the reference's ExecMirror, run on the GPU)."""
+import numpy as np
+import pytest
+
+from helpers import d2h
+
+pytestmark = pytest.mark.gpu
+
+
+def _device_state(dt):
+    table = d2h(dt.table_ptr, dt.table_size * 16).view(np.uint32).reshape(-1, 4)
+    arena = d2h(dt.arena_ptr, dt.arena_size * 4).view(np.uint32)
+    return table, arena
+
+
+def test_random_operations_device_tables_track_host(hlkv_lib, cuda_device):
+    """The reference's randomized differential test (test_hetero_block_table.cpp:675-784) with the
+    mirror on the GPU: irregular syncs, arena relocations, residency changes, format changes."""
+    h = hlkv_lib
+    t = h.Table(96, [(0, 4096, 48), (1, 2048, 48), (3, 1088, 64)])
+    dt = h.DeviceTables()
+    rng = np.random.default_rng(20261011)
+    seqs, transcoding = [], []
+    formats = (0, 1, 3)
+
+    def random_block():
+        if not seqs:
+            return None
+        st, ids = t.sequence_block_ids(seqs[rng.integers(len(seqs))])
+        return t.handle_of(ids[rng.integers(len(ids))]) if ids else None
+
+    checks = 0
+    for step in range(6000):
+        op = int(rng.integers(11))
+        if op == 0:
+            st, s = t.create_sequence()
+            if st == 0:
+                seqs.append(s)
+        elif op in (1, 2) and seqs:
+            t.append_block(seqs[rng.integers(len(seqs))], formats[rng.integers(3)], 16)
+        elif op == 3 and (b := random_block()) is not None:
+            t.seal(b)
+            t.append_shared_block(seqs[rng.integers(len(seqs))], b)
+        elif op == 4 and (b := random_block()) is not None:
+            t.seal(b)
+            if t.begin_format_change(b, formats[rng.integers(3)])[0] == 0:
+                transcoding.append(b)
+        elif op == 5 and transcoding:
+            b = transcoding.pop(int(rng.integers(len(transcoding))))
+            assert (t.commit_format_change(b) if rng.integers(2) else t.abort_format_change(b)) == 0
+        elif op == 6 and (b := random_block()) is not None:
+            t.set_residency(b, int(rng.integers(3)))
+        elif op == 7 and (b := random_block()) is not None:
+            t.set_valid_tokens(b, int(rng.integers(17)))
+        elif op >= 8 and seqs:
+            i = int(rng.integers(len(seqs)))
+            if t.release_sequence(seqs[i]) == 0:
+                seqs.pop(i)
+        if rng.integers(23) == 0:
+            dt.sync(t)
+            table, arena = _device_state(dt)
+            want = np.array([t.device_descriptor(i) for i in range(96)], np.uint32)
+            assert np.array_equal(table, want), f"step {step}"
+            st, segs = t.batch_segments(seqs)
+            for s, (off, ln) in zip(seqs, segs):
+                assert list(arena[off:off + ln]) == t.sequence_block_ids(s)[1], f"step {step}"
+            checks += 1
+    assert checks > 100
+    assert d2h(dt.error_word_ptr, 4).view(np.uint32)[0] == 0
+
+
+def test_apply_delta_kernel_matches_oracle_and_flags_range(hlkv_lib, oracle, cuda_device):
+    import torch
+    rng = np.random.default_rng(4)
+    n_table, n_arena = 300, 1000
+    table0 = rng.integers(0, 2 ** 32, size=(n_table, 4), dtype=np.uint64).astype(np.uint32)
+    arena0 = rng.integers(0, 2 ** 32, size=n_arena, dtype=np.uint64).astype(np.uint32)
+    ids = rng.permutation(n_table + 20)[:150].astype(np.uint32)          # some out of range
+    desc = rng.integers(0, 2 ** 32, size=(150, 4), dtype=np.uint64).astype(np.uint32)
+    desc[:, 3] = ids
+    offs = rng.permutation(n_arena + 50)[:700].astype(np.uint32)         # some out of range
+    idp = np.stack([offs, rng.integers(0, 2 ** 32, size=700, dtype=np.uint64).astype(np.uint32)], 1)
+    t_host, a_host = table0.copy(), arena0.copy()
+    oerr = oracle.apply_delta(t_host, a_host, desc, idp)
+    d_table = torch.from_numpy(table0.view(np.int32)).cuda()
+    d_arena = torch.from_numpy(arena0.view(np.int32)).cuda()
+    d_desc = torch.from_numpy(desc.view(np.int32)).cuda()
+    d_ids = torch.from_numpy(idp.view(np.int32)).cuda()
+    err = torch.zeros(1, dtype=torch.int32, device="cuda")
+    hlkv_lib.apply_delta(d_table.data_ptr(), n_table, d_arena.data_ptr(), n_arena, d_desc, d_ids, err)
+    torch.cuda.synchronize()
+    assert oerr == (1 << 11) == int(err.item())
+    assert np.array_equal(d_table.cpu().numpy().view(np.uint32), t_host)
+    assert np.array_equal(d_arena.cpu().numpy().view(np.uint32), a_host)
+
+
+def test_large_delta_and_arena_growth(hlkv_lib, cuda_device):
+    """Thousands of sequences: many relocations, a delta larger than the first staging buffer."""
+    h = hlkv_lib
+    t = h.Table(40000, [(1, 33792, 40000)])
+    dt = h.DeviceTables()
+    seqs = [t.create_sequence()[1] for _ in range(500)]
+    rng = np.random.default_rng(1)
+    for rnd in range(4):
+        for s in seqs:
+            for _ in range(int(rng.integers(1, 20))):
+                t.append_block(s, 1, 16)
+        dt.sync(t)
+    table, arena = _device_state(dt)
+    st, segs = t.batch_segments(seqs)
+    for s, (off, ln) in zip(seqs, segs):
+        assert list(arena[off:off + ln]) == t.sequence_block_ids(s)[1]
+    want = np.array([t.device_descriptor(i) for i in range(t.max_blocks())], np.uint32)
+    assert np.array_equal(table, want)

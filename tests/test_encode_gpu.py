@@ -1,0 +1,119 @@
+"""Kernel (2), hlkv_append_encode, against the CPU oracle's append (quantize_reference
+per row): every byte of every pool -- codes, parameters and untouched slots -- must
+match, and the error bits must agree."""
+import numpy as np
+import pytest
+
+from helpers import device_table_words, host_pools
+
+pytestmark = pytest.mark.gpu
+
+
+def _tokens(n: int, H: int, D: int, seed: int) -> np.ndarray:
+    """FP16 tokens [n, 2, H, D] with the awkward cases: signed-zero rows, constants,
+    subnormals, FP16 extremes, a ramp, big outliers."""
+    rng = np.random.default_rng(seed)
+    x = (rng.standard_normal((n, 2, H, D)) * rng.choice([0.01, 1, 30, 1000], size=(n, 2, H, 1))).astype(np.float16)
+    x[0, 0, 0] = 0.0
+    x[0, 0, 0, ::3] = -0.0                      # mixed signed zeros (min/max ties)
+    x[0, 1, 0] = -0.0
+    x[0, 1, 0, 5] = 0.0
+    x[1, 0, 0] = 2.5                            # constant row: INT4 scale 0
+    x[1, 1, 0] = np.float16(6e-8) * np.arange(D)  # subnormal ramp
+    x[2, 0, 0, :4] = [65504, -65504, 1, -1]
+    x[2, 1, 0] = np.linspace(-7, 7, D)
+    return x
+
+
+def _run(hlkv, wl, targets, tokens):
+    import torch
+    d_t = torch.from_numpy(targets.astype(np.int32)).cuda()
+    d_x = torch.from_numpy(tokens.view(np.int16).copy()).cuda()
+    err = torch.zeros(1, dtype=torch.int32, device="cuda")
+    hlkv.append_encode(wl.hlkv_pools(), wl.layout, wl.dt.table_ptr, wl.dt.table_size, d_t, d_x, err)
+    torch.cuda.synchronize()
+    return int(err.item())
+
+
+def _all_ids(wl):
+    ids = []
+    for s in wl.seqs:
+        st, b = wl.table.sequence_block_ids(s)
+        ids += b
+    return ids
+
+
+@pytest.mark.parametrize("T,H,D", [(16, 8, 128), (4, 2, 64), (2, 2, 256)])
+def test_append_encode_bit_exact(hlkv_lib, oracle, cuda_device, T, H, D):
+    from hlkv.workload import build_workload
+    fm = [[0, 1, 2, 3, 1, 3, 0], [3, 1, 2]]
+    wl = build_workload(fm, T=T, H=H, D=D, seed=T + D, valid_tokens=[[0] * 7, [1] * 3],
+                        outlier_channels=0)
+    ids = _all_ids(wl)
+    rng = np.random.default_rng(D)
+    pairs = [(i, t) for i in ids for t in range(T)]
+    pick = rng.choice(len(pairs), size=min(40, len(pairs)), replace=False)
+    targets = np.array([pairs[k] for k in pick], dtype=np.uint32)
+    tokens = _tokens(len(targets), H, D, seed=T * D)
+    before = host_pools(wl)
+    table = device_table_words(wl)
+    err = _run(hlkv_lib, wl, targets, tokens)
+    oerr = oracle.append_encode(before, T, H, D, 1, table, targets, tokens.view(np.uint16))
+    assert err == oerr == 0
+    after = host_pools(wl)
+    for f in before:
+        got, want = after[f][0], before[f][0]
+        bad = np.nonzero(got != want)[0]
+        assert bad.size == 0, f"format {f}: {bad.size} bytes differ, first at {bad[:4]}"
+
+
+def test_append_rejects_bad_rows_and_targets(hlkv_lib, oracle, cuda_device):
+    from hlkv.workload import build_workload
+    T, H, D = 4, 2, 64
+    wl = build_workload([[1, 3, 0]], T=T, H=H, D=D, seed=2, outlier_channels=0, spare_slots=1)
+    ids = _all_ids(wl)
+    free_id = next(i for i in range(wl.table.max_blocks()) if i not in ids)
+    targets = np.array([[ids[0], 1], [ids[1], 2], [ids[2], 0],   # valid
+                        [ids[0], T], [free_id, 0], [10 ** 6, 0],  # token range, not executable, id range
+                        [ids[1], 3]], dtype=np.uint32)
+    tokens = _tokens(len(targets), H, D, seed=5)
+    tokens[1, 0, 1, 7] = np.inf    # one INT4 row rejected
+    tokens[6, 1, 0, 0] = np.nan    # one INT4 row rejected
+    before = host_pools(wl)
+    table = device_table_words(wl)
+    err = _run(hlkv_lib, wl, targets, tokens)
+    oerr = oracle.append_encode(before, T, H, D, 1, table, targets, tokens.view(np.uint16))
+    assert oerr == (1 << 9) | (1 << 10) | (1 << 0) | (1 << 4)
+    assert err == oerr
+    after = host_pools(wl)
+    for f in before:
+        assert np.array_equal(after[f][0], before[f][0]), f
+
+
+def test_append_then_gather_round_trip(hlkv_lib, oracle, cuda_device):
+    """Decode step: encode one token per sequence into the tail block, set valid_tokens on the
+    host, apply the delta on the device, gather -- the new token decodes as the oracle says."""
+    import torch
+    from helpers import oracle_gather
+    from hlkv.workload import build_workload
+    T, H, D = 16, 8, 128
+    wl = build_workload([[1, 3], [3, 1], [0, 1]], T=T, H=H, D=D, seed=8,
+                        valid_tokens=[[16, 5], [16, 9], [16, 0]])
+    targets, tokens = [], _tokens(3, H, D, seed=9)
+    for s, vt in zip(wl.seqs, (5, 9, 0)):
+        st, ids = wl.table.sequence_block_ids(s)
+        tail = wl.table.handle_of(ids[-1])
+        assert wl.table.set_valid_tokens(tail, vt + 1) == 0
+        targets.append((ids[-1], vt))
+    wl.dt.sync(wl.table)
+    err = _run(hlkv_lib, wl, np.array(targets, np.uint32), tokens)
+    assert err == 0
+    n = wl.total_blocks * wl.block_elems
+    out = torch.empty(n, dtype=torch.int16, device="cuda")
+    e = torch.zeros(1, dtype=torch.int32, device="cuda")
+    hlkv_lib.gather_dequant(wl.hlkv_pools(), wl.layout, wl.dt.table_ptr, wl.dt.table_size,
+                            wl.dt.arena_ptr, wl.dt.arena_size, wl.segs, out, e)
+    torch.cuda.synchronize()
+    want, oerr = oracle_gather(oracle, wl)
+    assert int(e.item()) == 0 and oerr == 0
+    assert np.array_equal(out.cpu().numpy().view(np.uint16), want)
