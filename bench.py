@@ -43,6 +43,13 @@ WORKLOADS = {
                        "K+V, FP16 .25 / E4M3 .5 / INT4 .25, N(0,1) + 4 outlier channels x20"),
     "homogeneous": dict(nseq=1, blocks=256, probs=(0.0, 1.0, 0.0, 0.0),
                         name="homogeneous E4M3: 1 seq x 4096 tok, 16-tok blocks, 8 KV heads x 128, K+V"),
+    # Single-format caches of the mixed workload's size: per-format throughput.
+    "fp16": dict(nseq=64, blocks=128, probs=(1.0, 0.0, 0.0, 0.0),
+                 name="FP16 only: 64 seq x 2048 tok, 16-tok blocks, 8 KV heads x 128, K+V"),
+    "e4m3": dict(nseq=64, blocks=128, probs=(0.0, 1.0, 0.0, 0.0),
+                 name="E4M3 only: 64 seq x 2048 tok, 16-tok blocks, 8 KV heads x 128, K+V"),
+    "int4": dict(nseq=64, blocks=128, probs=(0.0, 0.0, 0.0, 1.0),
+                 name="INT4 only: 64 seq x 2048 tok, 16-tok blocks, 8 KV heads x 128, K+V"),
 }
 
 

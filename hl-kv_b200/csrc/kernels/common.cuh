@@ -33,3 +33,29 @@ __device__ __forceinline__ void st_stream(uint4* p, uint4 v) { __stcs(p, v); }
 
 }  // namespace dev
 }  // namespace hlkv
+
+namespace hlkv {
+namespace dev {
+
+// ---- TMA bulk copies (cp.async.bulk, no multicast) -------------------------------------------
+// Shared -> global bulk store of `bytes` (multiple of 16; both addresses 16-byte aligned),
+// tracked in the issuing thread's bulk group.
+__device__ __forceinline__ void bulk_store(void* gdst, const void* ssrc, uint32_t bytes) {
+  const uint32_t s = static_cast<uint32_t>(__cvta_generic_to_shared(ssrc));
+  asm volatile("cp.async.bulk.global.shared::cta.bulk_group [%0], [%1], %2;"
+               :: "l"(gdst), "r"(s), "r"(bytes) : "memory");
+}
+__device__ __forceinline__ void bulk_commit() { asm volatile("cp.async.bulk.commit_group;" ::: "memory"); }
+// Waits until this thread's committed bulk stores have finished reading shared memory.
+__device__ __forceinline__ void bulk_wait_read_all() {
+  asm volatile("cp.async.bulk.wait_group.read 0;" ::: "memory");
+}
+// Waits until this thread's committed bulk stores have completed.
+__device__ __forceinline__ void bulk_wait_all() { asm volatile("cp.async.bulk.wait_group 0;" ::: "memory"); }
+// Orders this thread's generic-proxy shared-memory writes before later async-proxy reads.
+__device__ __forceinline__ void fence_proxy_async_smem() {
+  asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+}
+
+}  // namespace dev
+}  // namespace hlkv

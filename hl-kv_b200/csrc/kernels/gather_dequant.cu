@@ -18,8 +18,10 @@
 //    shared memory; blocks are then streamed back to back without a barrier;
 //  * per block the format is CTA-uniform; each thread handles 8-element
 //    chunks: a 16-byte (FP16), 8-byte (FP8) or 4-byte (INT4) coalesced load,
-//    register-level byte/nibble unpack, one 16-byte streaming store.  Row
-//    parameters are read through the read-only path (16 threads share a row).
+//    register-level byte/nibble unpack into the warp's shared-memory tile;
+//    one lane writes each 2 KB tile to HBM with a TMA bulk store
+//    (cp.async.bulk, no multicast).  Row parameters are read through the
+//    read-only path (16 threads share a row).
 #include <cuda_runtime.h>
 
 #include <cstdint>
@@ -33,8 +35,14 @@ namespace hlkv {
 namespace {
 
 constexpr int kThreads = 256;
-constexpr int kMinCtasPerSm = 4;  // 64 registers per thread
-constexpr int kUnroll = 8;
+#ifndef HLKV_GATHER_MIN_CTAS
+#define HLKV_GATHER_MIN_CTAS 4
+#endif
+#ifndef HLKV_GATHER_UNROLL
+#define HLKV_GATHER_UNROLL 4
+#endif
+constexpr int kMinCtasPerSm = HLKV_GATHER_MIN_CTAS;  // 4: 64 registers per thread
+constexpr int kUnroll = HLKV_GATHER_UNROLL;          // chunks per lane per tile: 2 KB tiles
 constexpr int kDefaultWaves = 1;
 
 struct DevPool {
@@ -107,14 +115,24 @@ __device__ Item resolve(const Params& p, uint32_t seq, uint64_t j, uint64_t bloc
 }
 
 // Streams one block.  kD = head_dim; 8-element chunk v covers row v / (kD/8).
+//
+// Each warp owns consecutive 2 KB output tiles (128 chunks; lane l handles
+// chunks l, l+32, ... of the tile).  Per tile: the lanes issue their kUnroll
+// coalesced loads (codes plus, for FP8/INT4, the row parameters through the
+// read-only path; 16 lanes share a row), convert in registers, write the
+// binary16 results into the warp's shared-memory tile, and lane 0 writes the
+// tile to global memory with one TMA bulk store.  Bulk stores reach the DRAM
+// write ceiling with few resident warps, where per-thread stores need twice
+// the occupancy this kernel's registers allow.  Only __syncwarp is needed.
+//
 // One register set serves every format (raw chunk words + row parameters) and
-// the format test is CTA-uniform, so the compiler keeps one 64-register
-// allocation instead of one per format.  Per unrolled step every thread issues
-// its kUnroll loads first (codes plus, for FP8/INT4, the row parameters
-// through the read-only path; 16 threads share a row), then converts and stores.
+// the format test is CTA-uniform, so the compiler keeps one allocation
+// instead of one per format.
 template <int kD>
-__device__ __forceinline__ void stream_block(const Params& p, const Item& it) {
+__device__ __forceinline__ void stream_block(const Params& p, const Item& it, uint4* tile) {
   constexpr uint32_t kChunksPerRowLog2 = kD == 64 ? 3 : (kD == 128 ? 4 : 5);
+  constexpr uint32_t kTile = 32 * kUnroll;  // chunks per warp tile
+  const uint32_t lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
   const uint32_t nchunks = static_cast<uint32_t>(p.block_elems >> 3);
   const uint32_t rpk = p.rows_per_kv;
   const uint32_t f = it.fmt;
@@ -122,13 +140,13 @@ __device__ __forceinline__ void stream_block(const Params& p, const Item& it) {
   const uint8_t* params = payload + p.code_bytes[f];
   uint4* out = reinterpret_cast<uint4*>(it.out);
 
-  for (uint32_t v0 = threadIdx.x; v0 < nchunks; v0 += kThreads * kUnroll) {
+  for (uint32_t t0 = warp * kTile; t0 < nchunks; t0 += kThreads * kUnroll) {
     uint4 raw[kUnroll];
     float2 prm[kUnroll];
     uint32_t live = 0;
 #pragma unroll
     for (int u = 0; u < kUnroll; ++u) {
-      const uint32_t v = v0 + u * kThreads;
+      const uint32_t v = t0 + u * 32 + lane;
       const uint32_t row = v >> kChunksPerRowLog2;
       const uint32_t r = row >= rpk ? row - rpk : row;
       raw[u] = make_uint4(0u, 0u, 0u, 0u);
@@ -148,10 +166,11 @@ __device__ __forceinline__ void stream_block(const Params& p, const Item& it) {
         }
       }
     }
+    // The previous bulk store of this warp must have finished reading the tile.
+    if (lane == 0) dev::bulk_wait_read_all();
+    __syncwarp();
 #pragma unroll
     for (int u = 0; u < kUnroll; ++u) {
-      const uint32_t v = v0 + u * kThreads;
-      if (v >= nchunks) break;
       uint4 o = make_uint4(0u, 0u, 0u, 0u);
       if (live & (1u << u)) {
         switch (f) {
@@ -161,7 +180,14 @@ __device__ __forceinline__ void stream_block(const Params& p, const Item& it) {
           default: o = dev::int4x8_to_f16(raw[u].x, prm[u].x, prm[u].y); break;
         }
       }
-      dev::st_stream(out + v, o);
+      tile[u * 32 + lane] = o;
+    }
+    dev::fence_proxy_async_smem();
+    __syncwarp();
+    if (lane == 0) {
+      const uint32_t n = min(kTile, nchunks - t0);
+      dev::bulk_store(out + t0, tile, n * 16u);
+      dev::bulk_commit();
     }
   }
 }
@@ -200,6 +226,7 @@ __global__ void __launch_bounds__(kThreads, kMinCtasPerSm) gather_dequant_kernel
   __shared__ uint64_t s_prefix[kThreads + 1];
   __shared__ uint64_t s_warp[kThreads / 32];
   __shared__ Item s_item[kThreads];
+  __shared__ __align__(128) uint4 s_tile[kThreads / 32][32 * kUnroll];  // one output tile per warp
 
   const uint64_t G = gridDim.x, c = blockIdx.x;
   uint64_t base = 0;  // blocks before the current chunk of sequences
@@ -226,13 +253,15 @@ __global__ void __launch_bounds__(kThreads, kMinCtasPerSm) gather_dequant_kernel
           static_cast<uint32_t>(min(uint64_t{kThreads}, (end - first + G - 1) / G));
       for (uint32_t k = 0; k < n_items; ++k) {
         const Item it = s_item[k];
-        if (it.fmt != kSkip) stream_block<kD>(p, it);
+        if (it.fmt != kSkip) stream_block<kD>(p, it, s_tile[threadIdx.x >> 5]);
       }
       __syncthreads();  // s_item is rewritten by the next batch
     }
     base = end;
     __syncthreads();  // s_prefix is rewritten by the next chunk
   }
+  // Shared memory must outlive the bulk stores that read it.
+  if ((threadIdx.x & 31) == 0) dev::bulk_wait_all();
 }
 
 // Grid = waves x (SMs x resident CTAs).  With more than one wave the hardware
