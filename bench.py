@@ -122,12 +122,15 @@ class ClockSampler:
                 "reasons": reasons, "samples": len(inside), "window": window}
 
 
-def traffic_from_profile() -> float | None:
-    """DRAM bytes per launch recorded from an ncu capture of this workload (profiles/)."""
+def traffic_from_profile(workload: str) -> int | None:
+    """DRAM bytes (read + write) per launch of the gather kernel, from the committed ncu
+    summary of the same workload (profiles/gather_dequant_<workload>_full.md), or None."""
+    import re
     try:
-        with open(os.path.join(ROOT, "profiles", "gather_dequant_traffic.json")) as f:
-            return float(json.load(f)["dram_bytes_per_launch"])
-    except Exception:
+        with open(os.path.join(ROOT, "profiles", f"gather_dequant_{workload}_full.md")) as f:
+            m = re.search(r"traffic \(read \+ write\) per launch \| ([0-9,]+) B", f.read())
+        return int(m.group(1).replace(",", "")) if m else None
+    except OSError:
         return None
 
 
@@ -304,7 +307,7 @@ def run_hlkv(args) -> None:
             "roofline": {"bound": "hbm", "achieved": round(achieved, 2), "peak": peak,
                          "unit": "GB/s", "frac": round(achieved / peak, 4),
                          "peak_source": f"{peak_kind} (MEASURED_PEAKS.json hbm_gbs)",
-                         "traffic": traffic_from_profile(),
+                         "traffic": traffic_from_profile(args.workload),
                          "kernel": "gather_dequant_kernel<128>", "launch_ms": round(mean_launch_ms, 5)},
             "e2e": {"value": round(e2e_value, 2), "unit": "GB/s", "steps": e2e_steps,
                     "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h,

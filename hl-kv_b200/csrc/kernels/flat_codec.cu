@@ -1,7 +1,7 @@
 // Flat (contiguous) device codecs.
 //
 //  * hlkv_dequantize_fp8_to_fp16: drop-in for the reference's
-//    hl::quant::cuda::dequantize_fp8_to_fp16 (dequant_kernel.cu:244-264):
+//    hl::quant::cuda::dequantize_fp8_to_fp16 (dequant_kernel.cu:171-191):
 //    any alignment, any group size; an 8-element path (8-byte load, 16-byte
 //    store) when the pointers are aligned and every 8-element chunk lies in one
 //    group, a per-element path for the rest.

@@ -82,7 +82,7 @@ enum {
 };
 
 /* ---- ABI records (byte-identical to hl::alloc, block_descriptor.hpp:137-150 and
- *      id_arena.hpp:315-326) -------------------------------------------------------------- */
+ *      id_arena.hpp:32-43) -------------------------------------------------------------- */
 typedef struct {
   uint32_t slot;
   uint32_t info; /* format:4 | scale_mode:2 | layout:4 | valid_tokens:10 | 0:12 */
@@ -194,7 +194,7 @@ int hlkv_apply_delta(HlkvExecDescriptor* d_table, uint32_t table_size, uint32_t*
 /* ---- flat codecs ------------------------------------------------------------------------ */
 /*
  * Drop-in for hl::quant::cuda::dequantize_fp8_to_fp16 (cuda_dequant.hpp:47-50,
- * dequant_kernel.cu:244-264): out[i] = fp16_rn(decode_fp8(in[i]) * params[i/group].scale),
+ * dequant_kernel.cu:171-191): out[i] = fp16_rn(decode_fp8(in[i]) * params[i/group].scale),
  * any alignment, any group size >= 1.  d_params holds {scale, bias} binary32
  * pairs (AffineParams); only scale is read.
  */
@@ -203,7 +203,7 @@ int hlkv_dequantize_fp8_to_fp16(int format, const void* d_in, size_t n, const fl
 
 /*
  * Device counterpart of hl::quant::dequantize_reference_to_fp16
- * (cpu_dequant.hpp:267-278) for every format, with the same argument rules
+ * (cpu_dequant.hpp:44-54) for every format, with the same argument rules
  * checked on the host (format, group size, parameter count, buffer sizes).
  * Parameter values are checked per group on the device: a group with a
  * non-finite parameter (or a non-zero FP8 bias) is skipped, its outputs left
@@ -215,7 +215,7 @@ int hlkv_dequantize_to_fp16(int format, const void* d_packed, size_t packed_size
                             hlkv_stream_t stream);
 
 /*
- * Device counterpart of hl::quant::quantize_reference (cpu_quant.hpp:209-222):
+ * Device counterpart of hl::quant::quantize_reference (cpu_quant.hpp:33-47):
  * same argument rules on the host; codes and parameters bit-exact.  A group
  * with a non-finite input (or an INT4 range that overflows) is skipped, its
  * codes and parameters left untouched, and HLKV_ERR_NONFINITE is set.

@@ -313,7 +313,7 @@ ORC_API int orc_dequantize_to_fp16(int f, const uint8_t* packed, size_t packed_s
  *
  * The device descriptor table is 4 uint32 words per block id:
  * {slot, info, scale_ref, block_id} (block_descriptor.hpp:146-150); the arena is
- * uint32 block ids; a segment is {offset, length} (id_arena.hpp:322-326).
+ * uint32 block ids; a segment is {offset, length} (id_arena.hpp:39-43).
  */
 typedef struct {
   const uint8_t* base;
