@@ -66,6 +66,24 @@ def dist_env() -> tuple[int, int, int]:
             int(os.environ.get("LOCAL_RANK", "0")))
 
 
+def shard_range(n: int, world: int, rank: int) -> tuple[int, int]:
+    """Contiguous share [lo, hi) of n sequences for `rank` of `world` ranks; shares differ
+    by at most one sequence and cover 0..n-1 exactly once."""
+    base, extra = divmod(n, world)
+    lo = rank * base + min(rank, extra)
+    return lo, lo + base + (1 if rank < extra else 0)
+
+
+def max_over_ranks(values, world: int, device) -> list[float]:
+    """Element-wise maximum of per-rank timings (all ranks take part; a no-op at world 1)."""
+    import torch
+    import torch.distributed as dist
+    t = torch.tensor([float(v) for v in values], dtype=torch.float64, device=device)
+    if world > 1:
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+    return t.tolist()
+
+
 class ClockSampler:
     """Samples SM clock and throttle reasons of one GPU through NVML in a thread."""
 
@@ -235,10 +253,7 @@ def run_hlkv(args) -> None:
     assert int(err.item()) == 0
     if flush is not None:  # the timed work is the launches, not the flushes between them
         total_ms = sum(launch_ms)
-    t = torch.tensor([total_ms, statistics.mean(launch_ms)], dtype=torch.float64, device="cuda")
-    if world > 1:
-        dist.all_reduce(t, op=dist.ReduceOp.MAX)
-    total_ms, mean_launch_ms = float(t[0]), float(t[1])
+    total_ms, mean_launch_ms = max_over_ranks([total_ms, statistics.mean(launch_ms)], world, "cuda")
 
     bytes_per_step = wl.algorithmic_bytes
     value = world * bytes_per_step * args.steps / (total_ms / 1e3) / 1e9
@@ -248,38 +263,68 @@ def run_hlkv(args) -> None:
 
     # End to end through the C ABI with host buffers: every step uploads the pools and
     # segments from pinned host memory, syncs the (unchanged) device tables, runs the
-    # gather and reads the FP16 output back into pinned host memory.
+    # gather and reads the FP16 output back into pinned host memory.  Steps alternate
+    # between two sets of device buffers on an upload stream and a readback stream, so
+    # that one step's upload overlaps the previous step's readback (PCIe is full
+    # duplex); every step still moves all of its bytes in both directions.
     e2e_steps = max(1, min(args.steps, args.e2e_steps))
     host_pools = {f: buf.cpu().pin_memory() for f, (buf, _, _) in wl.pools.items()}
     host_segs = wl.segs.cpu().pin_memory()
-    host_out = torch.empty(n_out, dtype=torch.int16).pin_memory()
+    host_out = [torch.empty(n_out, dtype=torch.int16).pin_memory() for _ in range(2)]
     h2d = sum(p.numel() for p in host_pools.values()) + host_segs.numel() * 4
     d2h = n_out * 2
+    dev_pools = [wl.pools, {f: (torch.empty_like(buf), sb, ns) for f, (buf, sb, ns) in wl.pools.items()}]
+    dev_segs = [wl.segs, torch.empty_like(wl.segs)]
+    dev_out = [out, torch.empty_like(out)]
+    hl_pools = [hlkv.make_pools(dp) for dp in dev_pools]
+    s_in, s_out = torch.cuda.Stream(), torch.cuda.Stream()
+    uploaded = [torch.cuda.Event() for _ in range(2)]
+    gathered = [torch.cuda.Event() for _ in range(2)]
+    read_back = [torch.cuda.Event() for _ in range(2)]
+    used = [False, False]
 
-    def e2e_step():
-        for f, (buf, _, _) in wl.pools.items():
-            buf.copy_(host_pools[f], non_blocking=True)
-        wl.segs.copy_(host_segs, non_blocking=True)
+    def e2e_step(k: int) -> None:
+        b = k & 1
+        with torch.cuda.stream(s_in):
+            if used[b]:
+                s_in.wait_event(gathered[b])  # the gather two steps back has read pools[b]
+            for f, (buf, _, _) in dev_pools[b].items():
+                buf.copy_(host_pools[f], non_blocking=True)
+            dev_segs[b].copy_(host_segs, non_blocking=True)
+            uploaded[b].record(s_in)
+        stream.wait_event(uploaded[b])
+        if used[b]:
+            stream.wait_event(read_back[b])  # out[b] of two steps back has been read back
         wl.dt.sync(wl.table, stream)
-        step()
-        host_out.copy_(out, non_blocking=True)
+        hlkv.gather_dequant(hl_pools[b], wl.layout, wl.dt.table_ptr, wl.dt.table_size,
+                            wl.dt.arena_ptr, wl.dt.arena_size, dev_segs[b], dev_out[b], err,
+                            stream=stream)
+        gathered[b].record(stream)
+        with torch.cuda.stream(s_out):
+            s_out.wait_event(gathered[b])
+            host_out[b].copy_(dev_out[b], non_blocking=True)
+            read_back[b].record(s_out)
+        used[b] = True
 
-    e2e_step()
+    e2e_step(0)
+    e2e_step(1)
     torch.cuda.synchronize()
     barrier()
     e0 = torch.cuda.Event(enable_timing=True)
     e1 = torch.cuda.Event(enable_timing=True)
     e0.record(stream)
-    for _ in range(e2e_steps):
-        e2e_step()
-    e1.record(stream)
+    s_in.wait_event(e0)
+    s_out.wait_event(e0)
+    for k in range(e2e_steps):
+        e2e_step(k)
+    e1.record(s_out)  # after the last readback, which follows every other operation
     torch.cuda.synchronize()
-    te = torch.tensor([e0.elapsed_time(e1)], dtype=torch.float64, device="cuda")
-    if world > 1:
-        dist.all_reduce(te, op=dist.ReduceOp.MAX)
-    e2e_value = world * bytes_per_step * e2e_steps / (float(te[0]) / 1e3) / 1e9
-    ok_bits = np.array_equal(host_out.numpy().view(np.uint16)[:4096],
-                             out[:4096].cpu().numpy().view(np.uint16))
+    (e2e_ms,) = max_over_ranks([e0.elapsed_time(e1)], world, "cuda")
+    e2e_value = world * bytes_per_step * e2e_steps / (e2e_ms / 1e3) / 1e9
+    last = (e2e_steps - 1) & 1
+    ok_bits = np.array_equal(host_out[last].numpy().view(np.uint16),
+                             dev_out[last].cpu().numpy().view(np.uint16))
+    assert int(err.item()) == 0
 
     cpu = None
     if world == 1 and not args.no_cpu_baseline:
@@ -312,8 +357,9 @@ def run_hlkv(args) -> None:
             "e2e": {"value": round(e2e_value, 2), "unit": "GB/s", "steps": e2e_steps,
                     "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h,
                     "path": "pinned host pools+segments -> H2D -> device-table sync -> "
-                            "hlkv_gather_dequant -> D2H of the FP16 output", "readback_ok": ok_bits},
-            "gpu_launches": args.steps,
+                            "hlkv_gather_dequant -> D2H of the FP16 output; two buffer sets, "
+                            "upload of step k overlaps readback of step k-1", "readback_ok": ok_bits},
+            "gpu_launches": args.steps,  # gather launches in the timed region
             "clocks": clocks.summary(h0, h1),
             "cpu_baseline": cpu,
         }
