@@ -1,17 +1,24 @@
 """Benchmark of the heterogeneous KV gather-dequant path on B200.
 
     python bench.py [--gpus N] [--steps K] [--warmup W] [--impl hlkv|reference]
-                    [--workload mixed|homogeneous]
+                    [--workload mixed|homogeneous|fp16|e4m3|int4|llama8b|llama70b]
 
-One step = one hlkv_gather_dequant launch over the whole workload of a GPU:
-the mixed single-layer cache (64 sequences x 2048 tokens, 16-token blocks,
-8 KV heads x 128, K and V; per-block format FP16 0.25 / E4M3 0.5 / INT4 0.25;
-N(0,1) values with 4 outlier channels per head x20; block ids and slots
-scattered by a seeded scramble).  Inputs and outputs (about 850 MB) exceed the
-126 MB L2, so no flush is needed between steps.  With N GPUs (torchrun), each
-rank holds its own cache of that size (weak scaling, sequences sharded, no
+Default workload ("mixed", the headline configuration): one step = one
+hlkv_gather_dequant launch over a single-layer cache of 64 sequences x 2048
+tokens, 16-token blocks, 8 KV heads x 128, K and V; per-block format FP16 0.25
+/ E4M3 0.5 / INT4 0.25; N(0,1) values with 4 outlier channels per head x20;
+block ids and slots scattered by a seeded scramble.  Inputs and outputs (about
+850 MB) exceed the 126 MB L2, so no flush is needed between steps.  With N GPUs
+(torchrun), each rank holds its own cache of that size (weak scaling, no
 inter-GPU traffic); ranks meet only at barriers and at the max-over-ranks
 reduction of the timings.
+
+Other workloads: "homogeneous" (1 sequence x 4096 tokens of E4M3, L2-resident:
+flushed between steps), single-format caches "fp16" / "e4m3" / "int4", and the
+multi-layer caches "llama8b" (32 layers, 64 x 8192 tokens, age tiers) and
+"llama70b" (8 resident layers of 16 x 131072 tokens), whose sequences are
+sharded over the ranks (strong scaling); one step there is one launch per
+layer into a single FP16 scratch buffer.
 
 value = algorithmic bytes of all ranks / max-over-ranks device time, GB/s.
 Algorithmic bytes per block = codes + row parameters read + 2*T*H*D*2 bytes
@@ -38,18 +45,38 @@ sys.path.insert(0, os.path.join(ROOT, "hl-kv_b200"))
 
 METRIC = "hetero KV dequant GB/s per GPU (% of HBM peak) at 1/2/4/8 B200; CPU ref GB/s"
 WORKLOADS = {
-    "mixed": dict(nseq=64, blocks=128, probs=(0.25, 0.5, 0.0, 0.25),
+    # The reference's headline configuration (the default): one layer, per-GPU cache fixed.
+    "mixed": dict(nseq=64, blocks=128, probs=(0.25, 0.5, 0.0, 0.25), scaling="weak",
                   name="mixed-format single layer: 64 seq x 2048 tok, 16-tok blocks, 8 KV heads x 128, "
                        "K+V, FP16 .25 / E4M3 .5 / INT4 .25, N(0,1) + 4 outlier channels x20"),
-    "homogeneous": dict(nseq=1, blocks=256, probs=(0.0, 1.0, 0.0, 0.0),
+    "homogeneous": dict(nseq=1, blocks=256, probs=(0.0, 1.0, 0.0, 0.0), scaling="weak",
                         name="homogeneous E4M3: 1 seq x 4096 tok, 16-tok blocks, 8 KV heads x 128, K+V"),
     # Single-format caches of the mixed workload's size: per-format throughput.
-    "fp16": dict(nseq=64, blocks=128, probs=(1.0, 0.0, 0.0, 0.0),
+    "fp16": dict(nseq=64, blocks=128, probs=(1.0, 0.0, 0.0, 0.0), scaling="weak",
                  name="FP16 only: 64 seq x 2048 tok, 16-tok blocks, 8 KV heads x 128, K+V"),
-    "e4m3": dict(nseq=64, blocks=128, probs=(0.0, 1.0, 0.0, 0.0),
+    "e4m3": dict(nseq=64, blocks=128, probs=(0.0, 1.0, 0.0, 0.0), scaling="weak",
                  name="E4M3 only: 64 seq x 2048 tok, 16-tok blocks, 8 KV heads x 128, K+V"),
-    "int4": dict(nseq=64, blocks=128, probs=(0.0, 0.0, 0.0, 1.0),
+    "int4": dict(nseq=64, blocks=128, probs=(0.0, 0.0, 0.0, 1.0), scaling="weak",
                  name="INT4 only: 64 seq x 2048 tok, 16-tok blocks, 8 KV heads x 128, K+V"),
+    # Llama-3-8B-shaped cache sharded by sequence; a step dequantizes all 32 layers, one
+    # launch per layer into one FP16 scratch buffer.
+    "llama8b": dict(nseq=64, tokens=8192, tiers=(512, 2048), layers=32, scaling="strong",
+                    name="Llama-3-8B cache: 32 layers, 64 seq x 8192 tok sharded by sequence, "
+                         "8 KV heads x 128, K+V; newest 512 tok FP16, previous 2048 E4M3, rest INT4"),
+    # Llama-3-70B-shaped long context sharded by sequence; 8 resident layers per GPU (the
+    # 80-layer payload of 234 GB does not fit one GPU), one launch per layer per step.
+    "llama70b": dict(nseq=16, blocks=8192, probs=(0.05, 0.10, 0.0, 0.85), layers=8,
+                     scaling="strong",
+                     name="Llama-3-70B long context: 16 seq x 131072 tok sharded by sequence, "
+                          "8 resident layers, 8 KV heads x 128, K+V; INT4 .85 / E4M3 .10 / FP16 .05"),
+    # Decode step: every (sequence, layer) stream appends one token, encoded into its tail
+    # block (kernel 2), and the allocator's descriptor delta is applied on the device
+    # (kernel 3).  Sequences sharded over the ranks.
+    "decode": dict(nseq=256, min_len=512, max_len=8192, layers=32, scaling="strong", decode=True,
+                   name="decode-step append: 256 seq (lengths U[512, 8192]) x 32 layers, 8 KV heads "
+                        "x 128, K+V; one N(0,1) FP16 token per seq-layer per step encoded into its "
+                        "tail block (E4M3 or INT4 .5/.5, a new block every 16 tokens) + descriptor "
+                        "delta applied on the device"),
 }
 
 
@@ -187,31 +214,51 @@ def cpu_gather_sample(wl, nseq_sample: int, min_wall_s: float = 2.0, max_reps: i
                       f"{nbytes / 1e6:.1f} MB algorithmic) x {reps} passes, {wall:.2f} s wall"}
 
 
+def build_bench_workload(spec: dict, rank: int, world: int):
+    """This rank's cache: all spec["nseq"] sequences (weak scaling) or its contiguous
+    share of them (strong scaling), for every layer; table sequences are layer-major."""
+    from hlkv.workload import build_workload, mixed_formats, tiered_formats
+    lo, hi = (0, spec["nseq"]) if spec["scaling"] == "weak" else shard_range(spec["nseq"], world, rank)
+    n = hi - lo
+    rows = []
+    for layer in range(spec.get("layers", 1)):
+        if "tiers" in spec:
+            rows += tiered_formats(n, spec["tokens"], fp16_tokens=spec["tiers"][0],
+                                   fp8_tokens=spec["tiers"][1])
+        else:
+            rows += mixed_formats(n, spec["blocks"], probs=spec["probs"],
+                                  seed=1000 + rank + 7919 * layer)
+    return build_workload(rows, seed=1000 + rank), n
+
+
 def run_hlkv(args) -> None:
     import numpy as np
     import torch
     import torch.distributed as dist
     import hlkv
-    from hlkv.workload import build_workload, mixed_formats
 
     rank, world, local = dist_env()
     torch.cuda.set_device(local)
     if world > 1:
         from datetime import timedelta
-        dist.init_process_group("nccl", timeout=timedelta(seconds=120),
+        dist.init_process_group("nccl", timeout=timedelta(seconds=300),
                                 device_id=torch.device("cuda", local))
     spec = WORKLOADS[args.workload]
-    fm = mixed_formats(spec["nseq"], spec["blocks"], probs=spec["probs"], seed=1000 + rank)
-    wl = build_workload(fm, seed=1000 + rank)
+    layers = spec.get("layers", 1)
+    wl, nseq_rank = build_bench_workload(spec, rank, world)
     pools = wl.hlkv_pools()
-    n_out = wl.total_blocks * wl.block_elems
+    # One launch per layer per step, all into one FP16 scratch buffer of a layer's size.
+    layer_segs = [wl.segs[l * nseq_rank:(l + 1) * nseq_rank] for l in range(layers)]
+    layer_blocks = [int(wl.segs_host[l * nseq_rank:(l + 1) * nseq_rank, 1].sum()) for l in range(layers)]
+    n_out = max(layer_blocks) * wl.block_elems
     out = torch.empty(n_out, dtype=torch.int16, device="cuda")
     err = torch.zeros(1, dtype=torch.int32, device="cuda")
     stream = torch.cuda.current_stream()
 
     def step():
-        hlkv.gather_dequant(pools, wl.layout, wl.dt.table_ptr, wl.dt.table_size, wl.dt.arena_ptr,
-                            wl.dt.arena_size, wl.segs, out, err, stream=stream)
+        for segs in layer_segs:
+            hlkv.gather_dequant(pools, wl.layout, wl.dt.table_ptr, wl.dt.table_size,
+                                wl.dt.arena_ptr, wl.dt.arena_size, segs, out, err, stream=stream)
 
     def barrier():
         if world > 1:
@@ -224,10 +271,11 @@ def run_hlkv(args) -> None:
 
     # Inputs + outputs smaller than a few L2 capacities would be served from L2 on the
     # next step: then a buffer of twice the L2 size is overwritten between steps and the
-    # value is taken from the per-launch events (the flush is not timed).
+    # value is taken from the per-step events (the flush is not timed).
+    bytes_per_step = wl.algorithmic_bytes
     l2_bytes = torch.cuda.get_device_properties(torch.cuda.current_device()).L2_cache_size
     flush = None
-    if wl.algorithmic_bytes < 4 * l2_bytes:
+    if bytes_per_step < 4 * l2_bytes:
         flush = torch.empty(2 * l2_bytes, dtype=torch.uint8, device="cuda")
     ev = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True))
           for _ in range(args.steps)]
@@ -249,25 +297,282 @@ def run_hlkv(args) -> None:
         h1 = time.perf_counter()
         barrier()
     total_ms = t_start.elapsed_time(t_end)
-    launch_ms = [a.elapsed_time(b) for a, b in ev]
+    step_ms = [a.elapsed_time(b) for a, b in ev]
     assert int(err.item()) == 0
     if flush is not None:  # the timed work is the launches, not the flushes between them
-        total_ms = sum(launch_ms)
-    total_ms, mean_launch_ms = max_over_ranks([total_ms, statistics.mean(launch_ms)], world, "cuda")
+        total_ms = sum(step_ms)
+    total_ms, mean_step_ms = max_over_ranks([total_ms, statistics.mean(step_ms)], world, "cuda")
 
-    bytes_per_step = wl.algorithmic_bytes
-    value = world * bytes_per_step * args.steps / (total_ms / 1e3) / 1e9
+    if spec["scaling"] == "weak":
+        job_bytes = world * bytes_per_step
+    else:  # strong: the ranks' shares add up to the whole cache
+        (job_bytes,) = [int(x) for x in _sum_over_ranks([bytes_per_step], world)]
+    value = job_bytes * args.steps / (total_ms / 1e3) / 1e9
     per_gpu = value / world
     peak, peak_kind = measured_peak_gbs()
-    achieved = bytes_per_step / (mean_launch_ms / 1e3) / 1e9
+    achieved = bytes_per_step / (mean_step_ms / 1e3) / 1e9
+    mean_launch_ms = mean_step_ms / layers
 
-    # End to end through the C ABI with host buffers: every step uploads the pools and
-    # segments from pinned host memory, syncs the (unchanged) device tables, runs the
-    # gather and reads the FP16 output back into pinned host memory.  Steps alternate
-    # between two sets of device buffers on an upload stream and a readback stream, so
-    # that one step's upload overlaps the previous step's readback (PCIe is full
-    # duplex); every step still moves all of its bytes in both directions.
+    e2e = None
+    if layers == 1:
+        e2e = measure_e2e(args, wl, out, err, stream, world, bytes_per_step, barrier)
+    else:
+        e2e = {"value": None, "unit": "GB/s", "h2d_bytes_per_step": None, "d2h_bytes_per_step": None,
+               "reason": "multi-layer cache is resident in HBM; end to end is measured on the "
+                         "single-layer workloads"}
+
+    cpu = None
+    if world == 1 and not args.no_cpu_baseline and layers == 1:
+        cpu = cpu_gather_sample(wl, nseq_sample=min(16, len(wl.segs_host)))
+
+    if rank == 0:
+        line = {
+            "metric": METRIC, "value": round(value, 2), "unit": "GB/s", "n_gpus": world,
+            "steps": args.steps, "warmup": args.warmup,
+            "ms_per_step": round(total_ms / args.steps, 5), "higher_is_better": True,
+            "scaling": spec["scaling"], "vs_baseline": None, "dtype": "fp16 out; fp16/e4m3/int4 in",
+            "data": "synthetic (seeded N(0,1) + outlier channels, quantized on the GPU)",
+            "config": {"workload": spec["name"], "layers": layers,
+                       "sequences_per_gpu": nseq_rank,
+                       "blocks_per_gpu": wl.total_blocks,
+                       "blocks_per_format": {"fp16": wl.blocks_per_format[0],
+                                             "e4m3": wl.blocks_per_format[1],
+                                             "int4": wl.blocks_per_format[3]},
+                       "bytes_per_step_per_gpu": bytes_per_step,
+                       "l2": ("inputs+outputs (%.0f MB) exceed 4x the %.0f MB L2; no flush" % (
+                           bytes_per_step / 1e6, l2_bytes / 1e6)) if flush is None else
+                             ("L2 flushed between steps (%.0f MB overwritten); value from the "
+                              "per-step events" % (2 * l2_bytes / 1e6)),
+                       "parallelism": f"sequence-sharded x{world}, no collective on the data path"},
+            "per_gpu_gbs": round(per_gpu, 2),
+            "pct_hbm_peak": round(100 * per_gpu / peak, 2),
+            "roofline": {"bound": "hbm", "achieved": round(achieved, 2), "peak": peak,
+                         "unit": "GB/s", "frac": round(achieved / peak, 4),
+                         "peak_source": f"{peak_kind} (MEASURED_PEAKS.json hbm_gbs)",
+                         "traffic": traffic_from_profile(args.workload),
+                         "kernel": "gather_dequant_kernel<128>",
+                         "launch_ms": round(mean_launch_ms, 5)},
+            "e2e": e2e,
+            "gpu_launches": args.steps * layers,  # gather launches in the timed region
+            "clocks": clocks.summary(h0, h1),
+            "cpu_baseline": cpu,
+        }
+        print(json.dumps(line), flush=True)
+    if world > 1:
+        dist.barrier()
+        dist.destroy_process_group()
+
+
+def run_decode(args) -> None:
+    """Decode-append step (kernel 2 + kernel 3) on a resident multi-layer cache."""
+    import numpy as np
+    import torch
+    import torch.distributed as dist
+    import hlkv
+
+    rank, world, local = dist_env()
+    torch.cuda.set_device(local)
+    if world > 1:
+        from datetime import timedelta
+        dist.init_process_group("nccl", timeout=timedelta(seconds=600),
+                                device_id=torch.device("cuda", local))
+    spec = WORKLOADS[args.workload]
+    T, H, D, layers = 16, 8, 128, spec["layers"]
+    lo, hi = shard_range(spec["nseq"], world, rank)
+    lengths = np.random.default_rng(3000).integers(spec["min_len"], spec["max_len"] + 1,
+                                                   size=spec["nseq"])[lo:hi]
+    n = len(lengths) * layers  # streams: one table sequence per (layer, sequence), layer-major
+    stream_len = np.tile(lengths, layers)
+    rng = np.random.default_rng(3001 + rank)
+    quant = np.array([hlkv.FP8_E4M3, hlkv.INT4], dtype=np.uint32)
+    steps_total = args.warmup + args.steps
+    nb = -(-stream_len // T)
+    init_fmt = rng.choice(quant, size=int(nb.sum()))
+    new_fmt = rng.choice(quant, size=(steps_total, n)).astype(np.uint32)
+    layout = hlkv.Layout(T, H, D, 1)
+    extra = n * (steps_total // T + 2)
+    slots = {int(f): int((init_fmt == f).sum()) + extra for f in quant}
+    sbytes = {f: (hlkv.layout_slot_bytes(f, layout) + 15) // 16 * 16 for f in slots}
+    t_build = time.perf_counter()
+    table = hlkv.Table(int(nb.sum()) + 2 * extra, [(f, sbytes[f], slots[f]) for f in slots],
+                       block_tokens=T)
+    seqs, k = [], 0
+    for j in range(n):
+        st, s = table.create_sequence()
+        assert st == 0
+        seqs.append(s)
+        tail_tokens = int(stream_len[j]) - T * (int(nb[j]) - 1)
+        for b in range(int(nb[j])):
+            st, _ = table.append_block(s, int(init_fmt[k]), T if b + 1 < nb[j] else tail_tokens, 1)
+            assert st == 0, st
+            k += 1
+    tail_fmt = init_fmt[np.cumsum(nb) - 1].astype(np.uint32)
+    handles = (hlkv.Handle * n)(*seqs)
+    dt = hlkv.DeviceTables()
+    dt.sync(table)
+    pools_t = {f: (torch.empty((slots[f], sbytes[f]), dtype=torch.uint8, device="cuda"), sbytes[f],
+                   slots[f]) for f in slots}
+    pools = hlkv.make_pools(pools_t)
+    gen = torch.Generator(device="cuda")
+    gen.manual_seed(3002 + rank)
+    tokens = [torch.randn((n, 2, H, D), generator=gen, device="cuda").to(torch.float16)
+              for _ in range(4)]
+    pinned = [torch.empty((n, 2), dtype=torch.int32).pin_memory() for _ in range(2)]
+    pinned_np = [p.numpy().view(np.uint32) for p in pinned]
+    d_targets = [torch.empty((n, 2), dtype=torch.int32, device="cuda") for _ in range(2)]
+    copied = [torch.cuda.Event() for _ in range(2)]
+    err = torch.zeros(1, dtype=torch.int32, device="cuda")
+    stream = torch.cuda.current_stream()
+    torch.cuda.synchronize()
+    build_s = time.perf_counter() - t_build
+
+    rows_in = 2 * H * D * 2
+    enc_out = {int(hlkv.FP8_E4M3): 2 * H * D + 2 * H * 4, int(hlkv.INT4): 2 * H * D // 2 + 2 * H * 8}
+    ev = [[torch.cuda.Event(enable_timing=True) for _ in range(3)] for _ in range(steps_total)]
+    host = {"table_s": 0.0, "sync_s": 0.0}
+    nbytes = {"encode": 0, "delta": 0}
+
+    def step(k: int, timed: bool) -> None:
+        nonlocal tail_fmt
+        b = k & 1
+        if k >= 2:
+            copied[b].synchronize()  # the upload two steps back has read pinned[b]
+        h0 = time.perf_counter()
+        st, tg, done = table.append_tokens(handles, new_fmt[k], 1, out=pinned_np[b])
+        assert st == 0 and done == n, (st, done)
+        nd, ni = table.pending()
+        h1 = time.perf_counter()
+        ev[k][0].record(stream)
+        d_targets[b].copy_(pinned[b], non_blocking=True)
+        copied[b].record(stream)
+        dt.sync(table, stream)  # collect_delta on the host, upload, kernel (3)
+        h2 = time.perf_counter()
+        ev[k][1].record(stream)
+        hlkv.append_encode(pools, layout, dt.table_ptr, dt.table_size, d_targets[b], tokens[k % 4],
+                           err, stream=stream)
+        ev[k][2].record(stream)
+        tail_fmt = np.where(tg[:, 1] == 0, new_fmt[k], tail_fmt)
+        if timed:
+            host["table_s"] += h1 - h0
+            host["sync_s"] += h2 - h1
+            n8 = int((tail_fmt == hlkv.FP8_E4M3).sum())
+            nbytes["encode"] += n * (rows_in + 16) + n8 * enc_out[1] + (n - n8) * enc_out[3]
+            nbytes["delta"] += nd * 32 + ni * 12
+
+    for k in range(args.warmup):
+        step(k, False)
+    torch.cuda.synchronize()
+    assert int(err.item()) == 0, f"error bits {int(err.item()):#x}"
+    with ClockSampler(torch.cuda.current_device()) as clocks:
+        if world > 1:
+            dist.barrier()
+        torch.cuda.synchronize()
+        w0 = time.perf_counter()
+        for k in range(args.warmup, steps_total):
+            step(k, True)
+        torch.cuda.synchronize()
+        w1 = time.perf_counter()
+    assert int(err.item()) == 0, f"error bits {int(err.item()):#x}"
+    timed = ev[args.warmup:]
+    dev_ms = [e[0].elapsed_time(e[2]) for e in timed]
+    enc_ms = [e[1].elapsed_time(e[2]) for e in timed]
+    delta_ms = [e[0].elapsed_time(e[1]) for e in timed]
+    wall_ms = 1e3 * (w1 - w0)
+    dev_total, enc_mean, delta_mean, wall_ms = max_over_ranks(
+        [sum(dev_ms), statistics.mean(enc_ms), statistics.mean(delta_ms), wall_ms], world, "cuda")
+    step_bytes = (nbytes["encode"] + nbytes["delta"]) / args.steps
+    (job_bytes,) = _sum_over_ranks([step_bytes], world)
+    value = job_bytes * args.steps / (dev_total / 1e3) / 1e9
+    peak, peak_kind = measured_peak_gbs()
+    achieved = nbytes["encode"] / args.steps / (enc_mean / 1e3) / 1e9
+
+    cpu = None
+    if world == 1 and not args.no_cpu_baseline:
+        cpu = cpu_encode_sample(tokens[0], tail_fmt, H, D, n)
+    if rank == 0:
+        print(json.dumps({
+            "metric": METRIC, "value": round(value, 2), "unit": "GB/s", "n_gpus": world,
+            "steps": args.steps, "warmup": args.warmup,
+            "ms_per_step": round(dev_total / args.steps, 5), "higher_is_better": True,
+            "scaling": "strong", "vs_baseline": None, "dtype": "fp16 in; e4m3/int4 out",
+            "data": "synthetic (seeded lengths, formats and N(0,1) tokens)",
+            "config": {"workload": spec["name"], "streams_per_gpu": n, "sequences_per_gpu": len(lengths),
+                       "blocks_at_start": int(nb.sum()), "bytes_per_step_per_gpu": round(step_bytes),
+                       "build_s": round(build_s, 1),
+                       "parallelism": f"sequence-sharded x{world}, no collective on the data path"},
+            "us_per_step": {"device": round(1e3 * dev_total / args.steps, 2),
+                            "encode_kernel": round(1e3 * enc_mean, 2),
+                            "delta_upload_and_apply": round(1e3 * delta_mean, 2),
+                            "host_table_ops": round(1e6 * host["table_s"] / args.steps, 2),
+                            "host_collect_delta_and_launch": round(1e6 * host["sync_s"] / args.steps, 2),
+                            "wall": round(1e3 * wall_ms / args.steps, 2)},
+            "roofline": {"bound": "hbm", "achieved": round(achieved, 2), "peak": peak, "unit": "GB/s",
+                         "frac": round(achieved / peak, 4),
+                         "peak_source": f"{peak_kind} (MEASURED_PEAKS.json hbm_gbs)",
+                         "traffic": None, "kernel": "append_encode_kernel<128>",
+                         "launch_ms": round(enc_mean, 5)},
+            "e2e": {"value": round(job_bytes * args.steps / (wall_ms / 1e3) / 1e9, 2), "unit": "GB/s",
+                    "h2d_bytes_per_step": n * 8, "d2h_bytes_per_step": 0,
+                    "path": "host table ops + collect_delta -> H2D of targets and delta -> "
+                            "apply_delta -> append_encode, wall clock per step (tokens resident)"},
+            "gpu_launches": 2 * args.steps,
+            "clocks": clocks.summary(w0, w1),
+            "cpu_baseline": cpu,
+        }), flush=True)
+    if world > 1:
+        dist.barrier()
+        dist.destroy_process_group()
+
+
+def cpu_encode_sample(tokens, tail_fmt, H: int, D: int, n: int, min_wall_s: float = 2.0):
+    """The reference's quantize_reference per row (oracle/_ref), on all host threads, over
+    one step's tokens: n targets x 2*H rows of D values, in the formats of their blocks."""
+    import numpy as np
+    from oracle.oracle import Oracle, Ref, ref_available
+    kind = "reference" if ref_available() else "port"
+    impl = Ref() if kind == "reference" else Oracle()
+    x = tokens.float().cpu().numpy().reshape(n * 2 * H, D)
+    fm = np.repeat(tail_fmt.astype(np.uint8), 2 * H)
+    params = np.zeros((x.shape[0], 2), np.float32)
+    codes = np.zeros(x.shape, np.uint8)
+    threads = os.cpu_count() or 1
+    impl.quantize_rows(fm, x, params, codes, threads)
+    reps, t0 = 0, time.perf_counter()
+    while True:
+        bad = impl.quantize_rows(fm, x, params, codes, threads)
+        reps += 1
+        wall = time.perf_counter() - t0
+        if wall >= min_wall_s or reps >= 50:
+            break
+    assert bad == 0
+    n8 = int((tail_fmt == 1).sum())
+    nbytes = n * (2 * H * D * 2 + 16) + n8 * (2 * H * D + 2 * H * 4) + (n - n8) * (H * D + 2 * H * 8)
+    return {"value": round(nbytes * reps / wall / 1e9, 3), "unit": "GB/s", "cores": threads,
+            "kind": kind, "sample": f"one step's {n} appended tokens ({x.shape[0]} rows of {D}) "
+                                    f"x {reps} passes, {wall:.2f} s wall"}
+
+
+def _sum_over_ranks(values, world: int):
+    import torch
+    import torch.distributed as dist
+    t = torch.tensor([float(v) for v in values], dtype=torch.float64, device="cuda")
+    if world > 1:
+        dist.all_reduce(t, op=dist.ReduceOp.SUM)
+    return t.tolist()
+
+
+def measure_e2e(args, wl, out, err, stream, world, bytes_per_step, barrier) -> dict:
+    """End to end through the C ABI with host buffers: every step uploads the pools and
+    segments from pinned host memory, syncs the (unchanged) device tables, runs the
+    gather and reads the FP16 output back into pinned host memory.  Steps alternate
+    between two sets of device buffers on an upload stream and a readback stream, so
+    that one step's upload overlaps the previous step's readback (PCIe is full duplex);
+    every step still moves all of its bytes in both directions."""
+    import numpy as np
+    import torch
+    import hlkv
     e2e_steps = max(1, min(args.steps, args.e2e_steps))
+    n_out = out.numel()
     host_pools = {f: buf.cpu().pin_memory() for f, (buf, _, _) in wl.pools.items()}
     host_segs = wl.segs.cpu().pin_memory()
     host_out = [torch.empty(n_out, dtype=torch.int16).pin_memory() for _ in range(2)]
@@ -325,48 +630,21 @@ def run_hlkv(args) -> None:
     ok_bits = np.array_equal(host_out[last].numpy().view(np.uint16),
                              dev_out[last].cpu().numpy().view(np.uint16))
     assert int(err.item()) == 0
+    return {"value": round(e2e_value, 2), "unit": "GB/s", "steps": e2e_steps,
+            "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h,
+            "path": "pinned host pools+segments -> H2D -> device-table sync -> "
+                    "hlkv_gather_dequant -> D2H of the FP16 output; two buffer sets, "
+                    "upload of step k overlaps readback of step k-1", "readback_ok": ok_bits}
 
-    cpu = None
-    if world == 1 and not args.no_cpu_baseline:
-        cpu = cpu_gather_sample(wl, nseq_sample=min(16, len(wl.segs_host)))
 
-    if rank == 0:
-        line = {
-            "metric": METRIC, "value": round(value, 2), "unit": "GB/s", "n_gpus": world,
-            "steps": args.steps, "warmup": args.warmup,
-            "ms_per_step": round(total_ms / args.steps, 5), "higher_is_better": True,
-            "scaling": "weak", "vs_baseline": None, "dtype": "fp16 out; fp16/e4m3/int4 in",
-            "data": "synthetic (seeded N(0,1) + outlier channels, quantized on the GPU)",
-            "config": {"workload": spec["name"], "blocks_per_gpu": wl.total_blocks,
-                       "blocks_per_format": {"fp16": wl.blocks_per_format[0],
-                                             "e4m3": wl.blocks_per_format[1],
-                                             "int4": wl.blocks_per_format[3]},
-                       "bytes_per_step_per_gpu": bytes_per_step,
-                       "l2": ("inputs+outputs (%.0f MB) exceed 4x the %.0f MB L2; no flush" % (
-                           bytes_per_step / 1e6, l2_bytes / 1e6)) if flush is None else
-                             ("L2 flushed between steps (%.0f MB overwritten); value from the "
-                              "per-launch events" % (2 * l2_bytes / 1e6)),
-                       "parallelism": f"sequence-sharded x{world}, no collective on the data path"},
-            "per_gpu_gbs": round(per_gpu, 2),
-            "pct_hbm_peak": round(100 * per_gpu / peak, 2),
-            "roofline": {"bound": "hbm", "achieved": round(achieved, 2), "peak": peak,
-                         "unit": "GB/s", "frac": round(achieved / peak, 4),
-                         "peak_source": f"{peak_kind} (MEASURED_PEAKS.json hbm_gbs)",
-                         "traffic": traffic_from_profile(args.workload),
-                         "kernel": "gather_dequant_kernel<128>", "launch_ms": round(mean_launch_ms, 5)},
-            "e2e": {"value": round(e2e_value, 2), "unit": "GB/s", "steps": e2e_steps,
-                    "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h,
-                    "path": "pinned host pools+segments -> H2D -> device-table sync -> "
-                            "hlkv_gather_dequant -> D2H of the FP16 output; two buffer sets, "
-                            "upload of step k overlaps readback of step k-1", "readback_ok": ok_bits},
-            "gpu_launches": args.steps,  # gather launches in the timed region
-            "clocks": clocks.summary(h0, h1),
-            "cpu_baseline": cpu,
-        }
-        print(json.dumps(line), flush=True)
-    if world > 1:
-        dist.barrier()
-        dist.destroy_process_group()
+def _blocks_and_probs(spec: dict):
+    """Blocks per sequence-layer and the format mix; age tiers become their proportions
+    (the CPU cost of a block depends only on its format)."""
+    if "tiers" not in spec:
+        return spec["blocks"], spec["probs"]
+    nb = spec["tokens"] // 16
+    n16, n8 = spec["tiers"][0] // 16, spec["tiers"][1] // 16
+    return nb, (n16 / nb, n8 / nb, 0.0, (nb - n16 - n8) / nb)
 
 
 def run_reference(args) -> None:
@@ -379,12 +657,16 @@ def run_reference(args) -> None:
     spec = WORKLOADS[args.workload]
     kind = "reference" if ref_available() else "port"
     threads = os.cpu_count() or 1
+    if spec.get("decode"):
+        run_reference_decode(args, spec, kind, threads)
+        return
     # Size the per-step sample so that warm-up + steps stay within about two minutes.
     budget_s = 120.0 / max(1, args.steps + args.warmup)
-    wl = build_cpu_workload(kind, nseq=1, blocks=spec["blocks"], probs=spec["probs"], seed=1000)
+    blocks, probs = _blocks_and_probs(spec)
+    wl = build_cpu_workload(kind, nseq=1, blocks=blocks, probs=probs, seed=1000)
     per_seq_s = time_cpu_gather(wl, threads)[0]
     nseq = int(max(1, min(spec["nseq"], budget_s / max(per_seq_s, 1e-6))))
-    wl = build_cpu_workload(kind, nseq=nseq, blocks=spec["blocks"], probs=spec["probs"], seed=1000)
+    wl = build_cpu_workload(kind, nseq=nseq, blocks=blocks, probs=probs, seed=1000)
     for _ in range(args.warmup):
         time_cpu_gather(wl, threads)
     times = [time_cpu_gather(wl, threads)[0] for _ in range(args.steps)]
@@ -406,6 +688,45 @@ def run_reference(args) -> None:
     }), flush=True)
 
 
+def run_reference_decode(args, spec: dict, kind: str, threads: int) -> None:
+    """The reference's CPU encode of one decode step (quantize_reference per row of every
+    appended token, formats E4M3/INT4 .5/.5) on all host threads."""
+    import numpy as np
+    from oracle.oracle import Oracle, Ref
+    impl = Ref() if kind == "reference" else Oracle()
+    H, D = 8, 128
+    n = spec["nseq"] * spec["layers"]
+    rng = np.random.default_rng(3001)
+    fmt = rng.choice(np.array([1, 3], np.uint8), size=n)
+    x = rng.standard_normal((n * 2 * H, D)).astype(np.float16).astype(np.float32)
+    fm = np.repeat(fmt, 2 * H)
+    params = np.zeros((x.shape[0], 2), np.float32)
+    codes = np.zeros(x.shape, np.uint8)
+    for _ in range(args.warmup):
+        impl.quantize_rows(fm, x, params, codes, threads)
+    times = []
+    for _ in range(args.steps):
+        t0 = time.perf_counter()
+        assert impl.quantize_rows(fm, x, params, codes, threads) == 0
+        times.append(time.perf_counter() - t0)
+    n8 = int((fmt == 1).sum())
+    nbytes = n * (2 * H * D * 2 + 16) + n8 * (2 * H * D + 2 * H * 4) + (n - n8) * (H * D + 2 * H * 8)
+    total = sum(times)
+    value = nbytes * args.steps / total / 1e9
+    print(json.dumps({
+        "impl": "reference", "metric": METRIC, "value": round(value, 3), "unit": "GB/s",
+        "n_gpus": int(os.environ.get("WORLD_SIZE", "1")), "steps": args.steps, "warmup": args.warmup,
+        "ms_per_step": round(1e3 * total / args.steps, 3), "higher_is_better": True,
+        "scaling": "strong", "vs_baseline": None, "dtype": "fp16 in; e4m3/int4 out",
+        "data": "synthetic (seeded N(0,1) tokens, formats .5/.5)",
+        "config": {"workload": spec["name"], "parallelism": f"{threads} host threads"},
+        "cpu_baseline": {"value": round(value, 3), "unit": "GB/s", "cores": threads, "kind": kind,
+                         "sample": f"one full step: {n} appended tokens ({x.shape[0]} rows of {D})"},
+        "e2e": {"value": round(value, 3), "unit": "GB/s", "h2d_bytes_per_step": 0,
+                "d2h_bytes_per_step": 0},
+    }), flush=True)
+
+
 def main() -> None:
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
@@ -417,6 +738,9 @@ def main() -> None:
     ap.add_argument("--no-cpu-baseline", action="store_true")
     args = ap.parse_args()
     args.warmup = max(args.warmup, 3)
+    if args.impl == "hlkv" and WORKLOADS[args.workload].get("decode"):
+        run_decode(args)
+        return
     if args.impl == "reference":
         run_reference(args)
     else:

@@ -197,6 +197,44 @@ int hlkv_table_batch_segments(const hlkv_table* t, const HlkvHandle* seqs, size_
   return st(s);
 }
 
+int hlkv_table_append_tokens(hlkv_table* t, const HlkvHandle* seqs, size_t n,
+                             const uint32_t* new_formats, uint32_t layout,
+                             HlkvAppendTarget* out, size_t* n_done) {
+  if (n_done != nullptr) *n_done = 0;
+  if (n > 0 && (seqs == nullptr || new_formats == nullptr || out == nullptr)) {
+    return HLKV_STATUS_INVALID_ARGUMENT;
+  }
+  const std::uint32_t T = t->t.block_tokens();
+  for (size_t i = 0; i < n; ++i) {
+    const SequenceHandle seq = sh(seqs[i]);
+    const Result<std::span<const std::uint32_t>> ids = t->t.sequence_block_ids(seq);
+    if (!ids.ok()) return st(ids.status());
+    if (!ids.value().empty()) {
+      const std::uint32_t tail = ids.value().back();
+      const BlockHandle h = t->t.handle_of(tail);
+      const Result<BlockDescriptor> d = t->t.lookup(h);
+      if (!d.ok()) return st(d.status());
+      const std::uint32_t vt = d.value().exec.valid_tokens();
+      if (vt < T) {
+        const Status s = t->t.set_valid_tokens(h, vt + 1);
+        if (s != Status::kOk) return st(s);
+        out[i] = HlkvAppendTarget{tail, vt};
+        if (n_done != nullptr) *n_done = i + 1;
+        continue;
+      }
+    }
+    AllocRequest req;
+    req.format = fmt(new_formats[i]);
+    req.valid_tokens = 1;
+    req.layout = layout;
+    const Result<BlockHandle> r = t->t.append_block(seq, req);
+    if (!r.ok()) return st(r.status());
+    out[i] = HlkvAppendTarget{r.value().id, 0};
+    if (n_done != nullptr) *n_done = i + 1;
+  }
+  return HLKV_STATUS_OK;
+}
+
 int hlkv_table_build_exec_table(const hlkv_table* t, const HlkvHandle* seqs, size_t n,
                                 uint32_t* indptr, HlkvExecDescriptor* blocks, size_t cap,
                                 size_t* total) {

@@ -9,7 +9,9 @@
 // Structure (HBM-bound; no tensor cores):
 //  * persistent grid: one wave of CTAs (SMs x resident CTAs); CTA c owns the
 //    global block indices w = c, c + G, c + 2G, ... so every CTA gets a mix of
-//    formats;
+//    formats.  When a chunk holds fewer than two blocks per CTA, each block is
+//    split into 2, 4 or 8 tile ranges ("pieces") owned the same way, so small
+//    batches still occupy every SM;
 //  * the segments are scanned in chunks of 256 sequences (block-wide prefix
 //    sum in shared memory), so the kernel needs no host-side prefix and no
 //    scratch memory;
@@ -44,6 +46,7 @@ constexpr int kThreads = 256;
 constexpr int kMinCtasPerSm = HLKV_GATHER_MIN_CTAS;  // 4: 64 registers per thread
 constexpr int kUnroll = HLKV_GATHER_UNROLL;          // chunks per lane per tile: 2 KB tiles
 constexpr int kDefaultWaves = 1;
+constexpr uint32_t kTileChunks = 32 * kUnroll;  // 8-element chunks per warp tile
 
 struct DevPool {
   const uint8_t* base;
@@ -70,6 +73,8 @@ struct Item {
   uint16_t* out;
   uint32_t fmt;         // 0..3, or kSkip
   uint32_t valid_rows;  // rows per K/V half holding valid tokens: valid_tokens * H
+  uint32_t tile_begin;  // warp tiles [tile_begin, tile_end) of the block are streamed
+  uint32_t tile_end;
 };
 constexpr uint32_t kSkip = 0xFFu;
 
@@ -77,7 +82,7 @@ constexpr uint32_t kSkip = 0xFFu;
 // is skipped and its bit reported.  Check order matches the oracle's
 // resolve_block().
 __device__ Item resolve(const Params& p, uint32_t seq, uint64_t j, uint64_t blocks_before) {
-  Item it{nullptr, nullptr, kSkip, 0};
+  Item it{nullptr, nullptr, kSkip, 0, 0, 0};
   uint32_t bad = 0;
   const uint64_t base = p.out_offsets ? p.out_offsets[seq] : blocks_before * p.block_elems;
   if (base & 7u) {
@@ -140,7 +145,8 @@ __device__ __forceinline__ void stream_block(const Params& p, const Item& it, ui
   const uint8_t* params = payload + p.code_bytes[f];
   uint4* out = reinterpret_cast<uint4*>(it.out);
 
-  for (uint32_t t0 = warp * kTile; t0 < nchunks; t0 += kThreads * kUnroll) {
+  for (uint32_t t = it.tile_begin + warp; t < it.tile_end; t += kThreads / 32) {
+    const uint32_t t0 = t * kTile;
     uint4 raw[kUnroll];
     float2 prm[kUnroll];
     uint32_t live = 0;
@@ -229,28 +235,40 @@ __global__ void __launch_bounds__(kThreads, kMinCtasPerSm) gather_dequant_kernel
   __shared__ __align__(128) uint4 s_tile[kThreads / 32][32 * kUnroll];  // one output tile per warp
 
   const uint64_t G = gridDim.x, c = blockIdx.x;
-  uint64_t base = 0;  // blocks before the current chunk of sequences
+  const uint32_t ntiles = static_cast<uint32_t>(((p.block_elems >> 3) + kTileChunks - 1) / kTileChunks);
+  uint64_t base = 0;   // blocks before the current chunk of sequences
+  uint64_t pbase = 0;  // pieces before the current chunk
   for (uint32_t chunk = 0; chunk < p.nseq; chunk += kThreads) {
     const uint32_t cnt = min(p.nseq - chunk, static_cast<uint32_t>(kThreads));
     const uint64_t len = threadIdx.x < cnt ? p.segs[chunk + threadIdx.x].y : 0u;
     const uint64_t total = exclusive_scan(len, s_prefix, s_warp);
     const uint64_t end = base + total;
-    // First owned index >= base: w = c (mod G).
-    uint64_t first = base + (c + G - base % G) % G;
-    for (; first < end; first += uint64_t{kThreads} * G) {
-      const uint64_t w = first + threadIdx.x * G;
-      if (w < end) {
-        const uint64_t local = w - base;
+    // Pieces: a chunk with fewer than 2 blocks per CTA splits every block into `parts`
+    // tile ranges (each at least 8 tiles, one per warp), so that every CTA gets work.
+    uint32_t parts = 1;
+    while (parts < 8 && total * parts < 2 * G && ntiles >= 16 * parts) parts *= 2;
+    const uint64_t pend = pbase + total * parts;
+    // First owned piece >= pbase: q = c (mod G).
+    uint64_t first = pbase + (c + G - pbase % G) % G;
+    for (; first < pend; first += uint64_t{kThreads} * G) {
+      const uint64_t q = first + threadIdx.x * G;
+      if (q < pend) {
+        const uint64_t lq = q - pbase;
+        const uint64_t local = lq / parts;
         uint32_t lo = 0, hi = cnt;  // last s with s_prefix[s] <= local
         while (hi - lo > 1) {
           const uint32_t mid = (lo + hi) >> 1;
           if (s_prefix[mid] <= local) lo = mid; else hi = mid;
         }
-        s_item[threadIdx.x] = resolve(p, chunk + lo, local - s_prefix[lo], base + s_prefix[lo]);
+        Item it = resolve(p, chunk + lo, local - s_prefix[lo], base + s_prefix[lo]);
+        const uint32_t per_part = (ntiles + parts - 1) / parts;
+        it.tile_begin = static_cast<uint32_t>(lq % parts) * per_part;
+        it.tile_end = min(ntiles, it.tile_begin + per_part);
+        s_item[threadIdx.x] = it;
       }
       __syncthreads();
       const uint32_t n_items =
-          static_cast<uint32_t>(min(uint64_t{kThreads}, (end - first + G - 1) / G));
+          static_cast<uint32_t>(min(uint64_t{kThreads}, (pend - first + G - 1) / G));
       for (uint32_t k = 0; k < n_items; ++k) {
         const Item it = s_item[k];
         if (it.fmt != kSkip) stream_block<kD>(p, it, s_tile[threadIdx.x >> 5]);
@@ -258,6 +276,7 @@ __global__ void __launch_bounds__(kThreads, kMinCtasPerSm) gather_dequant_kernel
       __syncthreads();  // s_item is rewritten by the next batch
     }
     base = end;
+    pbase = pend;
     __syncthreads();  // s_prefix is rewritten by the next chunk
   }
   // Shared memory must outlive the bulk stores that read it.

@@ -158,6 +158,7 @@ SIGNATURES: list[tuple[str, object, list]] = [
     ("hlkv_table_release_sequence", _int, [_vp, Handle]),
     ("hlkv_table_sequence_block_ids", _int, [_vp, Handle, _P(_u32), _sz, _P(_sz)]),
     ("hlkv_table_batch_segments", _int, [_vp, _P(Handle), _sz, _P(Segment)]),
+    ("hlkv_table_append_tokens", _int, [_vp, _P(Handle), _sz, _P(_u32), _u32, _vp, _P(_sz)]),
     ("hlkv_table_build_exec_table", _int, [_vp, _P(Handle), _sz, _P(_u32), _P(ExecDescriptor),
                                            _sz, _P(_sz)]),
     ("hlkv_table_pending", None, [_vp, _P(_sz), _P(_sz)]),
@@ -340,6 +341,21 @@ class Table:
         out = np.zeros((max(len(seqs), 1), 2), dtype=np.uint32)
         st = lib().hlkv_table_batch_segments(self.h, hs, len(seqs), out.ctypes.data_as(_P(Segment)))
         return st, out[: len(seqs)]
+
+    def append_tokens(self, seqs, new_formats, layout: int, out=None):
+        """Decode-step driver: one more token per sequence.  seqs: a ctypes Handle array
+        (or sequence of Handles); new_formats: uint32 per sequence.  Returns (status,
+        targets uint32 [n, 2] = (block_id, token), n_done)."""
+        import numpy as np
+        n = len(seqs)
+        hs = seqs if isinstance(seqs, C.Array) else (Handle * max(n, 1))(*seqs)
+        fm = np.ascontiguousarray(new_formats, dtype=np.uint32)
+        if out is None:
+            out = np.zeros((max(n, 1), 2), dtype=np.uint32)
+        done = _sz()
+        st = lib().hlkv_table_append_tokens(self.h, hs, n, fm.ctypes.data_as(_P(_u32)), layout,
+                                            out.ctypes.data, C.byref(done))
+        return st, out[:n], done.value
 
     def build_exec_table(self, seqs: Sequence[Handle]):
         """Returns (status, indptr uint32 [n+1], blocks uint32 [m, 4])."""

@@ -285,6 +285,17 @@ int hlkv_table_sequence_block_ids(const hlkv_table* t, HlkvHandle seq, uint32_t*
                                   size_t* len);
 int hlkv_table_batch_segments(const hlkv_table* t, const HlkvHandle* seqs, size_t n,
                               HlkvSegment* out);
+/*
+ * Decode-step driver (no counterpart in the reference; built only from the public table
+ * operations above): for each sequence seqs[i], makes room for one more token -- in its
+ * tail block when that holds fewer than block_tokens valid tokens (set_valid_tokens + 1),
+ * else in a new block appended with req {new_formats[i], valid_tokens 1, layout} -- and
+ * writes the new token's kernel (2) target to out[i].  Stops at the first failing
+ * operation and returns its status; *n_done = sequences completed.
+ */
+int hlkv_table_append_tokens(hlkv_table* t, const HlkvHandle* seqs, size_t n,
+                             const uint32_t* new_formats, uint32_t layout,
+                             HlkvAppendTarget* out, size_t* n_done);
 /* CSR reference path: indptr[n+1], blocks[cap]; *total = number of blocks. */
 int hlkv_table_build_exec_table(const hlkv_table* t, const HlkvHandle* seqs, size_t n,
                                 uint32_t* indptr, HlkvExecDescriptor* blocks, size_t cap,

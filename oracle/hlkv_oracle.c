@@ -581,3 +581,46 @@ ORC_API void orc_gaussian(uint64_t seed, float sigma, float* out, size_t n) {
     out[i] = sigma * (float)(sqrt(-2.0 * log(u1)) * cos(6.283185307179586 * u2));
   }
 }
+
+/* ---- per-row encode over threads (the decode-append CPU baseline) ------------------------- */
+/* quantize_reference per row of D values (cpu_quant.cpp:97-170), one group per row, row r
+ * in format fmt[r] (E4M3, E5M2 or INT4); codes of row r at codes + r * D, params {scale, bias}
+ * at params + 2r.
+ * Returns the number of rows rejected. */
+typedef struct {
+  const uint8_t* fmt;
+  const float* in;
+  size_t lo, hi, D, bad;
+  float* params;
+  uint8_t* codes;
+} rows_job;
+
+static void* rows_worker(void* arg) {
+  rows_job* j = (rows_job*)arg;
+  for (size_t r = j->lo; r < j->hi; ++r) {
+    if (orc_quantize((int)j->fmt[r], j->in + r * j->D, j->D, j->D, j->params + 2 * r, 1,
+                     j->codes + r * j->D, j->D) != ORC_OK) {
+      ++j->bad;
+    }
+  }
+  return NULL;
+}
+
+ORC_API size_t orc_quantize_rows(const uint8_t* fmt, const float* in, size_t rows, size_t D,
+                                 float* params, uint8_t* codes, int threads) {
+  if (threads < 1) threads = 1;
+  if (threads > 256) threads = 256;
+  pthread_t tids[256];
+  rows_job jobs[256];
+  for (int t = 0; t < threads; ++t) {
+    jobs[t] = (rows_job){fmt, in, rows * (size_t)t / (size_t)threads,
+                         rows * (size_t)(t + 1) / (size_t)threads, D, 0, params, codes};
+    pthread_create(&tids[t], NULL, rows_worker, &jobs[t]);
+  }
+  size_t bad = 0;
+  for (int t = 0; t < threads; ++t) {
+    pthread_join(tids[t], NULL);
+    bad += jobs[t].bad;
+  }
+  return bad;
+}

@@ -83,6 +83,21 @@ class _Common:
         f.argtypes = [C.POINTER(Pool), C.c_uint32, C.c_uint32, C.c_uint32, C.c_uint32, u32p,
                       C.c_uint32, u32p, C.c_uint32, u32p, C.c_uint32, u64p, u16p, u64p, C.c_int]
         f.restype = C.c_uint32
+        f = getattr(L, p + "quantize_rows")
+        f.argtypes = [u8p, f32p, C.c_size_t, C.c_size_t, f32p, u8p, C.c_int]
+        f.restype = C.c_size_t
+
+    def quantize_rows(self, fmt: np.ndarray, x: np.ndarray, params: np.ndarray, codes: np.ndarray,
+                      threads: int = 1) -> int:
+        """quantize_reference per row of x [rows, D] (row r in format fmt[r], one group per
+        row) into params [rows, 2] and codes [rows, D] (packed bytes at the row start), over
+        `threads` threads; returns the number of rejected rows."""
+        rows, D = x.shape
+        fm = np.ascontiguousarray(fmt, dtype=np.uint8)
+        assert x.dtype == np.float32 and x.flags.c_contiguous and fm.size == rows
+        assert params.shape == (rows, 2) and codes.shape == (rows, D)
+        return int(getattr(self.lib, self.prefix + "quantize_rows")(
+            _p(fm, u8p), _p(x, f32p), rows, D, _p(params, f32p), _p(codes, u8p), threads))
 
     # -- codecs -------------------------------------------------------------------------
     def encode(self, fmt: int, x: np.ndarray) -> np.ndarray:

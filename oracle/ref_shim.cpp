@@ -362,3 +362,32 @@ REF_API std::uint32_t ref_workload_gather(void* wp, std::uint16_t* out, int thre
 }
 
 REF_API void ref_workload_free(void* w) { delete static_cast<RefWorkload*>(w); }
+
+// The CPU baseline of the decode-append step: quantize_reference on each row of D
+// binary32 values (one parameter group per row, format fmt[r]: E4M3, E5M2 or INT4), rows split over
+// `threads` std::thread workers.  codes: row r at codes + r * D (packed_bytes of the
+// format used); params: {scale, bias} per row.  Returns the number of rows rejected.
+REF_API std::size_t ref_quantize_rows(const std::uint8_t* fmt, const float* in, std::size_t rows,
+                                      std::size_t D, float* params, std::uint8_t* codes,
+                                      int threads) {
+  if (threads < 1) threads = 1;
+  std::vector<std::size_t> bad(static_cast<std::size_t>(threads), 0);
+  auto work = [&](int t) {
+    const std::size_t lo = rows * static_cast<std::size_t>(t) / static_cast<std::size_t>(threads);
+    const std::size_t hi = rows * static_cast<std::size_t>(t + 1) / static_cast<std::size_t>(threads);
+    for (std::size_t r = lo; r < hi; ++r) {
+      const auto f = static_cast<q::QuantFormat>(fmt[r]);
+      const q::QuantStatus s = q::quantize_reference(
+          f, std::span<const float>(in + r * D, D), D,
+          std::span<q::AffineParams>(reinterpret_cast<q::AffineParams*>(params + 2 * r), 1),
+          std::span<std::byte>(reinterpret_cast<std::byte*>(codes + r * D), D));
+      if (s != q::QuantStatus::kOk) ++bad[static_cast<std::size_t>(t)];
+    }
+  };
+  std::vector<std::thread> pool;
+  for (int t = 0; t < threads; ++t) pool.emplace_back(work, t);
+  for (std::thread& th : pool) th.join();
+  std::size_t n = 0;
+  for (const std::size_t b : bad) n += b;
+  return n;
+}

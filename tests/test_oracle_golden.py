@@ -302,3 +302,23 @@ def test_gather_oracle_matches_reference_gather(oracle, ref):
     eb = ref.gather_dequant(pools, T, H, D, 1, table, arena, segs, b, threads=3)
     assert ea == eb and ea & 8 and ea & 1
     assert np.array_equal(a, b)
+
+
+def test_quantize_rows_oracle_equals_reference(oracle, ref):
+    """The threaded per-row encoders (the decode-append CPU baseline) of the oracle and of
+    the reference library agree bit for bit, and each row equals a single quantize call."""
+    rng = np.random.default_rng(21)
+    x = (rng.standard_normal((777, 128)) * rng.choice([1e-3, 1.0, 50.0], size=(777, 1))).astype(np.float32)
+    x[3] = 0.0
+    x[4, ::2] = -0.0
+    fm = rng.choice([1, 2, 3], size=777).astype(np.uint8)
+    res = []
+    for impl in (oracle, ref):
+        p = np.zeros((777, 2), np.float32)
+        c = np.zeros((777, 128), np.uint8)
+        assert impl.quantize_rows(fm, x, p, c, threads=5) == 0
+        res.append((p.view(np.uint32).copy(), c.copy()))
+    assert np.array_equal(res[0][0], res[1][0]) and np.array_equal(res[0][1], res[1][1])
+    for r in (0, 3, 4, 500):
+        st, p1, c1 = oracle.quantize(int(fm[r]), x[r], 128)
+        assert st == 0 and np.array_equal(c1, res[0][1][r][:c1.size])

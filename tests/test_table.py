@@ -114,3 +114,47 @@ def test_c_abi_table_matches_reference_behaviour(hlkv_lib):
     stats = t.stats()
     assert stats["format_changes_committed"] == 1 and stats["arena_free_entries"] == 8
     assert t.device_descriptor(100) == (0xFFFFFFFF, 15, 0, 100)
+
+
+def test_append_tokens_decode_driver(hlkv_lib):
+    """hlkv_table_append_tokens = per sequence: set_valid_tokens(tail, vt + 1) while the tail
+    has room, else append_block(new format, 1 valid token); the same table state and the
+    same delta as those calls made one by one on a second table."""
+    h = hlkv_lib
+    T = 4
+    pools = [(1, 2048, 64), (3, 1088, 64)]
+    a, b = h.Table(128, pools, block_tokens=T), h.Table(128, pools, block_tokens=T)
+    seqs_a = [a.create_sequence()[1] for _ in range(3)]
+    seqs_b = [b.create_sequence()[1] for _ in range(3)]
+    for t, ss in ((a, seqs_a), (b, seqs_b)):       # sequence 0 starts with a partial tail
+        t.append_block(ss[0], 1, 2)
+    a.collect_delta()
+    b.collect_delta()
+    rng = np.random.default_rng(3)
+    for step in range(11):
+        fm = rng.choice([1, 3], size=3).astype(np.uint32)
+        st, targets, done = a.append_tokens(seqs_a, fm, 1)
+        assert st == 0 and done == 3
+        for i, s in enumerate(seqs_b):               # the same step, one call at a time
+            st_i, ids = b.sequence_block_ids(s)
+            vt = None
+            if ids:
+                tail = b.handle_of(ids[-1])
+                vt = (int(np.frombuffer(b.lookup(tail)[1], np.uint32)[1]) >> 10) & 0x3FF
+            if vt is not None and vt < T:
+                assert b.set_valid_tokens(tail, vt + 1) == 0
+                want = (ids[-1], vt)
+            else:
+                st_b, nb = b.append_block(s, int(fm[i]), 1, 1)
+                assert st_b == 0
+                want = (nb.id, 0)
+            assert tuple(targets[i]) == want, (step, i)
+        da, db = a.collect_delta(), b.collect_delta()
+        assert np.array_equal(da.descriptor_patches, db.descriptor_patches)
+        assert np.array_equal(da.id_patches, db.id_patches)
+    for sa, sb in zip(seqs_a, seqs_b):
+        assert a.sequence_block_ids(sa) == b.sequence_block_ids(sb)
+    # errors: a stale sequence handle stops the batch at that sequence
+    assert a.release_sequence(seqs_a[1]) == 0
+    st, targets, done = a.append_tokens(seqs_a, np.ones(3, np.uint32), 1)
+    assert st == h.Status.STALE_HANDLE and done == 1
