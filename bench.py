@@ -77,6 +77,11 @@ WORKLOADS = {
                         "x 128, K+V; one N(0,1) FP16 token per seq-layer per step encoded into its "
                         "tail block (E4M3 or INT4 .5/.5, a new block every 16 tokens) + descriptor "
                         "delta applied on the device"),
+    # The same step on short sequences (1-48 tokens): the same 8192 appends per step on
+    # a cache of a few hundred MB, the case small enough for a full ncu capture.
+    "decode_small": dict(nseq=256, min_len=1, max_len=48, layers=32, scaling="strong", decode=True,
+                         name="decode-step append, short sequences: 256 seq (lengths U[1, 48]) x 32 "
+                              "layers, 8 KV heads x 128, K+V; E4M3 or INT4 .5/.5 tail blocks"),
 }
 
 
@@ -111,45 +116,59 @@ def max_over_ranks(values, world: int, device) -> list[float]:
     return t.tolist()
 
 
-class ClockSampler:
-    """Samples SM clock and throttle reasons of one GPU through NVML in a thread."""
+_SAMPLER = r"""
+import sys, time
+import pynvml
+pynvml.nvmlInit()
+h = pynvml.nvmlDeviceGetHandleByIndex(int(sys.argv[1]))
+period = float(sys.argv[2])
+print("max", pynvml.nvmlDeviceGetMaxClockInfo(h, pynvml.NVML_CLOCK_SM), flush=True)
+while True:
+    try:
+        mhz = pynvml.nvmlDeviceGetClockInfo(h, pynvml.NVML_CLOCK_SM)
+        reasons = pynvml.nvmlDeviceGetCurrentClocksEventReasons(h)
+        print(time.time(), mhz, reasons, flush=True)
+    except pynvml.NVMLError:
+        pass
+    time.sleep(period)
+"""
 
-    def __init__(self, index: int, period_s: float = 0.002):
-        self.index, self.period = index, period_s
+
+class ClockSampler:
+    """Samples SM clock and throttle reasons of one GPU through NVML in a child process
+    (NVML calls made from the benchmarked process contend with its CUDA calls).
+    Sample times are time.time(); summary() takes the same clock."""
+
+    def __init__(self, index: int, period_s: float = 0.01):
+        # NVML enumerates all GPUs; map the CUDA index through CUDA_VISIBLE_DEVICES.
+        vis = os.environ.get("CUDA_VISIBLE_DEVICES")
+        self.index = int(vis.split(",")[index]) if vis and vis.split(",")[0].isdigit() else index
+        self.period = period_s
         self.samples: list[tuple[float, int, int]] = []
-        self._stop = threading.Event()
-        self._t = None
         self.max_mhz = None
+        self._p = None
 
     def __enter__(self):
+        import subprocess
         try:
-            import pynvml
-            pynvml.nvmlInit()
-            self._nv = pynvml
-            self._h = pynvml.nvmlDeviceGetHandleByIndex(self.index)
-            self.max_mhz = pynvml.nvmlDeviceGetMaxClockInfo(self._h, pynvml.NVML_CLOCK_SM)
+            self._p = subprocess.Popen([sys.executable, "-c", _SAMPLER, str(self.index), str(self.period)],
+                                       stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
+            first = self._p.stdout.readline().split()
+            self.max_mhz = int(first[1]) if len(first) == 2 and first[0] == "max" else None
         except Exception:
-            self._nv = None
-            return self
-        self._t = threading.Thread(target=self._run, daemon=True)
-        self._t.start()
+            self._p = None
         return self
 
-    def _run(self):
-        nv = self._nv
-        while not self._stop.is_set():
-            try:
-                mhz = nv.nvmlDeviceGetClockInfo(self._h, nv.NVML_CLOCK_SM)
-                reasons = nv.nvmlDeviceGetCurrentClocksEventReasons(self._h)
-                self.samples.append((time.perf_counter(), mhz, reasons))
-            except Exception:
-                pass
-            time.sleep(self.period)
-
     def __exit__(self, *exc):
-        self._stop.set()
-        if self._t is not None:
-            self._t.join()
+        if self._p is None:
+            return
+        time.sleep(2 * self.period)
+        self._p.terminate()  # this child only, by its own handle
+        out, _ = self._p.communicate(timeout=30)
+        for line in out.splitlines():
+            f = line.split()
+            if len(f) == 3:
+                self.samples.append((float(f[0]), int(f[1]), int(f[2])))
 
     def summary(self, t0: float, t1: float) -> dict:
         names = {0x2: "applications_clocks_setting", 0x4: "sw_power_cap", 0x8: "hw_slowdown",
@@ -284,7 +303,7 @@ def run_hlkv(args) -> None:
     with ClockSampler(torch.cuda.current_device()) as clocks:
         barrier()
         torch.cuda.synchronize()
-        h0 = time.perf_counter()
+        h0 = time.time()
         t_start.record(stream)
         for k in range(args.steps):
             if flush is not None:
@@ -294,7 +313,7 @@ def run_hlkv(args) -> None:
             ev[k][1].record(stream)
         t_end.record(stream)
         torch.cuda.synchronize()
-        h1 = time.perf_counter()
+        h1 = time.time()
         barrier()
     total_ms = t_start.elapsed_time(t_end)
     step_ms = [a.elapsed_time(b) for a, b in ev]
@@ -442,11 +461,12 @@ def run_decode(args) -> None:
         assert st == 0 and done == n, (st, done)
         nd, ni = table.pending()
         h1 = time.perf_counter()
+        dt.collect(table)  # host half of the delta protocol: nothing queued on the GPU yet
+        h2 = time.perf_counter()
         ev[k][0].record(stream)
         d_targets[b].copy_(pinned[b], non_blocking=True)
         copied[b].record(stream)
-        dt.sync(table, stream)  # collect_delta on the host, upload, kernel (3)
-        h2 = time.perf_counter()
+        dt.flush(stream)  # upload + kernel (3)
         ev[k][1].record(stream)
         hlkv.append_encode(pools, layout, dt.table_ptr, dt.table_size, d_targets[b], tokens[k % 4],
                            err, stream=stream)
@@ -467,11 +487,11 @@ def run_decode(args) -> None:
         if world > 1:
             dist.barrier()
         torch.cuda.synchronize()
-        w0 = time.perf_counter()
+        w0, c0 = time.perf_counter(), time.time()
         for k in range(args.warmup, steps_total):
             step(k, True)
         torch.cuda.synchronize()
-        w1 = time.perf_counter()
+        w1, c1 = time.perf_counter(), time.time()
     assert int(err.item()) == 0, f"error bits {int(err.item()):#x}"
     timed = ev[args.warmup:]
     dev_ms = [e[0].elapsed_time(e[2]) for e in timed]
@@ -504,7 +524,7 @@ def run_decode(args) -> None:
                             "encode_kernel": round(1e3 * enc_mean, 2),
                             "delta_upload_and_apply": round(1e3 * delta_mean, 2),
                             "host_table_ops": round(1e6 * host["table_s"] / args.steps, 2),
-                            "host_collect_delta_and_launch": round(1e6 * host["sync_s"] / args.steps, 2),
+                            "host_collect_delta": round(1e6 * host["sync_s"] / args.steps, 2),
                             "wall": round(1e3 * wall_ms / args.steps, 2)},
             "roofline": {"bound": "hbm", "achieved": round(achieved, 2), "peak": peak, "unit": "GB/s",
                          "frac": round(achieved / peak, 4),
@@ -515,8 +535,8 @@ def run_decode(args) -> None:
                     "h2d_bytes_per_step": n * 8, "d2h_bytes_per_step": 0,
                     "path": "host table ops + collect_delta -> H2D of targets and delta -> "
                             "apply_delta -> append_encode, wall clock per step (tokens resident)"},
-            "gpu_launches": 2 * args.steps,
-            "clocks": clocks.summary(w0, w1),
+            "gpu_launches": 2 * args.steps,  # apply_delta + append_encode per step
+            "clocks": clocks.summary(c0, c1),
             "cpu_baseline": cpu,
         }), flush=True)
     if world > 1:

@@ -331,6 +331,20 @@ int hlkv_device_tables_sync(hlkv_device_tables* dt, hlkv_table* t, hlkv_stream_t
   return static_cast<int>(s.status);
 }
 
+int hlkv_device_tables_collect(hlkv_device_tables* dt, hlkv_table* t) {
+  if (dt == nullptr || t == nullptr) return HLKV_INVALID_ARGUMENT;
+  try {
+    return static_cast<int>(dt->dt.collect(t->t).status);
+  } catch (const std::bad_alloc&) {
+    return HLKV_BUFFER_TOO_SMALL;
+  }
+}
+
+int hlkv_device_tables_flush(hlkv_device_tables* dt, hlkv_stream_t stream) {
+  if (dt == nullptr) return HLKV_INVALID_ARGUMENT;
+  return static_cast<int>(dt->dt.flush(reinterpret_cast<cudaStream_t>(stream)).status);
+}
+
 const HlkvExecDescriptor* hlkv_device_tables_table(const hlkv_device_tables* dt) {
   return reinterpret_cast<const HlkvExecDescriptor*>(dt->dt.table());
 }

@@ -10,7 +10,8 @@
 // A row is handled by D/8 lanes (16 for D = 128), 8 elements per lane from one
 // 16-byte load; group statistics use shuffle reductions across those lanes:
 //   FP8   amax -> scale = max(amax / max_finite, FLT_MIN) (1 when amax == 0),
-//         code = RNE-saturating encode of x / scale (IEEE division);
+//         code = RNE-saturating encode of x / scale (IEEE division; the encode is
+//         the hardware cvt.rn.satfinite, equal to the reference's integer RNE);
 //   INT4  (min, first index) and (max, last index), which is what
 //         std::minmax_element returns and what makes the bias bits of +-0
 //         ties exact; scale = (max - min) / 15, q = clamp(rint((x - min)/scale)).
@@ -91,8 +92,10 @@ __global__ void __launch_bounds__(kThreads) append_encode_kernel(const Params p)
     const uint32_t r = static_cast<uint32_t>(g % two_h);
     const uint32_t kv = r / p.H, h = r % p.H;
 
-    uint32_t bad = 0, f = 0, slot = 0;
+    // The token row does not depend on the descriptor: both loads go out together.
     const uint2 t = __ldg(p.targets + k);
+    const uint4 raw = __ldcs(p.tokens + g * kLanes + lane);
+    uint32_t bad = 0, f = 0, slot = 0;
     const uint32_t id = t.x, tok = t.y;
     if (id >= p.table_size) {
       bad = dev::kErrBlockIdRange;
@@ -114,7 +117,6 @@ __global__ void __launch_bounds__(kThreads) append_encode_kernel(const Params p)
       continue;
     }
 
-    const uint4 raw = __ldcs(p.tokens + g * kLanes + lane);
     const uint32_t row = (kv * p.T + tok) * p.H + h;
     uint8_t* payload = p.pool[f].base + uint64_t{slot} * p.pool[f].slot_bytes;
     if (f == dev::kFp16) {  // encode_fp16 of an FP16 value: itself, NaN canonicalized
@@ -150,12 +152,16 @@ __global__ void __launch_bounds__(kThreads) append_encode_kernel(const Params p)
         const float q = __fdiv_rn(amax, max_finite);
         scale = q < 1.17549435e-38f ? 1.17549435e-38f : q;  // std::max(q, FLT_MIN)
       }
-      uint32_t lo = 0, hi = 0;
+      float y[8];
 #pragma unroll
-      for (int i = 0; i < 8; ++i) {
-        const float y = __fdiv_rn(x[i], scale);
-        const uint32_t c = f == dev::kE4M3 ? dev::encode_e4m3(y) : dev::encode_e5m2(y);
-        if (i < 4) lo |= c << (8 * i); else hi |= c << (8 * (i - 4));
+      for (int i = 0; i < 8; ++i) y[i] = __fdiv_rn(x[i], scale);
+      uint32_t lo, hi;
+      if (f == dev::kE4M3) {
+        lo = dev::cvt_e4m3x2(y[0], y[1]) | dev::cvt_e4m3x2(y[2], y[3]) << 16;
+        hi = dev::cvt_e4m3x2(y[4], y[5]) | dev::cvt_e4m3x2(y[6], y[7]) << 16;
+      } else {
+        lo = dev::cvt_e5m2x2(y[0], y[1]) | dev::cvt_e5m2x2(y[2], y[3]) << 16;
+        hi = dev::cvt_e5m2x2(y[4], y[5]) | dev::cvt_e5m2x2(y[6], y[7]) << 16;
       }
       reinterpret_cast<uint2*>(payload + uint64_t{row} * kD)[lane] = make_uint2(lo, hi);
       if (lane == 0) reinterpret_cast<float*>(payload + p.code_bytes[f])[row] = scale;

@@ -243,6 +243,22 @@ __device__ __forceinline__ uint32_t encode_f16(float x) {
   return encode_minifloat<5, 10, 15, false, 0x7BFFu, 0x7E00u, 0x7C00u>(x);
 }
 
+// Two binary32 -> two FP8 codes (lo in bits 0..7, hi in bits 8..15), round to nearest
+// even, saturating to the largest finite code: the hardware conversion.  For every
+// finite binary32 input it equals encode_e4m3 / encode_e5m2 bit for bit (checked
+// exhaustively over all 2^32 patterns on sm_100a); NaN and Inf never reach it (the
+// encoders reject non-finite groups and x / scale stays finite).
+__device__ __forceinline__ uint32_t cvt_e4m3x2(float lo, float hi) {
+  unsigned short r;
+  asm("cvt.rn.satfinite.e4m3x2.f32 %0, %1, %2;" : "=h"(r) : "f"(hi), "f"(lo));
+  return r;
+}
+__device__ __forceinline__ uint32_t cvt_e5m2x2(float lo, float hi) {
+  unsigned short r;
+  asm("cvt.rn.satfinite.e5m2x2.f32 %0, %1, %2;" : "=h"(r) : "f"(hi), "f"(lo));
+  return r;
+}
+
 __device__ __forceinline__ bool finite_f32(float x) {
   return (__float_as_uint(x) & 0x7F800000u) != 0x7F800000u;
 }

@@ -4,6 +4,7 @@
 #include <cuda_runtime_api.h>
 
 #include <cstring>
+#include <unordered_map>
 
 #include "hlkv.h"
 
@@ -66,33 +67,76 @@ DeviceTables::~DeviceTables() {
   if (h_staging_ != nullptr) (void)cudaFreeHost(h_staging_);
 }
 
-DeviceStatus DeviceTables::reserve_staging(std::size_t bytes, cudaStream_t stream) {
-  if (bytes <= staging_bytes_) {
-    // The previous upload must have read the pinned buffer before it is rewritten.
-    if (staging_free_ != nullptr) return from_cuda(cudaEventSynchronize(staging_free_));
-    return {};
+DeviceStatus DeviceTables::stage(const alloc::ExecDelta& delta) {
+  DeviceGuard g(device_);
+  if (!g.ok()) return from_cuda(cudaErrorInvalidDevice);
+  const std::size_t n_desc = delta.descriptor_patches.size(), n_id = delta.id_patches.size();
+  const std::size_t bytes = 16 * n_desc + 8 * n_id;
+  // The last flush's upload and kernel (3) must be done with both staging buffers.
+  if (staging_free_ != nullptr) {
+    if (const cudaError_t e = cudaEventSynchronize(staging_free_); e != cudaSuccess) return from_cuda(e);
   }
-  std::size_t cap = staging_bytes_ == 0 ? std::size_t{64} << 10 : staging_bytes_;
-  while (cap < bytes) cap *= 2;
-  // The old buffers may still feed a queued upload / kernel.
-  if (const cudaError_t e = cudaStreamSynchronize(stream); e != cudaSuccess) return from_cuda(e);
-  if (d_staging_ != nullptr) (void)cudaFree(d_staging_);
-  if (h_staging_ != nullptr) (void)cudaFreeHost(h_staging_);
-  d_staging_ = nullptr;
-  h_staging_ = nullptr;
-  staging_bytes_ = 0;
-  if (const cudaError_t e = cudaMallocHost(&h_staging_, cap); e != cudaSuccess) return from_cuda(e);
-  if (const cudaError_t e = cudaMalloc(&d_staging_, cap); e != cudaSuccess) return from_cuda(e);
-  staging_bytes_ = cap;
+  if (bytes > staging_bytes_) {
+    std::size_t cap = staging_bytes_ == 0 ? std::size_t{64} << 10 : staging_bytes_;
+    while (cap < bytes) cap *= 2;
+    if (d_staging_ != nullptr) (void)cudaFree(d_staging_);
+    if (h_staging_ != nullptr) (void)cudaFreeHost(h_staging_);
+    d_staging_ = nullptr;
+    h_staging_ = nullptr;
+    staging_bytes_ = 0;
+    if (const cudaError_t e = cudaMallocHost(&h_staging_, cap); e != cudaSuccess) return from_cuda(e);
+    if (const cudaError_t e = cudaMalloc(&d_staging_, cap); e != cudaSuccess) return from_cuda(e);
+    staging_bytes_ = cap;
+  }
+  auto* h = static_cast<unsigned char*>(h_staging_);
+  if (n_desc > 0) std::memcpy(h, delta.descriptor_patches.data(), 16 * n_desc);
+  if (n_id > 0) std::memcpy(h + 16 * n_desc, delta.id_patches.data(), 8 * n_id);
   return {};
 }
 
 DeviceStatus DeviceTables::sync(alloc::HeteroBlockTable& table, cudaStream_t stream) {
-  table.collect_delta(delta_);
-  return apply(delta_, stream);
+  if (DeviceStatus s = collect(table); !s.ok()) return s;
+  return flush(stream);
+}
+
+DeviceStatus DeviceTables::collect(alloc::HeteroBlockTable& table) {
+  if (!pending_) {
+    table.collect_delta(delta_);
+  } else {
+    // A second collect before a flush: merge, later patches winning and one patch per
+    // target (kernel (3) applies each list in parallel).
+    table.collect_delta(scratch_);
+    delta_.descriptor_table_size = scratch_.descriptor_table_size;
+    delta_.arena_size = scratch_.arena_size;
+    auto merge = [](auto& into, const auto& later, auto key) {
+      std::unordered_map<std::uint32_t, std::size_t> at;
+      at.reserve(into.size() + later.size());
+      for (std::size_t i = 0; i < into.size(); ++i) at[key(into[i])] = i;
+      for (const auto& p : later) {
+        const auto [it, fresh] = at.try_emplace(key(p), into.size());
+        if (fresh) into.push_back(p); else into[it->second] = p;
+      }
+    };
+    merge(delta_.descriptor_patches, scratch_.descriptor_patches,
+          [](const alloc::BlockExecDescriptor& d) { return d.block_id; });
+    merge(delta_.id_patches, scratch_.id_patches, [](const alloc::IdPatch& d) { return d.offset; });
+  }
+  pending_ = true;
+  return stage(delta_);
+}
+
+DeviceStatus DeviceTables::flush(cudaStream_t stream) {
+  if (!pending_) return {};
+  pending_ = false;
+  return upload_and_apply(delta_, stream);
 }
 
 DeviceStatus DeviceTables::apply(const alloc::ExecDelta& delta, cudaStream_t stream) {
+  if (DeviceStatus s = stage(delta); !s.ok()) return s;
+  return upload_and_apply(delta, stream);
+}
+
+DeviceStatus DeviceTables::upload_and_apply(const alloc::ExecDelta& delta, cudaStream_t stream) {
   DeviceGuard g(device_);
   if (!g.ok()) return from_cuda(cudaErrorInvalidDevice);
   if (d_err_ == nullptr) {
@@ -151,15 +195,10 @@ DeviceStatus DeviceTables::apply(const alloc::ExecDelta& delta, cudaStream_t str
   const std::size_t n_desc = delta.descriptor_patches.size(), n_id = delta.id_patches.size();
   const std::size_t bytes = 16 * n_desc + 8 * n_id;
   if (bytes == 0) return {};
-  if (DeviceStatus s = reserve_staging(bytes, stream); !s.ok()) return s;
-  auto* h = static_cast<unsigned char*>(h_staging_);
-  if (n_desc > 0) std::memcpy(h, delta.descriptor_patches.data(), 16 * n_desc);
-  if (n_id > 0) std::memcpy(h + 16 * n_desc, delta.id_patches.data(), 8 * n_id);
   if (const cudaError_t e = cudaMemcpyAsync(d_staging_, h_staging_, bytes, cudaMemcpyHostToDevice, stream);
       e != cudaSuccess) {
     return from_cuda(e);
   }
-  if (const cudaError_t e = cudaEventRecord(staging_free_, stream); e != cudaSuccess) return from_cuda(e);
   auto* d = static_cast<unsigned char*>(d_staging_);
   const int st = hlkv_apply_delta(
       reinterpret_cast<HlkvExecDescriptor*>(d_table_), table_size_, d_arena_, arena_size_,
@@ -169,6 +208,8 @@ DeviceStatus DeviceTables::apply(const alloc::ExecDelta& delta, cudaStream_t str
   if (st != HLKV_OK) {
     return DeviceStatus{static_cast<QuantStatus>(st), static_cast<cudaError_t>(hlkv_last_cuda_error())};
   }
+  // Both staging buffers are free again once kernel (3) has run.
+  if (const cudaError_t e = cudaEventRecord(staging_free_, stream); e != cudaSuccess) return from_cuda(e);
   return {};
 }
 

@@ -177,6 +177,8 @@ SIGNATURES: list[tuple[str, object, list]] = [
     ("hlkv_device_tables_create", _int, [_P(_vp)]),
     ("hlkv_device_tables_destroy", None, [_vp]),
     ("hlkv_device_tables_sync", _int, [_vp, _vp, _vp]),
+    ("hlkv_device_tables_collect", _int, [_vp, _vp]),
+    ("hlkv_device_tables_flush", _int, [_vp, _vp]),
     ("hlkv_device_tables_table", _vp, [_vp]),
     ("hlkv_device_tables_table_size", _u32, [_vp]),
     ("hlkv_device_tables_arena", _vp, [_vp]),
@@ -440,6 +442,14 @@ class DeviceTables:
 
     def sync(self, table: Table, stream=None) -> None:
         check(lib().hlkv_device_tables_sync(self.h, table.h, _stream_handle(stream)), "device_tables_sync")
+
+    def collect(self, table: Table) -> None:
+        """Host half of sync(): takes the table's pending changes (no CUDA call)."""
+        check(lib().hlkv_device_tables_collect(self.h, table.h), "device_tables_collect")
+
+    def flush(self, stream=None) -> None:
+        """Device half of sync(): uploads and applies the collected changes on `stream`."""
+        check(lib().hlkv_device_tables_flush(self.h, _stream_handle(stream)), "device_tables_flush")
 
     @property
     def table_ptr(self) -> int: return lib().hlkv_device_tables_table(self.h) or 0

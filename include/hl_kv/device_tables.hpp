@@ -13,6 +13,8 @@
 //      allocated once at max_blocks entries;
 //   3. copy the patches into pinned staging and upload them;
 //   4. run kernel (3) (hlkv_apply_delta).
+// collect() is the host part (1 and the copy of 3) and flush() the queued part, so
+// host table work can run while the stream is busy.
 // Kernels issued later on the same stream see the updated tables.  One
 // DeviceTables per table and device, used from the table's first delta on;
 // not thread-safe (like the table).
@@ -35,8 +37,16 @@ class DeviceTables {
   DeviceTables(const DeviceTables&) = delete;
   DeviceTables& operator=(const DeviceTables&) = delete;
 
-  /// collect_delta() + upload + apply on `stream`.
+  /// collect_delta() + upload + apply on `stream`: collect() then flush().
   [[nodiscard]] DeviceStatus sync(alloc::HeteroBlockTable& table, cudaStream_t stream);
+  /// Host half of sync(): moves the table's pending changes into this object (merged
+  /// with changes collected earlier and not yet flushed, later patches winning) and
+  /// copies them into pinned staging.  Queues nothing; it waits only until the previous
+  /// flush's upload and kernel (3) are done with the staging buffers.
+  [[nodiscard]] DeviceStatus collect(alloc::HeteroBlockTable& table);
+  /// Device half of sync(): queues the upload and kernel (3) for what collect()
+  /// gathered, on `stream`.  A no-op when nothing is pending.
+  [[nodiscard]] DeviceStatus flush(cudaStream_t stream);
   /// Uploads and applies an already collected delta.
   [[nodiscard]] DeviceStatus apply(const alloc::ExecDelta& delta, cudaStream_t stream);
 
@@ -48,7 +58,8 @@ class DeviceTables {
   [[nodiscard]] std::uint32_t* error_word() const noexcept { return d_err_; }
 
  private:
-  [[nodiscard]] DeviceStatus reserve_staging(std::size_t bytes, cudaStream_t stream);
+  [[nodiscard]] DeviceStatus stage(const alloc::ExecDelta& delta);
+  [[nodiscard]] DeviceStatus upload_and_apply(const alloc::ExecDelta& delta, cudaStream_t stream);
 
   int device_ = 0;
   alloc::BlockExecDescriptor* d_table_ = nullptr;
@@ -60,8 +71,10 @@ class DeviceTables {
   void* h_staging_ = nullptr;   // pinned
   void* d_staging_ = nullptr;
   std::size_t staging_bytes_ = 0;
-  cudaEvent_t staging_free_ = nullptr;  // recorded after the upload that reads h_staging_
-  alloc::ExecDelta delta_;
+  cudaEvent_t staging_free_ = nullptr;  // recorded after kernel (3), the last reader of both buffers
+  alloc::ExecDelta delta_;    // collected, not yet flushed
+  alloc::ExecDelta scratch_;  // the next collect_delta() before merging into delta_
+  bool pending_ = false;
 };
 
 }  // namespace hl::kv

@@ -330,6 +330,14 @@ void hlkv_device_tables_destroy(hlkv_device_tables* dt);
  * Returns an HLKV_* device status.
  */
 int hlkv_device_tables_sync(hlkv_device_tables* dt, hlkv_table* t, hlkv_stream_t stream);
+/*
+ * The two halves of hlkv_device_tables_sync, so that host table work can run ahead of
+ * the stream: collect moves the table's pending changes into dt (merged with changes
+ * collected earlier, later patches winning) and into pinned staging, queueing nothing;
+ * flush queues their upload and kernel (3) on `stream`.  No counterpart in the reference.
+ */
+int hlkv_device_tables_collect(hlkv_device_tables* dt, hlkv_table* t);
+int hlkv_device_tables_flush(hlkv_device_tables* dt, hlkv_stream_t stream);
 const HlkvExecDescriptor* hlkv_device_tables_table(const hlkv_device_tables* dt);
 uint32_t hlkv_device_tables_table_size(const hlkv_device_tables* dt);
 const uint32_t* hlkv_device_tables_arena(const hlkv_device_tables* dt);

@@ -113,3 +113,32 @@ def test_large_delta_and_arena_growth(hlkv_lib, cuda_device):
         assert list(arena[off:off + ln]) == t.sequence_block_ids(s)[1]
     want = np.array([t.device_descriptor(i) for i in range(t.max_blocks())], np.uint32)
     assert np.array_equal(table, want)
+
+
+def test_collect_flush_split_merges_pending_changes(hlkv_lib, cuda_device):
+    """DeviceTables.collect (host) twice before one flush (device): the merged delta --
+    later patches winning, one patch per target -- leaves the device tables equal to the
+    host table, as one sync would."""
+    h = hlkv_lib
+    t = h.Table(64, [(1, 2048, 64), (3, 1088, 64)], block_tokens=4)
+    dt = h.DeviceTables()
+    rng = np.random.default_rng(9)
+    seqs = [t.create_sequence()[1] for _ in range(6)]
+    for rnd in range(30):
+        for _ in range(int(rng.integers(1, 4))):       # several collects per flush
+            st, tg, done = t.append_tokens(seqs, rng.choice([1, 3], size=len(seqs)).astype(np.uint32), 1)
+            assert st == 0 and done == len(seqs)
+            if rng.integers(4) == 0:
+                i = int(rng.integers(len(seqs)))
+                assert t.release_sequence(seqs[i]) == 0
+                seqs[i] = t.create_sequence()[1]
+            dt.collect(t)
+        dt.flush()
+        table, arena = _device_state(dt)
+        want = np.array([t.device_descriptor(i) for i in range(64)], np.uint32)
+        assert np.array_equal(table, want), rnd
+        st, segs = t.batch_segments(seqs)
+        for s, (off, ln) in zip(seqs, segs):
+            assert list(arena[off:off + ln]) == t.sequence_block_ids(s)[1], rnd
+    dt.flush()  # nothing pending: a no-op
+    assert d2h(dt.error_word_ptr, 4).view(np.uint32)[0] == 0
