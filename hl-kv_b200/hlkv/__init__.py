@@ -131,6 +131,7 @@ SIGNATURES: list[tuple[str, object, list]] = [
     ("hlkv_last_cuda_error", _int, []),
     ("hlkv_gather_dequant", _int, [_P(Pools), _P(Layout), _vp, _u32, _vp, _u32, _vp, _u32, _vp,
                                    _vp, _vp, _vp]),
+    ("hlkv_transcode", _int, [_P(Pools), _P(Layout), _vp, _u32, _vp, _vp]),
     ("hlkv_append_encode", _int, [_P(Pools), _P(Layout), _vp, _u32, _vp, _u32, _vp, _vp, _vp]),
     ("hlkv_apply_delta", _int, [_vp, _u32, _vp, _u32, _vp, _u32, _vp, _u32, _vp, _vp]),
     ("hlkv_dequantize_fp8_to_fp16", _int, [_int, _vp, _sz, _vp, _sz, _vp, _vp]),
@@ -494,6 +495,16 @@ def append_encode(pools: Pools, layout: Layout, table_ptr: int, table_size: int,
     st = lib().hlkv_append_encode(C.byref(pools), C.byref(layout), table_ptr or None, table_size,
                                   _ptr(targets), n, _ptr(tokens), _ptr(err), _stream_handle(stream))
     check(st, "hlkv_append_encode")
+    return st
+
+
+def transcode(pools: Pools, layout: Layout, jobs, err, stream=None) -> int:
+    """Format-change transcode.  jobs: device int32 [n, 8] = {from_format, from_slot,
+    to_format, to_slot, valid_tokens, 0, 0, 0} (16-byte aligned)."""
+    n = int(jobs.shape[0])
+    st = lib().hlkv_transcode(C.byref(pools), C.byref(layout), _ptr(jobs), n, _ptr(err),
+                              _stream_handle(stream))
+    check(st, "hlkv_transcode")
     return st
 
 

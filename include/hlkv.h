@@ -191,6 +191,30 @@ int hlkv_apply_delta(HlkvExecDescriptor* d_table, uint32_t table_size, uint32_t*
                      uint32_t n_desc, const HlkvIdPatch* d_id_patches, uint32_t n_id,
                      uint32_t* d_err, hlkv_stream_t stream);
 
+/* ---- format-change transcode ------------------------------------------------------------ */
+typedef struct {
+  uint32_t from_format; /* the block's current format and slot ...                  */
+  uint32_t from_slot;
+  uint32_t to_format;   /* ... and the target pool and slot (begin_format_change)     */
+  uint32_t to_slot;
+  uint32_t valid_tokens; /* rows of later tokens are encoded from zeros              */
+  uint32_t reserved[3];  /* 0 */
+} HlkvTranscodeJob;
+
+/*
+ * Device half of a format change (hetero_block_table.cpp:251-287; no kernel in the
+ * reference): for each job, re-encodes the block in (from_format, from_slot) into
+ * (to_format, to_slot) -- each row of a valid token decoded as kernel (1) decodes it
+ * (dequantize_reference_to_fp16) and encoded as kernel (2) encodes an appended row
+ * (quantize_reference on those binary16 values); rows of later tokens encoded from +0.
+ * Jobs come from hlkv_table_begin_format_change; commit the changes (and flush the
+ * delta) after this call on the same stream.  Source and destination slots must not
+ * overlap.  d_jobs 16-byte aligned.  Bad jobs and non-finite rows are skipped with
+ * their HLKV_ERR_* bits.
+ */
+int hlkv_transcode(const HlkvPools* pools, const HlkvLayout* layout, const HlkvTranscodeJob* d_jobs,
+                   uint32_t n, uint32_t* d_err, hlkv_stream_t stream);
+
 /* ---- flat codecs ------------------------------------------------------------------------ */
 /*
  * Drop-in for hl::quant::cuda::dequantize_fp8_to_fp16 (cuda_dequant.hpp:47-50,

@@ -557,6 +557,56 @@ ORC_API uint32_t orc_append_encode(const orc_pool* pools, uint32_t T, uint32_t H
   return err;
 }
 
+/* ---- format-change transcode (device half of hetero_block_table.cpp:251-287) ---------------- */
+/* Job k: {from_format, from_slot, to_format, to_slot, valid_tokens, 0, 0, 0}.  Each row of a
+ * valid token is decoded with dequantize_reference_to_fp16 (cpu_dequant.cpp:127-141) from the
+ * source slot and re-encoded with quantize_reference (cpu_quant.cpp:97-170) on the binary32
+ * values of those binary16 results into the destination slot; rows of later tokens are
+ * encoded from +0.  A rejected row leaves the destination row untouched (E_NONFINITE). */
+ORC_API uint32_t orc_transcode(const orc_pool* pools, uint32_t T, uint32_t H, uint32_t D,
+                               const uint32_t* jobs, uint32_t n) {
+  uint32_t err = 0;
+  float vals[4096];
+  uint16_t half[4096];
+  uint8_t codes[8192];
+  if (D > 4096) return E_LAYOUT;
+  const size_t rows = (size_t)2 * T * H;
+  for (uint32_t k = 0; k < n; ++k) {
+    const uint32_t* j = jobs + 8 * (size_t)k;
+    const uint32_t ff = j[0], fs = j[1], tf = j[2], ts = j[3], vt = j[4];
+    if (ff > 3 || tf > 3 || pools[ff].base == NULL || pools[tf].base == NULL) { err |= E_BAD_FORMAT; continue; }
+    if (fs >= pools[ff].num_slots || ts >= pools[tf].num_slots) { err |= E_SLOT_RANGE; continue; }
+    if (vt > T) { err |= E_VALID_TOKENS; continue; }
+    const uint8_t* src = pools[ff].base + (size_t)fs * pools[ff].slot_bytes;
+    uint8_t* dst = (uint8_t*)pools[tf].base + (size_t)ts * pools[tf].slot_bytes;
+    const size_t src_codes = fmt_packed_bytes((int)ff, rows * D);
+    const size_t dst_codes = fmt_packed_bytes((int)tf, rows * D);
+    for (size_t r = 0; r < rows; ++r) {
+      const uint32_t tok = (uint32_t)((r / H) % T);
+      if (tok < vt) {
+        float p[2] = {0.0f, 0.0f};
+        if (ff == F_E4M3 || ff == F_E5M2) memcpy(&p[0], src + src_codes + 4 * r, 4);
+        if (ff == F_INT4) memcpy(p, src + src_codes + 8 * r, 8);
+        const int st = orc_dequantize_to_fp16((int)ff, src + fmt_packed_bytes((int)ff, r * D),
+                                              fmt_packed_bytes((int)ff, D), D, p,
+                                              ff == F_FP16 ? 0 : 1, ff == F_FP16 ? 0 : D, half, D);
+        if (st != ORC_OK) { err |= E_NONFINITE; continue; }
+        for (uint32_t i = 0; i < D; ++i) vals[i] = mf_decode(half[i], &kSpecFp16);
+      } else {
+        for (uint32_t i = 0; i < D; ++i) vals[i] = 0.0f;
+      }
+      float p[2];
+      const int st = orc_quantize((int)tf, vals, D, tf == F_FP16 ? 0 : D, p, tf == F_FP16 ? 0 : 1,
+                                  codes, sizeof(codes));
+      if (st != ORC_OK) { err |= E_NONFINITE; continue; }
+      memcpy(dst + fmt_packed_bytes((int)tf, r * D), codes, fmt_packed_bytes((int)tf, D));
+      if (tf == F_E4M3 || tf == F_E5M2) memcpy(dst + dst_codes + 4 * r, &p[0], 4);
+      if (tf == F_INT4) memcpy(dst + dst_codes + 8 * r, p, 8);
+    }
+  }
+  return err;
+}
+
 ORC_API size_t orc_slot_bytes_needed(int f, uint32_t T, uint32_t H, uint32_t D) {
   const orc_geom g = {T, H, D, 1};
   return slot_need(f, &g);

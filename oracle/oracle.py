@@ -192,6 +192,9 @@ class Oracle(_Common):
         L.orc_append_encode.argtypes = [C.POINTER(Pool), C.c_uint32, C.c_uint32, C.c_uint32,
                                         C.c_uint32, u32p, C.c_uint32, u32p, C.c_uint32, u16p]
         L.orc_append_encode.restype = C.c_uint32
+        L.orc_transcode.argtypes = [C.POINTER(Pool), C.c_uint32, C.c_uint32, C.c_uint32, u32p,
+                                    C.c_uint32]
+        L.orc_transcode.restype = C.c_uint32
         L.orc_gaussian.argtypes = [C.c_uint64, C.c_float, f32p, C.c_size_t]
         L.orc_slot_bytes_needed.argtypes = [C.c_int, C.c_uint32, C.c_uint32, C.c_uint32]
         L.orc_slot_bytes_needed.restype = C.c_size_t
@@ -229,6 +232,16 @@ class Oracle(_Common):
         return self.lib.orc_append_encode(parr, T, H, D, layout_id, _p(table, u32p),
                                           table.size // 4, _p(tg, u32p) if tg.size else None,
                                           tg.size // 2, _p(tok, u16p) if tok.size else None)
+
+
+    def transcode(self, pools: dict, T: int, H: int, D: int, jobs: np.ndarray) -> int:
+        """jobs: uint32 [n, 8] = {from_format, from_slot, to_format, to_slot, valid_tokens,
+        0, 0, 0}; the pool arrays are modified in place.  Returns the error bits."""
+        for buf, _, _ in pools.values():
+            assert buf.flags.c_contiguous and buf.dtype == np.uint8
+        parr, keep = _pool_array(pools)
+        j = np.ascontiguousarray(jobs, dtype=np.uint32).reshape(-1)
+        return self.lib.orc_transcode(parr, T, H, D, _p(j, u32p) if j.size else None, j.size // 8)
 
 
 class Ref(_Common):

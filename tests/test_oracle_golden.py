@@ -322,3 +322,83 @@ def test_quantize_rows_oracle_equals_reference(oracle, ref):
     for r in (0, 3, 4, 500):
         st, p1, c1 = oracle.quantize(int(fm[r]), x[r], 128)
         assert st == 0 and np.array_equal(c1, res[0][1][r][:c1.size])
+
+
+def _ref_transcode(ref, pools, T, H, D, jobs):
+    """The transcode spelled out with the reference library's own calls: per row,
+    dequantize_reference_to_fp16 of the source row, then quantize_reference of its
+    binary32 values into the destination row (rows of later tokens from zeros)."""
+    rows = 2 * T * H
+    packed = lambda f, n: 2 * n if f == 0 else (n // 2 if f == 3 else n)
+    for ff, fs, tf, ts, vt in jobs[:, :5]:
+        src_buf, sb_s, _ = pools[int(ff)]
+        dst_buf, sb_d, _ = pools[int(tf)]
+        src = src_buf[int(fs) * sb_s:(int(fs) + 1) * sb_s]
+        dst = dst_buf[int(ts) * sb_d:(int(ts) + 1) * sb_d]
+        sc, dc = packed(int(ff), rows * D), packed(int(tf), rows * D)
+        for r in range(rows):
+            if (r // H) % T < vt:
+                codes = src[packed(int(ff), r * D):packed(int(ff), (r + 1) * D)]
+                if ff == 0:
+                    p = np.zeros((0, 2), np.float32)
+                elif ff == 3:
+                    p = src[sc + 8 * r:sc + 8 * r + 8].view(np.float32).reshape(1, 2)
+                else:
+                    p = np.array([[src[sc + 4 * r:sc + 4 * r + 4].view(np.float32)[0], 0]], np.float32)
+                st, h16 = ref.dequantize_to_fp16(int(ff), codes, D, p, 0 if ff == 0 else D)
+                assert st == 0
+                x = h16.view(np.float16).astype(np.float32)
+            else:
+                x = np.zeros(D, np.float32)
+            st, p2, c2 = ref.quantize(int(tf), x, 0 if tf == 0 else D)
+            if st != 0:
+                continue
+            dst[packed(int(tf), r * D):packed(int(tf), (r + 1) * D)] = c2
+            if tf == 3:
+                dst[dc + 8 * r:dc + 8 * r + 8] = p2.reshape(-1).view(np.uint8)
+            elif tf != 0:
+                dst[dc + 4 * r:dc + 4 * r + 4] = p2[0, :1].view(np.uint8)
+
+
+def test_transcode_oracle_matches_reference_calls(oracle, ref):
+    rng = np.random.default_rng(31)
+    T, H, D, n_slots = 4, 2, 64, 6
+    rows = 2 * T * H
+    pools = {}
+    for f in (0, 1, 2, 3):
+        sb = oracle.slot_bytes_needed(f, T, H, D)
+        sb = (sb + 15) // 16 * 16
+        buf = np.zeros(n_slots * sb, np.uint8)
+        for s in range(n_slots):   # valid encoded content
+            x = (rng.standard_normal((rows, D)) * rng.choice([1e-3, 1, 300])).astype(np.float16).astype(np.float32)
+            for r in range(rows):
+                st, p, c = oracle.quantize(f, x[r], 0 if f == 0 else D)
+                cb = {0: 2 * D, 1: D, 2: D, 3: D // 2}[f]
+                buf[s * sb + r * cb:s * sb + (r + 1) * cb] = c
+                code_total = {0: 2, 1: 1, 2: 1, 3: 0.5}[f] * rows * D
+                o = s * sb + int(code_total)
+                if f == 3:
+                    buf[o + 8 * r:o + 8 * r + 8] = p.reshape(-1).view(np.uint8)
+                elif f != 0:
+                    buf[o + 4 * r:o + 4 * r + 4] = p[0, :1].view(np.uint8)
+        pools[f] = (buf, sb, n_slots)
+    # an FP16 row with Inf: rejected when encoding to FP8/INT4, copied when to FP16
+    pools[0][0][2 * D * 3 + 5 * 2:2 * D * 3 + 6 * 2] = np.array([0x7C00], np.uint16).view(np.uint8)
+    jobs = []
+    slot = {f: 0 for f in range(4)}
+    for ff in range(4):
+        for tf in range(4):
+            if ff == tf:
+                continue
+            jobs.append([ff, slot[ff] % 3, tf, 3 + slot[tf] % 3, int(rng.integers(0, T + 1)), 0, 0, 0])
+            slot[ff] += 1
+            slot[tf] += 1
+    jobs[0][4] = T  # FP16 slot 0 with the Inf row, all rows valid
+    jobs = np.array(jobs, np.uint32)
+    a = {f: (b.copy(), sb, ns) for f, (b, sb, ns) in pools.items()}
+    b = {f: (b.copy(), sb, ns) for f, (b, sb, ns) in pools.items()}
+    err = oracle.transcode(a, T, H, D, jobs)
+    _ref_transcode(ref, b, T, H, D, jobs)
+    assert err == (1 << 9)
+    for f in range(4):
+        assert np.array_equal(a[f][0], b[f][0]), f
