@@ -28,7 +28,7 @@ def test_transcode_bit_exact_then_gather(hlkv_lib, oracle, cuda_device, T, H, D)
     from hlkv.workload import build_workload
     fm = [[0, 1, 3, 0, 2, 1], [3, 0, 1, 1, 3], [0, 0, 2]]
     vt = [[T, T, T, T, T, max(1, T // 2)], [T, T, T, T, 1], [T, T, 0]]
-    wl = build_workload(fm, T=T, H=H, D=D, seed=T * H + D, valid_tokens=vt, spare_slots=12)
+    wl = build_workload(fm, T=T, H=H, D=D, seed=T * H + D, valid_tokens=vt, spare_slots=16)
     ids = []
     for s in wl.seqs:
         ids += wl.table.sequence_block_ids(s)[1]
