@@ -66,9 +66,11 @@ WORKLOADS = {
     # Llama-3-70B-shaped long context sharded by sequence; 8 resident layers per GPU (the
     # 80-layer payload of 234 GB does not fit one GPU), one launch per layer per step.
     "llama70b": dict(nseq=16, blocks=8192, probs=(0.05, 0.10, 0.0, 0.85), layers=8,
-                     scaling="strong",
+                     scaling="strong", updates=1000,
                      name="Llama-3-70B long context: 16 seq x 131072 tok sharded by sequence, "
-                          "8 resident layers, 8 KV heads x 128, K+V; INT4 .85 / E4M3 .10 / FP16 .05"),
+                          "8 resident layers, 8 KV heads x 128, K+V; INT4 .85 / E4M3 .10 / FP16 .05; "
+                          "1000 random descriptor updates (valid_tokens changes and format "
+                          "changes transcoded on the device) before each sweep"),
     # Decode step: every (sequence, layer) stream appends one token, encoded into its tail
     # block (kernel 2), and the allocator's descriptor delta is applied on the device
     # (kernel 3).  Sequences sharded over the ranks.
@@ -233,7 +235,7 @@ def cpu_gather_sample(wl, nseq_sample: int, min_wall_s: float = 2.0, max_reps: i
                       f"{nbytes / 1e6:.1f} MB algorithmic) x {reps} passes, {wall:.2f} s wall"}
 
 
-def build_bench_workload(spec: dict, rank: int, world: int):
+def build_bench_workload(spec: dict, rank: int, world: int, spare_slots: int = 0):
     """This rank's cache: all spec["nseq"] sequences (weak scaling) or its contiguous
     share of them (strong scaling), for every layer; table sequences are layer-major."""
     from hlkv.workload import build_workload, mixed_formats, tiered_formats
@@ -247,7 +249,91 @@ def build_bench_workload(spec: dict, rank: int, world: int):
         else:
             rows += mixed_formats(n, spec["blocks"], probs=spec["probs"],
                                   seed=1000 + rank + 7919 * layer)
-    return build_workload(rows, seed=1000 + rank), n
+    return build_workload(rows, seed=1000 + rank, spare_slots=spare_slots), n
+
+
+class RandomUpdates:
+    """Seeded stream of descriptor updates applied before each sweep of a multi-layer
+    cache: half set_valid_tokens on a random unsealed block, half format changes to the
+    next tier (seal, begin_format_change, device transcode, commit), then one delta flush,
+    all queued on the stream ahead of the sweep's launches.  Keeps the sweep's algorithmic
+    bytes current (valid tokens and formats change them)."""
+
+    _NEXT = {0: 1, 1: 3, 3: 1}  # FP16 -> E4M3 -> INT4 -> E4M3
+
+    def __init__(self, wl, n: int, seed: int):
+        import numpy as np
+        import torch
+        from hlkv.workload import block_bytes
+        self.wl, self.n, self.block_bytes = wl, n, block_bytes
+        self.rng = np.random.default_rng(seed)
+        self.ids = np.concatenate([np.array(wl.table.sequence_block_ids(s)[1], np.uint32)
+                                   for s in wl.seqs])
+        m = wl.table.max_blocks()
+        self.sealed = np.zeros(m, bool)
+        self.fmt = np.zeros(m, np.uint8)
+        self.vt = np.zeros(m, np.uint32)
+        for bid in self.ids:
+            info = wl.table.device_descriptor(int(bid))[1]
+            self.fmt[bid], self.vt[bid] = info & 0xF, (info >> 10) & 0x3FF
+        self.sweep_bytes = wl.algorithmic_bytes
+        self.jobs_host = torch.empty((n, 8), dtype=torch.int32).pin_memory()
+        self.jobs_dev = torch.empty((n, 8), dtype=torch.int32, device="cuda")
+        self.jobs_np = self.jobs_host.numpy().view(np.uint32)
+        self.uploaded = torch.cuda.Event()
+        self.first = True
+        self.counts = {"valid_tokens": 0, "format_changes": 0}
+
+    def _bytes(self, f: int, vt: int) -> int:
+        w = self.wl
+        return self.block_bytes(f, w.T, w.H, w.D, vt)
+
+    def step(self, stream, err) -> int:
+        """Queues one batch of updates; returns the bytes it moves (patches, transcodes)."""
+        import hlkv
+        w, t, rng = self.wl, self.wl.table, self.rng
+        if not self.first:
+            self.uploaded.synchronize()  # the previous upload has read jobs_host
+        self.first = False
+        picks = rng.choice(self.ids.size, size=self.n, replace=False)
+        kinds = rng.integers(0, 2, size=self.n)
+        out_bytes = 2 * 2 * w.T * w.H * w.D + 20  # FP16 written + descriptor per block
+        nj, moved, changed = 0, 0, []
+        for i, kind in zip(picks, kinds):
+            bid = int(self.ids[i])
+            h = t.handle_of(bid)
+            f, vt = int(self.fmt[bid]), int(self.vt[bid])
+            if kind == 0 and not self.sealed[bid]:
+                nvt = int(rng.integers(1, w.T + 1))
+                assert t.set_valid_tokens(h, nvt) == 0
+                self.sweep_bytes += self._bytes(f, nvt) - self._bytes(f, vt)
+                self.vt[bid] = nvt
+                self.counts["valid_tokens"] += 1
+                moved += 32  # one descriptor patch read and written
+                continue
+            target = self._NEXT[f]
+            if not self.sealed[bid]:
+                assert t.seal(h) == 0
+                self.sealed[bid] = True
+            st, fc = t.begin_format_change(h, target)
+            assert st == 0, st
+            self.jobs_np[nj] = (fc[0], fc[1], fc[2], fc[3], vt, 0, 0, 0)
+            nj += 1
+            changed.append(h)
+            # source codes + params of the valid rows read, all destination rows written
+            moved += (self._bytes(f, vt) - out_bytes) + (self._bytes(target, w.T) - out_bytes) + 64
+            self.sweep_bytes += self._bytes(target, vt) - self._bytes(f, vt)
+            self.fmt[bid] = target
+        if nj:
+            self.jobs_dev[:nj].copy_(self.jobs_host[:nj], non_blocking=True)
+            self.uploaded.record(stream)
+            hlkv.transcode(w.hlkv_pools(), w.layout, self.jobs_dev[:nj], err, stream=stream)
+        for h in changed:
+            assert t.commit_format_change(h, 0, 0) == 0
+        self.counts["format_changes"] += nj
+        w.dt.collect(t)
+        w.dt.flush(stream)
+        return moved
 
 
 def run_hlkv(args) -> None:
@@ -264,7 +350,9 @@ def run_hlkv(args) -> None:
                                 device_id=torch.device("cuda", local))
     spec = WORKLOADS[args.workload]
     layers = spec.get("layers", 1)
-    wl, nseq_rank = build_bench_workload(spec, rank, world)
+    # Format changes take a slot in the target pool before the commit frees the old one.
+    spare = spec.get("updates", 0) * (args.steps + args.warmup + 1)
+    wl, nseq_rank = build_bench_workload(spec, rank, world, spare)
     pools = wl.hlkv_pools()
     # One launch per layer per step, all into one FP16 scratch buffer of a layer's size.
     layer_segs = [wl.segs[l * nseq_rank:(l + 1) * nseq_rank] for l in range(layers)]
@@ -274,7 +362,13 @@ def run_hlkv(args) -> None:
     err = torch.zeros(1, dtype=torch.int32, device="cuda")
     stream = torch.cuda.current_stream()
 
+    updates = RandomUpdates(wl, spec["updates"], 5000 + rank) if spec.get("updates") else None
+    moved = [0]  # algorithmic bytes of the steps run so far (updates change the sweep's bytes)
+
     def step():
+        if updates is not None:
+            moved[0] += updates.step(stream, err)
+        moved[0] += updates.sweep_bytes if updates is not None else wl.algorithmic_bytes
         for segs in layer_segs:
             hlkv.gather_dequant(pools, wl.layout, wl.dt.table_ptr, wl.dt.table_size,
                                 wl.dt.arena_ptr, wl.dt.arena_size, segs, out, err, stream=stream)
@@ -291,10 +385,9 @@ def run_hlkv(args) -> None:
     # Inputs + outputs smaller than a few L2 capacities would be served from L2 on the
     # next step: then a buffer of twice the L2 size is overwritten between steps and the
     # value is taken from the per-step events (the flush is not timed).
-    bytes_per_step = wl.algorithmic_bytes
     l2_bytes = torch.cuda.get_device_properties(torch.cuda.current_device()).L2_cache_size
     flush = None
-    if bytes_per_step < 4 * l2_bytes:
+    if wl.algorithmic_bytes < 4 * l2_bytes:
         flush = torch.empty(2 * l2_bytes, dtype=torch.uint8, device="cuda")
     ev = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True))
           for _ in range(args.steps)]
@@ -303,6 +396,7 @@ def run_hlkv(args) -> None:
     with ClockSampler(torch.cuda.current_device()) as clocks:
         barrier()
         torch.cuda.synchronize()
+        moved[0] = 0
         h0 = time.time()
         t_start.record(stream)
         for k in range(args.steps):
@@ -317,6 +411,7 @@ def run_hlkv(args) -> None:
         barrier()
     total_ms = t_start.elapsed_time(t_end)
     step_ms = [a.elapsed_time(b) for a, b in ev]
+    bytes_per_step = moved[0] / args.steps
     assert int(err.item()) == 0
     if flush is not None:  # the timed work is the launches, not the flushes between them
         total_ms = sum(step_ms)
@@ -357,7 +452,9 @@ def run_hlkv(args) -> None:
                        "blocks_per_format": {"fp16": wl.blocks_per_format[0],
                                              "e4m3": wl.blocks_per_format[1],
                                              "int4": wl.blocks_per_format[3]},
-                       "bytes_per_step_per_gpu": bytes_per_step,
+                       "bytes_per_step_per_gpu": round(bytes_per_step),
+                       "updates_per_step": spec.get("updates", 0),
+                       "updates_applied": updates.counts if updates is not None else None,
                        "l2": ("inputs+outputs (%.0f MB) exceed 4x the %.0f MB L2; no flush" % (
                            bytes_per_step / 1e6, l2_bytes / 1e6)) if flush is None else
                              ("L2 flushed between steps (%.0f MB overwritten); value from the "
