@@ -1,7 +1,7 @@
 """Benchmark of the heterogeneous KV gather-dequant path on B200.
 
     python bench.py [--gpus N] [--steps K] [--warmup W] [--impl hlkv|reference]
-                    [--workload mixed|homogeneous|fp16|e4m3|int4|llama8b|llama70b]
+                    [--workload mixed|mixed_updates|homogeneous|fp16|e4m3|int4|llama8b|llama70b|decode|decode_small]
 
 Default workload ("mixed", the headline configuration): one step = one
 hlkv_gather_dequant launch over a single-layer cache of 64 sequences x 2048
@@ -49,6 +49,12 @@ WORKLOADS = {
     "mixed": dict(nseq=64, blocks=128, probs=(0.25, 0.5, 0.0, 0.25), scaling="weak",
                   name="mixed-format single layer: 64 seq x 2048 tok, 16-tok blocks, 8 KV heads x 128, "
                        "K+V, FP16 .25 / E4M3 .5 / INT4 .25, N(0,1) + 4 outlier channels x20"),
+    # The headline cache with the allocator live: 1000 random descriptor updates (valid
+    # tokens, format changes transcoded on the device) applied before every gather.
+    "mixed_updates": dict(nseq=64, blocks=128, probs=(0.25, 0.5, 0.0, 0.25), scaling="weak",
+                          updates=1000,
+                          name="mixed-format single layer (as 'mixed') + 1000 random descriptor "
+                               "updates per step (valid tokens; format changes transcoded on the device)"),
     "homogeneous": dict(nseq=1, blocks=256, probs=(0.0, 1.0, 0.0, 0.0), scaling="weak",
                         name="homogeneous E4M3: 1 seq x 4096 tok, 16-tok blocks, 8 KV heads x 128, K+V"),
     # Single-format caches of the mixed workload's size: per-format throughput.
@@ -288,8 +294,9 @@ class RandomUpdates:
         w = self.wl
         return self.block_bytes(f, w.T, w.H, w.D, vt)
 
-    def step(self, stream, err) -> int:
-        """Queues one batch of updates; returns the bytes it moves (patches, transcodes)."""
+    def prepare(self) -> int:
+        """Host half: one batch of table updates (commits included) collected into the
+        device tables' staging; returns the bytes the batch moves on the device."""
         import hlkv
         w, t, rng = self.wl, self.wl.table, self.rng
         if not self.first:
@@ -324,16 +331,24 @@ class RandomUpdates:
             moved += (self._bytes(f, vt) - out_bytes) + (self._bytes(target, w.T) - out_bytes) + 64
             self.sweep_bytes += self._bytes(target, vt) - self._bytes(f, vt)
             self.fmt[bid] = target
+        # The commits only change host state; the device sees them through the delta,
+        # which launch() queues after the transcode.
+        for h in changed:
+            assert t.commit_format_change(h, 0, 0) == 0
+        self.counts["format_changes"] += nj
+        self.n_jobs = nj
+        w.dt.collect(t)
+        return moved
+
+    def launch(self, stream, err) -> None:
+        """Device half: job upload, transcode, delta upload and kernel (3), in stream order."""
+        import hlkv
+        w, nj = self.wl, self.n_jobs
         if nj:
             self.jobs_dev[:nj].copy_(self.jobs_host[:nj], non_blocking=True)
             self.uploaded.record(stream)
             hlkv.transcode(w.hlkv_pools(), w.layout, self.jobs_dev[:nj], err, stream=stream)
-        for h in changed:
-            assert t.commit_format_change(h, 0, 0) == 0
-        self.counts["format_changes"] += nj
-        w.dt.collect(t)
         w.dt.flush(stream)
-        return moved
 
 
 def run_hlkv(args) -> None:
@@ -364,10 +379,18 @@ def run_hlkv(args) -> None:
 
     updates = RandomUpdates(wl, spec["updates"], 5000 + rank) if spec.get("updates") else None
     moved = [0]  # algorithmic bytes of the steps run so far (updates change the sweep's bytes)
+    host_update_s = [0.0]
+
+    def prepare():
+        """Host work of a step (table updates), outside the device-timed window."""
+        if updates is not None:
+            t0 = time.perf_counter()
+            moved[0] += updates.prepare()
+            host_update_s[0] += time.perf_counter() - t0
 
     def step():
         if updates is not None:
-            moved[0] += updates.step(stream, err)
+            updates.launch(stream, err)
         moved[0] += updates.sweep_bytes if updates is not None else wl.algorithmic_bytes
         for segs in layer_segs:
             hlkv.gather_dequant(pools, wl.layout, wl.dt.table_ptr, wl.dt.table_size,
@@ -378,6 +401,7 @@ def run_hlkv(args) -> None:
             dist.barrier()
 
     for _ in range(args.warmup):
+        prepare()
         step()
     torch.cuda.synchronize()
     assert int(err.item()) == 0, f"error bits {int(err.item()):#x}"
@@ -397,11 +421,13 @@ def run_hlkv(args) -> None:
         barrier()
         torch.cuda.synchronize()
         moved[0] = 0
+        host_update_s[0] = 0.0
         h0 = time.time()
         t_start.record(stream)
         for k in range(args.steps):
             if flush is not None:
                 flush.fill_(k & 0xFF)
+            prepare()
             ev[k][0].record(stream)
             step()
             ev[k][1].record(stream)
@@ -413,7 +439,8 @@ def run_hlkv(args) -> None:
     step_ms = [a.elapsed_time(b) for a, b in ev]
     bytes_per_step = moved[0] / args.steps
     assert int(err.item()) == 0
-    if flush is not None:  # the timed work is the launches, not the flushes between them
+    if flush is not None or updates is not None:
+        # the timed work is the launches, not the flushes or the host table updates between them
         total_ms = sum(step_ms)
     total_ms, mean_step_ms = max_over_ranks([total_ms, statistics.mean(step_ms)], world, "cuda")
 
@@ -455,6 +482,8 @@ def run_hlkv(args) -> None:
                        "bytes_per_step_per_gpu": round(bytes_per_step),
                        "updates_per_step": spec.get("updates", 0),
                        "updates_applied": updates.counts if updates is not None else None,
+                       "host_update_ms_per_step": round(1e3 * host_update_s[0] / args.steps, 3)
+                       if updates is not None else None,
                        "l2": ("inputs+outputs (%.0f MB) exceed 4x the %.0f MB L2; no flush" % (
                            bytes_per_step / 1e6, l2_bytes / 1e6)) if flush is None else
                              ("L2 flushed between steps (%.0f MB overwritten); value from the "

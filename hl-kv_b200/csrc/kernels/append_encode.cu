@@ -37,7 +37,8 @@ struct Params {
   const uint2* targets;
   const uint4* tokens;
   uint32_t* err;
-  uint64_t rows_total;  // n * 2H
+  uint32_t rows_total;  // n * 2H < 2^31
+  FastDiv two_h;        // 2H
   uint32_t table_size, T, H, layout_id;
 };
 
@@ -47,17 +48,16 @@ __global__ void __launch_bounds__(kThreads) append_encode_kernel(const Params p)
   constexpr int kRowsPerIter = kThreads / kLanes;
   const uint32_t lane = threadIdx.x % kLanes;
   const uint32_t mask = dev::row_mask<kD>();
-  const uint32_t two_h = 2 * p.H;
-  for (uint64_t g = uint64_t{blockIdx.x} * kRowsPerIter + threadIdx.x / kLanes; g < p.rows_total;
-       g += uint64_t{gridDim.x} * kRowsPerIter) {
+  for (uint32_t g = blockIdx.x * kRowsPerIter + threadIdx.x / kLanes; g < p.rows_total;
+       g += gridDim.x * kRowsPerIter) {
     // Everything below is uniform over the lanes of row g.
-    const uint64_t k = g / two_h;
-    const uint32_t r = static_cast<uint32_t>(g % two_h);
-    const uint32_t kv = r / p.H, h = r % p.H;
+    const uint32_t k = p.two_h.div(g);
+    const uint32_t r = g - k * p.two_h.d;
+    const uint32_t kv = r >= p.H ? 1u : 0u, h = r - kv * p.H;
 
     // The token row does not depend on the descriptor: both loads go out together.
     const uint2 t = __ldg(p.targets + k);
-    const uint4 raw = __ldcs(p.tokens + g * kLanes + lane);
+    const uint4 raw = __ldcs(p.tokens + uint64_t{g} * kLanes + lane);
     uint32_t bad = 0, f = 0, slot = 0;
     const uint32_t id = t.x, tok = t.y;
     if (id >= p.table_size) {
@@ -118,7 +118,10 @@ extern "C" int hlkv_append_encode(const HlkvPools* pools, const HlkvLayout* layo
   p.targets = reinterpret_cast<const uint2*>(d_targets);
   p.tokens = reinterpret_cast<const uint4*>(d_tokens);
   p.err = d_err;
-  p.rows_total = uint64_t{n} * 2 * layout->kv_heads;
+  const uint64_t rows_total = uint64_t{n} * 2 * layout->kv_heads;
+  if (rows_total >= (uint64_t{1} << 31)) return HLKV_INVALID_ARGUMENT;
+  p.rows_total = static_cast<uint32_t>(rows_total);
+  p.two_h = FastDiv(2 * layout->kv_heads);
   p.table_size = table_size;
   p.T = layout->block_tokens;
   p.H = layout->kv_heads;

@@ -21,6 +21,25 @@ uint64_t layout_code_bytes(int format, uint64_t elems);
 /// A layout the kernels support (block_tokens 1..512, head_dim 64/128/256, ...).
 bool layout_ok(const HlkvLayout* l);
 
+// Division by a run-time constant d >= 1 through a multiply and a shift
+// (Granlund and Montgomery, "Division by invariant integers using multiplication",
+// 1994, theorem 4.2 with N = 31): with l = ceil(log2 d) and m = ceil(2^(31+l) / d),
+// floor(n / d) = floor(n * m / 2^(31+l)) for every 0 <= n < 2^31.
+struct FastDiv {
+  uint32_t d = 1, m = 0, s = 0;
+  FastDiv() = default;
+  explicit FastDiv(uint32_t divisor) : d(divisor) {
+    uint32_t l = 0;
+    while ((uint64_t{1} << l) < d) ++l;
+    if (d > 1) {
+      m = static_cast<uint32_t>(((uint64_t{1} << (31 + l)) + d - 1) / d);
+      s = l - 1;
+    }
+  }
+  // n < 2^31
+  __device__ __forceinline__ uint32_t div(uint32_t n) const { return d == 1 ? n : __umulhi(n, m) >> s; }
+};
+
 namespace dev {
 
 // Streaming (evict-first) global loads and stores: the payload is read once and

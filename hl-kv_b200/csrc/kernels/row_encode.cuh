@@ -61,6 +61,35 @@ __device__ __forceinline__ uint32_t row_mask() {
   return kLanes == 32 ? 0xFFFFFFFFu : ((1u << kLanes) - 1u) << ((threadIdx.x % 32) / kLanes * kLanes);
 }
 
+// ---- the exact quotient shortcut -----------------------------------------------------
+//
+// Both encoders round a quotient q = RN(v / s) once more: to an FP8 code (RNE,
+// saturating) or to an integer (rint).  With y = RN(1/s), the products v*y*(1 -+ e),
+// e = 2^-21, each rounded to binary32, lie at least 5 * 2^-24 * |v/s| below and above
+// v/s, while RN(v/s) lies within 2^-24 * |v/s| of it (v a binary16 value or a
+// difference of two, s > 0, no underflow or overflow for such inputs).  Both final
+// roundings are monotone, so when the two ends round to the same result, RN(v/s)
+// rounds to it too; otherwise (within a few units of a rounding boundary, about one
+// value in 2^17) the quotient is computed with an IEEE division.  The results equal
+// the division-based ones bit for bit.
+constexpr float kBracketLo = 1.0f - 0x1p-21f;
+constexpr float kBracketHi = 1.0f + 0x1p-21f;
+
+// Order-preserving 16-bit key of a binary16 pattern (two per word): -x < -y < -0 < +0 < y.
+__device__ __forceinline__ uint32_t f16x2_keys(uint32_t w) {
+  const uint32_t neg = (w >> 15) & 0x00010001u;
+  return w ^ (neg * 0x7FFFu) ^ 0x80008000u;
+}
+__device__ __forceinline__ float key_to_float(uint32_t k) {
+  const uint32_t h = (k & 0x8000u) ? (k & 0x7FFFu) : (~k & 0xFFFFu);
+  return __half2float(__ushort_as_half(static_cast<unsigned short>(h)));
+}
+
+// rint(v) for 0 <= v < 2^22 as an integer: the addition rounds to nearest even.
+__device__ __forceinline__ uint32_t rint_u(float v) {
+  return __float_as_uint(__fadd_rn(v, 12582912.0f)) - 0x4B400000u;
+}
+
 // Encodes one row (this lane's 8 binary16 values in `raw`) in format f into row `row` of
 // a slot laid out as codes then per-row parameters (`payload`, code region of
 // `code_bytes`).  Uniform over the row's lanes; returns 0 or kErrNonFinite.
@@ -72,66 +101,115 @@ __device__ __forceinline__ uint32_t encode_row(uint32_t f, uint4 raw, uint32_t l
     reinterpret_cast<uint4*>(payload + uint64_t{row} * kD * 2)[lane] = canon_f16x8(raw);
     return 0;
   }
+  const uint32_t w[4] = {raw.x, raw.y, raw.z, raw.w};
+  // Inf / NaN halves: exponent field all ones.
+  uint32_t special = 0;
+#pragma unroll
+  for (int i = 0; i < 4; ++i) special |= __vcmpeq2(w[i] & 0x7C007C00u, 0x7C007C00u);
+  if (lanes_any<kLanes>(mask, special != 0)) return kErrNonFinite;
   float x[8];
-  {
-    const uint32_t w[4] = {raw.x, raw.y, raw.z, raw.w};
 #pragma unroll
-    for (int i = 0; i < 4; ++i) {
-      x[2 * i] = __half2float(__ushort_as_half(static_cast<unsigned short>(w[i] & 0xFFFFu)));
-      x[2 * i + 1] = __half2float(__ushort_as_half(static_cast<unsigned short>(w[i] >> 16)));
-    }
+  for (int i = 0; i < 4; ++i) {
+    x[2 * i] = __half2float(__ushort_as_half(static_cast<unsigned short>(w[i] & 0xFFFFu)));
+    x[2 * i + 1] = __half2float(__ushort_as_half(static_cast<unsigned short>(w[i] >> 16)));
   }
-  bool nonfinite = false;
-#pragma unroll
-  for (int i = 0; i < 8; ++i) nonfinite |= !finite_f32(x[i]);
-  if (lanes_any<kLanes>(mask, nonfinite)) return kErrNonFinite;
 
   if (f == kE4M3 || f == kE5M2) {
-    float a = 0.0f;
+    // amax on the magnitude bits (finite values: unsigned order = magnitude order).
+    uint32_t m = __vmaxu2(__vmaxu2(w[0] & 0x7FFF7FFFu, w[1] & 0x7FFF7FFFu),
+                          __vmaxu2(w[2] & 0x7FFF7FFFu, w[3] & 0x7FFF7FFFu));
+    m = max(m & 0xFFFFu, m >> 16);
 #pragma unroll
-    for (int i = 0; i < 8; ++i) a = fmaxf(a, fabsf(x[i]));
-    const float amax = lanes_max<kLanes>(mask, a);
+    for (int o = kLanes / 2; o > 0; o >>= 1) m = max(m, __shfl_xor_sync(mask, m, o, kLanes));
+    const float amax = __half2float(__ushort_as_half(static_cast<unsigned short>(m)));
     const float max_finite = f == kE4M3 ? 448.0f : 57344.0f;
     float scale = 1.0f;
     if (amax > 0.0f) {
       const float q = __fdiv_rn(amax, max_finite);
       scale = q < 1.17549435e-38f ? 1.17549435e-38f : q;  // std::max(q, FLT_MIN)
     }
-    float y[8];
+    const float y = __frcp_rn(scale);
+    const float ylo = __fmul_rn(y, kBracketLo), yhi = __fmul_rn(y, kBracketHi);
+    uint32_t c[4];
+    bool exact = true;
 #pragma unroll
-    for (int i = 0; i < 8; ++i) y[i] = __fdiv_rn(x[i], scale);
-    uint32_t lo, hi;
-    if (f == kE4M3) {
-      lo = cvt_e4m3x2(y[0], y[1]) | cvt_e4m3x2(y[2], y[3]) << 16;
-      hi = cvt_e4m3x2(y[4], y[5]) | cvt_e4m3x2(y[6], y[7]) << 16;
-    } else {
-      lo = cvt_e5m2x2(y[0], y[1]) | cvt_e5m2x2(y[2], y[3]) << 16;
-      hi = cvt_e5m2x2(y[4], y[5]) | cvt_e5m2x2(y[6], y[7]) << 16;
+    for (int i = 0; i < 4; ++i) {
+      const float a0 = __fmul_rn(x[2 * i], ylo), a1 = __fmul_rn(x[2 * i + 1], ylo);
+      const float b0 = __fmul_rn(x[2 * i], yhi), b1 = __fmul_rn(x[2 * i + 1], yhi);
+      const uint32_t lo = f == kE4M3 ? cvt_e4m3x2(a0, a1) : cvt_e5m2x2(a0, a1);
+      const uint32_t hi = f == kE4M3 ? cvt_e4m3x2(b0, b1) : cvt_e5m2x2(b0, b1);
+      exact &= lo == hi;
+      c[i] = lo;
     }
-    reinterpret_cast<uint2*>(payload + uint64_t{row} * kD)[lane] = make_uint2(lo, hi);
+    if (!exact) {  // near an FP8 rounding boundary: the divisions themselves
+#pragma unroll
+      for (int i = 0; i < 4; ++i) {
+        const float q0 = __fdiv_rn(x[2 * i], scale), q1 = __fdiv_rn(x[2 * i + 1], scale);
+        c[i] = f == kE4M3 ? cvt_e4m3x2(q0, q1) : cvt_e5m2x2(q0, q1);
+      }
+    }
+    reinterpret_cast<uint2*>(payload + uint64_t{row} * kD)[lane] =
+        make_uint2(c[0] | c[1] << 16, c[2] | c[3] << 16);
     if (lane == 0) reinterpret_cast<float*>(payload + code_bytes)[row] = scale;
     return 0;
   }
-  float mn = x[0], mx = x[0];
-  uint32_t imn = lane * 8, imx = lane * 8;
+
+  // INT4: min and max through order-preserving keys; one shuffle per round carries both
+  // (the min key low, the complement of the max key high).
+  uint32_t kmin = 0xFFFFu, kmax = 0u;
 #pragma unroll
-  for (int i = 1; i < 8; ++i) {
-    if (x[i] < mn) { mn = x[i]; imn = lane * 8 + i; }
-    if (!(x[i] < mx)) { mx = x[i]; imx = lane * 8 + i; }
+  for (int i = 0; i < 4; ++i) {
+    const uint32_t k = f16x2_keys(w[i]);
+    kmin = min(kmin, min(k & 0xFFFFu, k >> 16));
+    kmax = max(kmax, max(k & 0xFFFFu, k >> 16));
   }
-  lanes_minmax<kLanes>(mask, mn, imn, mx, imx);
+  uint32_t both = kmin | (0xFFFFu - kmax) << 16;
+#pragma unroll
+  for (int o = kLanes / 2; o > 0; o >>= 1) both = __vminu2(both, __shfl_xor_sync(mask, both, o, kLanes));
+  kmin = both & 0xFFFFu;
+  kmax = 0xFFFFu - (both >> 16);
+  float mn, mx;
+  // -0 and +0 compare equal: std::minmax_element then returns the first minimum and the
+  // last maximum by index, which decides the sign of a zero bias.  Only a row whose
+  // minimum is -0 with values >= +0 present, or whose maximum is +0 with values <= -0
+  // present, can hold both; it takes the index-tracking reduction.
+  if ((kmin == 0x7FFFu && kmax >= 0x8000u) || (kmax == 0x8000u && kmin <= 0x7FFFu)) {
+    mn = x[0];
+    mx = x[0];
+    uint32_t imn = lane * 8, imx = lane * 8;
+#pragma unroll
+    for (int i = 1; i < 8; ++i) {
+      if (x[i] < mn) { mn = x[i]; imn = lane * 8 + i; }
+      if (!(x[i] < mx)) { mx = x[i]; imx = lane * 8 + i; }
+    }
+    lanes_minmax<kLanes>(mask, mn, imn, mx, imx);
+  } else {
+    mn = key_to_float(kmin);
+    mx = key_to_float(kmax);
+  }
   const float range = __fsub_rn(mx, mn);
   if (!finite_f32(range)) return kErrNonFinite;
   const float scale = __fdiv_rn(range, 15.0f);
   uint32_t word = 0;
+  if (scale > 0.0f) {
+    const float y = __frcp_rn(scale);
+    const float ylo = __fmul_rn(y, kBracketLo), yhi = __fmul_rn(y, kBracketHi);
+    bool exact = true;
 #pragma unroll
-  for (int i = 0; i < 8; ++i) {
-    uint32_t q = 0;
-    if (scale > 0.0f) {
-      const float rq = rintf(__fdiv_rn(__fsub_rn(x[i], mn), scale));
-      q = static_cast<uint32_t>(rq < 0.0f ? 0.0f : (15.0f < rq ? 15.0f : rq));
+    for (int i = 0; i < 8; ++i) {
+      const float d = __fsub_rn(x[i], mn);
+      const uint32_t qa = rint_u(__fmul_rn(d, ylo)), qb = rint_u(__fmul_rn(d, yhi));
+      exact &= qa == qb;
+      word |= min(qa, 15u) << (4 * i);
     }
-    word |= q << (4 * i);
+    if (!exact) {  // near a .5 boundary: the divisions themselves
+      word = 0;
+#pragma unroll
+      for (int i = 0; i < 8; ++i) {
+        const uint32_t q = rint_u(__fdiv_rn(__fsub_rn(x[i], mn), scale));
+        word |= min(q, 15u) << (4 * i);
+      }
+    }
   }
   reinterpret_cast<uint32_t*>(payload + uint64_t{row} * (kD / 2))[lane] = word;
   if (lane == 0) reinterpret_cast<float2*>(payload + code_bytes)[row] = make_float2(scale, mn);

@@ -42,8 +42,9 @@ struct Params {
   uint64_t code_bytes[4];
   const uint4* jobs;  // HlkvTranscodeJob: {from_format, from_slot, to_format, to_slot}, {valid_tokens, 0, 0, 0}
   uint32_t* err;
-  uint64_t rows_total;  // n * rows_per_block
+  uint32_t rows_total;  // n * rows_per_block < 2^31
   uint32_t rows_per_block, T, H;
+  FastDiv div_rows, div_h, div_t;
 };
 
 template <int kD>
@@ -52,13 +53,13 @@ __global__ void __launch_bounds__(kThreads) transcode_kernel(const Params p) {
   constexpr int kRowsPerIter = kThreads / kLanes;
   const uint32_t lane = threadIdx.x % kLanes;
   const uint32_t mask = dev::row_mask<kD>();
-  for (uint64_t g = uint64_t{blockIdx.x} * kRowsPerIter + threadIdx.x / kLanes; g < p.rows_total;
-       g += uint64_t{gridDim.x} * kRowsPerIter) {
+  for (uint32_t g = blockIdx.x * kRowsPerIter + threadIdx.x / kLanes; g < p.rows_total;
+       g += gridDim.x * kRowsPerIter) {
     // Uniform over the lanes of row g.
-    const uint64_t k = g / p.rows_per_block;
-    const uint32_t r = static_cast<uint32_t>(g % p.rows_per_block);
-    const uint4 j0 = __ldg(p.jobs + 2 * k);
-    const uint32_t vt = __ldg(p.jobs + 2 * k + 1).x;
+    const uint32_t k = p.div_rows.div(g);
+    const uint32_t r = g - k * p.rows_per_block;
+    const uint4 j0 = __ldg(p.jobs + 2 * uint64_t{k});
+    const uint32_t vt = __ldg(p.jobs + 2 * uint64_t{k} + 1).x;
     const uint32_t ff = j0.x, fs = j0.y, tf = j0.z, ts = j0.w;
     uint32_t bad = 0;
     if (ff > 3 || tf > 3 || p.pool[ff].base == nullptr || p.pool[tf].base == nullptr) {
@@ -72,7 +73,8 @@ __global__ void __launch_bounds__(kThreads) transcode_kernel(const Params p) {
       if (r == 0 && lane == 0) atomicOr(p.err, bad);  // once per job
       continue;
     }
-    const uint32_t tok = (r / p.H) % p.T;
+    const uint32_t rh = p.div_h.div(r);             // r / H
+    const uint32_t tok = rh - p.div_t.div(rh) * p.T;  // (r / H) % T
     const uint8_t* src = p.pool[ff].base + uint64_t{fs} * p.pool[ff].slot_bytes;
     uint4 raw = make_uint4(0u, 0u, 0u, 0u);
     if (tok < vt) {
@@ -127,7 +129,12 @@ extern "C" int hlkv_transcode(const HlkvPools* pools, const HlkvLayout* layout,
   }
   p.jobs = reinterpret_cast<const uint4*>(d_jobs);
   p.err = d_err;
-  p.rows_total = uint64_t{n} * p.rows_per_block;
+  const uint64_t rows_total = uint64_t{n} * p.rows_per_block;
+  if (rows_total >= (uint64_t{1} << 31)) return HLKV_INVALID_ARGUMENT;
+  p.rows_total = static_cast<uint32_t>(rows_total);
+  p.div_rows = FastDiv(p.rows_per_block);
+  p.div_h = FastDiv(layout->kv_heads);
+  p.div_t = FastDiv(layout->block_tokens);
   p.T = layout->block_tokens;
   p.H = layout->kv_heads;
   const cudaStream_t s = reinterpret_cast<cudaStream_t>(stream);

@@ -22,6 +22,14 @@ def _tokens(n: int, H: int, D: int, seed: int) -> np.ndarray:
     x[1, 1, 0] = np.float16(6e-8) * np.arange(D)  # subnormal ramp
     x[2, 0, 0, :4] = [65504, -65504, 1, -1]
     x[2, 1, 0] = np.linspace(-7, 7, D)
+    if n > 3:
+        # quotients exactly on rounding boundaries (the encoders' exact fallback path):
+        # INT4 min 0 / max 15 -> scale 1 and .5 ties; E4M3 amax 448 -> scale 1 and FP8
+        # midpoints (normal, subnormal, saturating); E5M2 amax 57344 likewise
+        x[3, 0, 0] = np.tile([0, 15, 0.5, 1.5, 7.5, 14.5, 3.5, 8.5], D // 8)
+        x[3, 1, 0] = np.tile([448, 1.0625, -3.25, 248, 464, 2.0 ** -10, -3 * 2.0 ** -10, 17], D // 8)
+        x[3, 1, 1] = np.tile([57344, 1.125, -2.25, 2.0 ** -17, 3 * 2.0 ** -17, 40960, -5, 0.5], D // 8)
+        x[3, 0, 1] = np.tile([-0.0, 0.0, 2.0, -0.0, 1.0, 0.0, 3.0, 0.5], D // 8)   # min -0 with +0 present
     return x
 
 
@@ -43,7 +51,7 @@ def _all_ids(wl):
     return ids
 
 
-@pytest.mark.parametrize("T,H,D", [(16, 8, 128), (4, 2, 64), (2, 2, 256)])
+@pytest.mark.parametrize("T,H,D", [(16, 8, 128), (4, 2, 64), (2, 2, 256), (5, 3, 64)])
 def test_append_encode_bit_exact(hlkv_lib, oracle, cuda_device, T, H, D):
     from hlkv.workload import build_workload
     fm = [[0, 1, 2, 3, 1, 3, 0], [3, 1, 2]]
