@@ -77,6 +77,11 @@ WORKLOADS = {
                           "8 resident layers, 8 KV heads x 128, K+V; INT4 .85 / E4M3 .10 / FP16 .05; "
                           "1000 random descriptor updates (valid_tokens changes and format "
                           "changes transcoded on the device) before each sweep"),
+    # Config 1's data as one contiguous E4M3 array (8,388,608 values, 128-value groups):
+    # the drop-in hlkv_dequantize_fp8_to_fp16 against the reference's own GPU kernel.
+    "flat_e4m3": dict(n=8_388_608, group=128, fmt=1, scaling="weak", flat=True,
+                      name="contiguous E4M3 -> FP16: 8,388,608 values (1 seq x 4096 tok x K+V x 8 "
+                           "heads x 128), scale per 128 values; drop-in vs the reference's kernel"),
     # Decode step: every (sequence, layer) stream appends one token, encoded into its tail
     # block (kernel 2), and the allocator's descriptor delta is applied on the device
     # (kernel 3).  Sequences sharded over the ranks.
@@ -698,6 +703,164 @@ def cpu_encode_sample(tokens, tail_fmt, H: int, D: int, n: int, min_wall_s: floa
                                     f"x {reps} passes, {wall:.2f} s wall"}
 
 
+def run_flat(args) -> None:
+    """The flat FP8 -> FP16 drop-in and the reference's own kernel, on one contiguous array."""
+    import numpy as np
+    import torch
+    import torch.distributed as dist
+    import hlkv
+
+    rank, world, local = dist_env()
+    torch.cuda.set_device(local)
+    if world > 1:
+        from datetime import timedelta
+        dist.init_process_group("nccl", timeout=timedelta(seconds=300),
+                                device_id=torch.device("cuda", local))
+    spec = WORKLOADS[args.workload]
+    n, group, fmt = spec["n"], spec["group"], spec["fmt"]
+    ng = -(-n // group)
+    gen = torch.Generator(device="cuda")
+    gen.manual_seed(7000 + rank)
+    x = torch.randn(n, generator=gen, device="cuda").to(torch.float16).to(torch.float32)
+    codes = torch.empty(n, dtype=torch.uint8, device="cuda")
+    params = torch.empty((ng, 2), dtype=torch.float32, device="cuda")
+    err = torch.zeros(1, dtype=torch.int32, device="cuda")
+    hlkv.check(hlkv.quantize(fmt, x.data_ptr(), n, group, params.data_ptr(), ng, codes.data_ptr(), n,
+                             err.data_ptr()), "quantize")
+    del x
+    out = torch.empty(n, dtype=torch.int16, device="cuda")
+    out_ref = torch.empty(n, dtype=torch.int16, device="cuda")
+    stream = torch.cuda.current_stream()
+    ref = None
+    try:
+        from oracle.oracle import RefCuda
+        ref = RefCuda()
+    except Exception:
+        ref = None
+
+    def ours():
+        hlkv.check(hlkv.dequantize_fp8_to_fp16(fmt, codes.data_ptr(), n, params.data_ptr(), group,
+                                                out.data_ptr(), stream=stream), "dequantize_fp8_to_fp16")
+
+    def theirs():
+        assert ref.dequantize_fp8_to_fp16(fmt, codes.data_ptr(), n, params.data_ptr(), group,
+                                          out_ref.data_ptr(), stream.cuda_stream) == 0
+
+    # codes + one scale per group read, FP16 written
+    nbytes = n + 4 * ng + 2 * n
+    l2_bytes = torch.cuda.get_device_properties(torch.cuda.current_device()).L2_cache_size
+    flush = torch.empty(2 * l2_bytes, dtype=torch.uint8, device="cuda")
+
+    def timed(fn):
+        for _ in range(args.warmup):
+            fn()
+        ev = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True))
+              for _ in range(args.steps)]
+        for k in range(args.steps):
+            flush.fill_(k & 0xFF)  # inputs and outputs fit in L2: evict them between launches
+            ev[k][0].record(stream)
+            fn()
+            ev[k][1].record(stream)
+        torch.cuda.synchronize()
+        return [a.elapsed_time(b) for a, b in ev]
+
+    with ClockSampler(torch.cuda.current_device()) as clocks:
+        if world > 1:
+            dist.barrier()
+        c0 = time.time()
+        ms = timed(ours)
+        c1 = time.time()
+    total_ms, mean_ms = max_over_ranks([sum(ms), statistics.mean(ms)], world, "cuda")
+    value = world * nbytes * args.steps / (total_ms / 1e3) / 1e9
+    peak, peak_kind = measured_peak_gbs()
+    achieved = nbytes / (mean_ms / 1e3) / 1e9
+    ref_line = None
+    if ref is not None:
+        rms = timed(theirs)
+        torch.cuda.synchronize()
+        a = out.cpu().numpy().view(np.uint16)
+        b = out_ref.cpu().numpy().view(np.uint16)
+        nan = ((a & 0x7C00) == 0x7C00) & ((a & 0x3FF) != 0)
+        same = bool(np.array_equal(a[~nan], b[~nan]))
+        rmean = statistics.mean(rms)
+        ref_line = {"kernel": "reference dequant_kernel.cu (fp8_to_fp16_vec8), built from its "
+                              "source for sm_100a", "value": round(nbytes / (rmean / 1e3) / 1e9, 2),
+                    "unit": "GB/s", "launch_ms": round(rmean, 5), "outputs_equal": same,
+                    "speedup_of_drop_in": round(rmean / mean_ms, 3)}
+
+    # End to end through the C ABI: codes and scales from pinned host memory, the kernel,
+    # the FP16 output back into pinned host memory.
+    e2e_steps = max(1, min(args.steps, args.e2e_steps))
+    h_codes = codes.cpu().pin_memory()
+    h_params = params.cpu().pin_memory()
+    h_out = torch.empty(n, dtype=torch.int16).pin_memory()
+    for k in range(e2e_steps + 1):
+        if k == 1:
+            torch.cuda.synchronize()
+            e0 = torch.cuda.Event(enable_timing=True)
+            e1 = torch.cuda.Event(enable_timing=True)
+            e0.record(stream)
+        codes.copy_(h_codes, non_blocking=True)
+        params.copy_(h_params, non_blocking=True)
+        ours()
+        h_out.copy_(out, non_blocking=True)
+    e1.record(stream)
+    torch.cuda.synchronize()
+    (e2e_ms,) = max_over_ranks([e0.elapsed_time(e1)], world, "cuda")
+
+    cpu = None
+    if world == 1 and not args.no_cpu_baseline:
+        cpu = cpu_flat_sample(h_codes.numpy(), h_params.numpy(), fmt, group)
+    if rank == 0:
+        print(json.dumps({
+            "metric": METRIC, "value": round(value, 2), "unit": "GB/s", "n_gpus": world,
+            "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(total_ms / args.steps, 5),
+            "higher_is_better": True, "scaling": "weak", "vs_baseline": None,
+            "dtype": "e4m3 in; fp16 out", "data": "synthetic (seeded N(0,1), quantized on the GPU)",
+            "config": {"workload": spec["name"], "bytes_per_step_per_gpu": nbytes,
+                       "l2": "L2 flushed between launches (%.0f MB overwritten); value from the "
+                             "per-launch events" % (2 * l2_bytes / 1e6),
+                       "parallelism": f"one array per GPU x{world}"},
+            "roofline": {"bound": "hbm", "achieved": round(achieved, 2), "peak": peak, "unit": "GB/s",
+                         "frac": round(achieved / peak, 4),
+                         "peak_source": f"{peak_kind} (MEASURED_PEAKS.json hbm_gbs)", "traffic": None,
+                         "kernel": "fp8_vec8 (hlkv_dequantize_fp8_to_fp16)", "launch_ms": round(mean_ms, 5)},
+            "reference_gpu_kernel": ref_line,
+            "e2e": {"value": round(world * nbytes * e2e_steps / (e2e_ms / 1e3) / 1e9, 2), "unit": "GB/s",
+                    "h2d_bytes_per_step": n + 8 * ng, "d2h_bytes_per_step": 2 * n,
+                    "path": "pinned host codes + params -> H2D -> hlkv_dequantize_fp8_to_fp16 -> D2H"},
+            "gpu_launches": args.steps,
+            "clocks": clocks.summary(c0, c1),
+            "cpu_baseline": cpu,
+        }), flush=True)
+    if world > 1:
+        dist.barrier()
+        dist.destroy_process_group()
+
+
+def cpu_flat_sample(codes, params, fmt: int, group: int, min_wall_s: float = 2.0):
+    """The reference's dequantize_reference_to_fp16 (oracle/_ref) on one thread, over the
+    first 1,048,576 values of the same array."""
+    import numpy as np
+    from oracle.oracle import Oracle, Ref, ref_available
+    kind = "reference" if ref_available() else "port"
+    impl = Ref() if kind == "reference" else Oracle()
+    m = min(codes.size, 1 << 20)
+    c = codes[:m].view(np.uint8)
+    p = params[: -(-m // group)].view(np.float32).reshape(-1, 2)
+    reps, t0 = 0, time.perf_counter()
+    while True:
+        st, _ = impl.dequantize_to_fp16(fmt, c, m, p, group)
+        reps += 1
+        wall = time.perf_counter() - t0
+        if wall >= min_wall_s or reps >= 50:
+            break
+    assert st == 0
+    nbytes = m + 4 * p.shape[0] + 2 * m
+    return {"value": round(nbytes * reps / wall / 1e9, 3), "unit": "GB/s", "cores": 1, "kind": kind,
+            "sample": f"{m} of {codes.size} values x {reps} passes, {wall:.2f} s wall"}
+
+
 def _sum_over_ranks(values, world: int):
     import torch
     import torch.distributed as dist
@@ -806,6 +969,9 @@ def run_reference(args) -> None:
     if spec.get("decode"):
         run_reference_decode(args, spec, kind, threads)
         return
+    if spec.get("flat"):
+        run_reference_flat(args, spec, kind, threads)
+        return
     # Size the per-step sample so that warm-up + steps stay within about two minutes.
     budget_s = 120.0 / max(1, args.steps + args.warmup)
     blocks, probs = _blocks_and_probs(spec)
@@ -829,6 +995,52 @@ def run_reference(args) -> None:
         "config": {"workload": spec["name"], "parallelism": f"{threads} host threads"},
         "cpu_baseline": {"value": round(value, 3), "unit": "GB/s", "cores": threads, "kind": kind,
                          "sample": sample},
+        "e2e": {"value": round(value, 3), "unit": "GB/s", "h2d_bytes_per_step": 0,
+                "d2h_bytes_per_step": 0},
+    }), flush=True)
+
+
+def run_reference_flat(args, spec: dict, kind: str, threads: int) -> None:
+    """The reference's CPU dequantize_reference_to_fp16 over the whole contiguous array, in
+    equal slices (whole parameter groups) on all host threads."""
+    import numpy as np
+    from concurrent.futures import ThreadPoolExecutor
+    from oracle.oracle import Oracle, Ref
+    impl = Ref() if kind == "reference" else Oracle()
+    n, group, fmt = spec["n"], spec["group"], spec["fmt"]
+    ng = -(-n // group)
+    rng = np.random.default_rng(7000)
+    x = rng.standard_normal(n).astype(np.float16).astype(np.float32)
+    st, params, codes = impl.quantize(fmt, x, group)
+    assert st == 0
+    per = -(-ng // threads) * group
+    slices = [(lo, min(n, lo + per)) for lo in range(0, n, per)]
+
+    def one(sl):
+        lo, hi = sl
+        st, _ = impl.dequantize_to_fp16(fmt, codes[lo:hi], hi - lo, params[lo // group:-(-hi // group)], group)
+        return st
+
+    with ThreadPoolExecutor(max_workers=threads) as ex:
+        for _ in range(args.warmup):
+            assert all(s == 0 for s in ex.map(one, slices))
+        times = []
+        for _ in range(args.steps):
+            t0 = time.perf_counter()
+            assert all(s == 0 for s in ex.map(one, slices))
+            times.append(time.perf_counter() - t0)
+    nbytes = n + 4 * ng + 2 * n
+    total = sum(times)
+    value = nbytes * args.steps / total / 1e9
+    print(json.dumps({
+        "impl": "reference", "metric": METRIC, "value": round(value, 3), "unit": "GB/s",
+        "n_gpus": int(os.environ.get("WORLD_SIZE", "1")), "steps": args.steps, "warmup": args.warmup,
+        "ms_per_step": round(1e3 * total / args.steps, 3), "higher_is_better": True,
+        "scaling": "weak", "vs_baseline": None, "dtype": "e4m3 in; fp16 out",
+        "data": "synthetic (seeded N(0,1), quantize_reference)",
+        "config": {"workload": spec["name"], "parallelism": f"{threads} host threads"},
+        "cpu_baseline": {"value": round(value, 3), "unit": "GB/s", "cores": threads, "kind": kind,
+                         "sample": f"the whole array ({n} values) per step"},
         "e2e": {"value": round(value, 3), "unit": "GB/s", "h2d_bytes_per_step": 0,
                 "d2h_bytes_per_step": 0},
     }), flush=True)
@@ -886,6 +1098,9 @@ def main() -> None:
     args.warmup = max(args.warmup, 3)
     if args.impl == "hlkv" and WORKLOADS[args.workload].get("decode"):
         run_decode(args)
+        return
+    if args.impl == "hlkv" and WORKLOADS[args.workload].get("flat"):
+        run_flat(args)
         return
     if args.impl == "reference":
         run_reference(args)

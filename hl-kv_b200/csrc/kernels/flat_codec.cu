@@ -42,22 +42,55 @@ __device__ __forceinline__ bool params_ok(uint32_t f, float2 sb) {
 
 // 8 elements per thread; requires aligned pointers and chunks inside one group
 // (cpg = 8-element chunks per group, or all-ones for a single group).
+// kVecUnroll chunks per thread per pass: every load of a pass is issued before the
+// first conversion, so each thread keeps kVecUnroll code loads (and their scale loads)
+// in flight; a short array then occupies the whole GPU in a single pass.
+constexpr uint32_t kVecUnroll = 4;
+
 template <uint32_t kF, typename Index, bool kCheck>
 __global__ void __launch_bounds__(kThreads)
     dequant_vec8(const uint8_t* __restrict__ in, const float2* __restrict__ params, Index cpg,
                  uint64_t nchunks, uint4* __restrict__ out, uint32_t* err) {
-  const uint64_t stride = uint64_t{gridDim.x} * kThreads;
+  constexpr uint64_t kPass = uint64_t{kThreads} * kVecUnroll;
   uint32_t bad = 0;
-  for (uint64_t c = uint64_t{blockIdx.x} * kThreads + threadIdx.x; c < nchunks; c += stride) {
-    if constexpr (kF == dev::kFp16) {
-      out[c] = dev::canon_f16x8(reinterpret_cast<const uint4*>(in)[c]);
-    } else {
-      const float2 sb = __ldg(params + static_cast<Index>(c) / cpg);
-      if (kCheck && !params_ok(kF, sb)) { bad = dev::kErrNonFinite; continue; }
-      if constexpr (kF == dev::kInt4) {
-        out[c] = dev::int4x8_to_f16(reinterpret_cast<const uint32_t*>(in)[c], sb.x, sb.y);
+  for (uint64_t base = uint64_t{blockIdx.x} * kPass; base < nchunks; base += uint64_t{gridDim.x} * kPass) {
+    uint4 raw[kVecUnroll];
+    float2 sb[kVecUnroll];
+#pragma unroll
+    for (uint32_t j = 0; j < kVecUnroll; ++j) {
+      const uint64_t c = base + j * kThreads + threadIdx.x;
+      raw[j] = make_uint4(0u, 0u, 0u, 0u);
+      sb[j] = make_float2(0.0f, 0.0f);
+      if (c < nchunks) {
+        if constexpr (kF == dev::kFp16) {
+          raw[j] = dev::ld_stream(reinterpret_cast<const uint4*>(in) + c);
+        } else if constexpr (kF == dev::kInt4) {
+          raw[j].x = dev::ld_stream(reinterpret_cast<const uint32_t*>(in) + c);
+          sb[j] = __ldg(params + static_cast<Index>(c) / cpg);
+        } else {
+          const uint2 v = dev::ld_stream(reinterpret_cast<const uint2*>(in) + c);
+          raw[j].x = v.x;
+          raw[j].y = v.y;
+          sb[j] = __ldg(params + static_cast<Index>(c) / cpg);
+        }
+      }
+    }
+#pragma unroll
+    for (uint32_t j = 0; j < kVecUnroll; ++j) {
+      const uint64_t c = base + j * kThreads + threadIdx.x;
+      if (c >= nchunks) continue;
+      if constexpr (kF == dev::kFp16) {
+        out[c] = dev::canon_f16x8(raw[j]);
       } else {
-        out[c] = dev::fp8x8_to_f16<kF>(reinterpret_cast<const uint2*>(in)[c], sb.x);
+        if (kCheck && !params_ok(kF, sb[j])) {
+          bad = dev::kErrNonFinite;
+          continue;
+        }
+        if constexpr (kF == dev::kInt4) {
+          out[c] = dev::int4x8_to_f16(raw[j].x, sb[j].x, sb[j].y);
+        } else {
+          out[c] = dev::fp8x8_to_f16<kF>(make_uint2(raw[j].x, raw[j].y), sb[j].x);
+        }
       }
     }
   }
@@ -98,7 +131,7 @@ void launch_dequant(const uint8_t* in, uint64_t n, const float2* params, uint64_
   if (aligned && n >= 8 && (single || group % 8 == 0)) {
     const uint64_t nchunks = n / 8;
     const Index cpg = single ? static_cast<Index>(~Index{0}) : static_cast<Index>(group / 8);
-    dequant_vec8<kF, Index, kCheck><<<grid_for(nchunks, kThreads), kThreads, 0, s>>>(
+    dequant_vec8<kF, Index, kCheck><<<grid_for(nchunks, uint64_t{kThreads} * kVecUnroll), kThreads, 0, s>>>(
         in, params, cpg, nchunks, reinterpret_cast<uint4*>(out), err);
     done = nchunks * 8;
   }

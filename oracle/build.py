@@ -3,6 +3,9 @@
     python oracle/build.py            # both, when the reference tree is present
 
 * ``oracle/_build/liboracle.so`` -- the C restatement in ``hlkv_oracle.c``.
+* ``oracle/_ref/libhlkv_ref_cuda.so`` -- the reference's own GPU kernel
+  (project2_quant/src/dequant_kernel.cu, flat FP8 -> FP16) compiled for sm_100a
+  with ``ref_cuda_shim.cu``: the GPU comparison point for this library's drop-in.
 * ``oracle/_ref/libhlkv_ref.so`` -- the reference's own CPU library compiled
   straight from its sources (hl_quant: cpu_quant.cpp, cpu_dequant.cpp,
   quant_types.cpp; hl_allocator: hetero_block_table.cpp, id_arena.cpp,
@@ -26,6 +29,10 @@ BUILD_DIR = os.path.join(HERE, "_build")
 REF_DIR = os.path.join(HERE, "_ref")
 ORACLE_SO = os.path.join(BUILD_DIR, "liboracle.so")
 REF_SO = os.path.join(REF_DIR, "libhlkv_ref.so")
+REF_CUDA_SO = os.path.join(REF_DIR, "libhlkv_ref_cuda.so")
+NVCC = os.environ.get("NVCC", "/usr/local/cuda/bin/nvcc")
+# The reference's one GPU kernel (flat FP8 -> FP16) and what it links against.
+REF_CUDA_SOURCES = ["project2_quant/src/dequant_kernel.cu", "project2_quant/src/quant_types.cpp"]
 
 REF_SOURCES = [
     "project2_quant/src/cpu_quant.cpp",
@@ -82,9 +89,29 @@ def build_ref(force: bool = False) -> str | None:
     return REF_SO
 
 
+def build_ref_cuda(force: bool = False) -> str | None:
+    """Compiles the reference's FP8 -> FP16 kernel (its own source, sm_100a only, no
+    fast-math) with oracle/ref_cuda_shim.cu into oracle/_ref; None without the tree."""
+    srcs = [os.path.join(REF_ROOT, s) for s in REF_CUDA_SOURCES]
+    if not all(os.path.exists(s) for s in srcs):
+        return REF_CUDA_SO if os.path.exists(REF_CUDA_SO) else None
+    shim = os.path.join(HERE, "ref_cuda_shim.cu")
+    if force or _stale(REF_CUDA_SO, srcs + [shim, __file__]):
+        os.makedirs(REF_DIR, exist_ok=True)
+        tmp = REF_CUDA_SO + f".tmp{os.getpid()}"
+        _run([NVCC, "-std=c++20", "-O3", "-shared", "-Xcompiler", "-fPIC",
+              "-gencode", "arch=compute_100a,code=sm_100a",
+              "-I", os.path.join(REF_ROOT, "project2_quant/include"),
+              "-I", os.path.join(REF_ROOT, "project2_quant/src"),
+              "-o", tmp, *srcs, shim])
+        os.replace(tmp, REF_CUDA_SO)
+    return REF_CUDA_SO
+
+
 def build_all(force: bool = False) -> None:
     build_oracle(force)
     build_ref(force)
+    build_ref_cuda(force)
 
 
 if __name__ == "__main__":

@@ -269,3 +269,31 @@ def table_trace(lib: C.CDLL, seed: int, steps: int, max_blocks: int = 96,
 
 def ref_available() -> bool:
     return os.path.exists(_build.REF_SO) or _build.reference_available()
+
+
+class RefCuda:
+    """The reference's own GPU kernel hl::quant::cuda::dequantize_fp8_to_fp16, compiled
+    from its sources for sm_100a (oracle/_ref/libhlkv_ref_cuda.so)."""
+
+    def __init__(self, path: str | None = None):
+        path = path or _build.build_ref_cuda()
+        if path is None or not os.path.exists(path):
+            raise FileNotFoundError("oracle/_ref/libhlkv_ref_cuda.so is not built")
+        self.lib = C.CDLL(path)
+        f = self.lib.ref_cuda_dequantize_fp8_to_fp16
+        f.argtypes = [C.c_int, C.c_void_p, C.c_size_t, C.c_void_p, C.c_size_t, C.c_void_p,
+                      C.c_void_p, C.POINTER(C.c_int)]
+        f.restype = C.c_int
+
+    def dequantize_fp8_to_fp16(self, fmt: int, d_in: int, n: int, d_params: int, group: int,
+                               d_out: int, stream: int | None = None) -> int:
+        e = C.c_int(0)
+        st = self.lib.ref_cuda_dequantize_fp8_to_fp16(fmt, d_in, n, d_params, group, d_out, stream,
+                                                      C.byref(e))
+        self.last_cuda_error = e.value
+        return st
+
+
+def ref_cuda_available() -> bool:
+    p = _build.REF_CUDA_SO
+    return os.path.exists(p) or _build.build_ref_cuda() is not None

@@ -6,6 +6,8 @@ import os
 import numpy as np
 import pytest
 
+from helpers import fp16_nan
+
 pytestmark = pytest.mark.gpu
 GOLDEN = os.path.join(os.path.dirname(os.path.abspath(__file__)), "golden", "golden.npz")
 
@@ -182,3 +184,48 @@ def test_device_dequantize_every_format_and_bad_params(hlkv_lib, oracle, cuda_de
         else:
             st, want = oracle.dequantize_to_fp16(fmt, packed, n, params[:max(ng, 0)] if ng else np.zeros((0, 2), np.float32), gs)
             assert st == 0 and int(err.item()) == 0 and np.array_equal(got, want)
+
+
+@pytest.fixture(scope="module")
+def ref_cuda():
+    from oracle.oracle import RefCuda, ref_cuda_available
+    if not ref_cuda_available():
+        pytest.skip("the reference's GPU kernel is not built (no reference tree)")
+    return RefCuda()
+
+
+def test_fp8_drop_in_equals_reference_gpu_kernel(hlkv_lib, ref_cuda, cuda_device):
+    """The drop-in against the reference's own kernel (dequant_kernel.cu, compiled for
+    sm_100a from its source): bit-identical outputs over every code, the kScales set, random
+    group sizes and both kernels' vector and per-element paths (aligned and not)."""
+    import torch
+    rng = np.random.default_rng(41)
+    cases = [(fmt, 256, 256, 0, 0) for fmt in (1, 2)]
+    cases += [(int(rng.choice([1, 2])), int(n), int(g), int(a), int(b))
+              for n, g, a, b in [(4096, 128, 0, 0), (4099, 24, 3, 1), (65543, 8, 0, 0),
+                                 (1 << 20, 128, 0, 0), (1000, 1000, 5, 3), (77, 7, 1, 0)]]
+    for fmt, n, g, in_off, out_off in cases:
+        codes = np.arange(256, dtype=np.uint8) if n == 256 else rng.integers(0, 256, n, dtype=np.uint8)
+        ng = -(-n // g)
+        scales = (rng.choice([-1.0, 1.0], ng) * np.ldexp(1 + rng.integers(0, 1024, ng) / 1024.0,
+                                                          rng.integers(-30, 20, ng))).astype(np.float32)
+        params = np.stack([scales, np.zeros(ng, np.float32)], 1)
+        keep_in, din = _dev(codes, in_off)
+        keep_p, dp = _dev(params)
+        outs = []
+        for impl in ("ours", "ref"):
+            out = torch.full((n + out_off + 8,), 0x3333, dtype=torch.int32, device="cuda").to(torch.int16)
+            d_out = out.data_ptr() + 2 * out_off
+            if impl == "ours":
+                st = hlkv_lib.dequantize_fp8_to_fp16(fmt, din, n, dp, g, d_out)
+            else:
+                st = ref_cuda.dequantize_fp8_to_fp16(fmt, din, n, dp, g, d_out)
+            torch.cuda.synchronize()
+            assert st == 0, (impl, st)
+            outs.append(out.cpu().numpy().view(np.uint16)[out_off:out_off + n])
+        # NaN codes: both give a NaN (the reference test compares NaN by class,
+        # test_dequant_cuda.cpp:81-86); every other output bit for bit.
+        nan0, nan1 = fp16_nan(outs[0]), fp16_nan(outs[1])
+        assert np.array_equal(nan0, nan1), (fmt, n, g)
+        bad = np.nonzero((outs[0] != outs[1]) & ~nan0)[0]
+        assert bad.size == 0, (fmt, n, g, in_off, out_off, bad[:4], outs[0][bad[:4]], outs[1][bad[:4]])
