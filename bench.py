@@ -77,6 +77,12 @@ WORKLOADS = {
                           "8 resident layers, 8 KV heads x 128, K+V; INT4 .85 / E4M3 .10 / FP16 .05; "
                           "1000 random descriptor updates (valid_tokens changes and format "
                           "changes transcoded on the device) before each sweep"),
+    # Decode attention straight from the quantized blocks of the mixed cache: 32 query
+    # heads over the 8 KV heads (Llama-3-8B's GQA group of 4), one query per sequence.
+    "attn_mixed": dict(nseq=64, blocks=128, probs=(0.25, 0.5, 0.0, 0.25), scaling="weak",
+                       attn=True, q_heads=32,
+                       name="decode attention fused with dequant over the mixed cache: 64 seq x 2048 "
+                            "tok, 8 KV heads x 128, 32 query heads, FP16 .25 / E4M3 .5 / INT4 .25"),
     # Config 1's data as one contiguous E4M3 array (8,388,608 values, 128-value groups):
     # the drop-in hlkv_dequantize_fp8_to_fp16 against the reference's own GPU kernel.
     "flat_e4m3": dict(n=8_388_608, group=128, fmt=1, scaling="weak", flat=True,
@@ -703,6 +709,94 @@ def cpu_encode_sample(tokens, tail_fmt, H: int, D: int, n: int, min_wall_s: floa
                                     f"x {reps} passes, {wall:.2f} s wall"}
 
 
+def run_attention(args) -> None:
+    """hlkv_decode_attention over a whole cache per step (one launch)."""
+    import numpy as np
+    import torch
+    import torch.distributed as dist
+    import hlkv
+    from hlkv.workload import code_bytes, param_bytes
+
+    rank, world, local = dist_env()
+    torch.cuda.set_device(local)
+    if world > 1:
+        from datetime import timedelta
+        dist.init_process_group("nccl", timeout=timedelta(seconds=300),
+                                device_id=torch.device("cuda", local))
+    spec = WORKLOADS[args.workload]
+    wl, nseq = build_bench_workload(spec, rank, world)
+    qh, D = spec["q_heads"], wl.D
+    gen = torch.Generator(device="cuda")
+    gen.manual_seed(9000 + rank)
+    q = torch.randn((nseq, qh, D), generator=gen, device="cuda").to(torch.float16)
+    out = torch.empty((nseq, qh, D), dtype=torch.float16, device="cuda")
+    err = torch.zeros(1, dtype=torch.int32, device="cuda")
+    pools = wl.hlkv_pools()
+    stream = torch.cuda.current_stream()
+    scale = 1.0 / float(np.sqrt(D))
+
+    def step():
+        hlkv.decode_attention(pools, wl.layout, wl.dt.table_ptr, wl.dt.table_size, wl.dt.arena_ptr,
+                              wl.dt.arena_size, wl.segs, q, qh, scale, out, err, stream=stream)
+
+    # Algorithmic bytes: codes + row parameters of the K and V rows read, 20 B of descriptor
+    # and arena entry per block, the queries read and the outputs written.
+    rows, elems = 2 * wl.T * wl.H, wl.block_elems
+    per_fmt = {f: code_bytes(f, elems) + param_bytes(f, rows) + 20 for f in (0, 1, 2, 3)}
+    nbytes = sum(per_fmt[f] * n for f, n in wl.blocks_per_format.items()) + 2 * 2 * nseq * qh * D
+    l2_bytes = torch.cuda.get_device_properties(torch.cuda.current_device()).L2_cache_size
+    flush = torch.empty(2 * l2_bytes, dtype=torch.uint8, device="cuda") if nbytes < 4 * l2_bytes else None
+    for _ in range(args.warmup):
+        step()
+    torch.cuda.synchronize()
+    assert int(err.item()) == 0
+    ev = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True))
+          for _ in range(args.steps)]
+    with ClockSampler(torch.cuda.current_device()) as clocks:
+        if world > 1:
+            dist.barrier()
+        torch.cuda.synchronize()
+        c0 = time.time()
+        for k in range(args.steps):
+            if flush is not None:
+                flush.fill_(k & 0xFF)
+            ev[k][0].record(stream)
+            step()
+            ev[k][1].record(stream)
+        torch.cuda.synchronize()
+        c1 = time.time()
+    ms = [a.elapsed_time(b) for a, b in ev]
+    total_ms, mean_ms = max_over_ranks([sum(ms), statistics.mean(ms)], world, "cuda")
+    value = world * nbytes * args.steps / (total_ms / 1e3) / 1e9
+    peak, peak_kind = measured_peak_gbs()
+    tokens = wl.valid_tokens_total
+    if rank == 0:
+        print(json.dumps({
+            "metric": METRIC, "value": round(value, 2), "unit": "GB/s", "n_gpus": world,
+            "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(total_ms / args.steps, 5),
+            "higher_is_better": True, "scaling": "weak", "vs_baseline": None,
+            "dtype": "fp16/e4m3/int4 KV in; fp32 math; fp16 out",
+            "data": "synthetic (seeded N(0,1) + outlier channels; N(0,1) queries)",
+            "config": {"workload": spec["name"], "bytes_per_step_per_gpu": nbytes,
+                       "kv_tokens_per_step_per_gpu": tokens, "query_heads": qh,
+                       "l2": "L2 flushed between launches" if flush is not None else "no flush needed",
+                       "parallelism": f"sequence-sharded x{world}, no collective on the data path"},
+            "kv_tokens_per_s": round(world * tokens * args.steps / (total_ms / 1e3), 1),
+            "roofline": {"bound": "hbm", "achieved": round(nbytes / (mean_ms / 1e3) / 1e9, 2), "peak": peak,
+                         "unit": "GB/s", "frac": round(nbytes / (mean_ms / 1e3) / 1e9 / peak, 4),
+                         "peak_source": f"{peak_kind} (MEASURED_PEAKS.json hbm_gbs)", "traffic": None,
+                         "kernel": "decode_attention_kernel<128,4>", "launch_ms": round(mean_ms, 5)},
+            "e2e": {"value": None, "unit": "GB/s", "h2d_bytes_per_step": None, "d2h_bytes_per_step": None,
+                    "reason": "the cache is resident in HBM; end to end is measured on 'mixed'"},
+            "gpu_launches": args.steps,
+            "clocks": clocks.summary(c0, c1),
+            "cpu_baseline": None,
+        }), flush=True)
+    if world > 1:
+        dist.barrier()
+        dist.destroy_process_group()
+
+
 def run_flat(args) -> None:
     """The flat FP8 -> FP16 drop-in and the reference's own kernel, on one contiguous array."""
     import numpy as np
@@ -1098,6 +1192,9 @@ def main() -> None:
     args.warmup = max(args.warmup, 3)
     if args.impl == "hlkv" and WORKLOADS[args.workload].get("decode"):
         run_decode(args)
+        return
+    if args.impl == "hlkv" and WORKLOADS[args.workload].get("attn"):
+        run_attention(args)
         return
     if args.impl == "hlkv" and WORKLOADS[args.workload].get("flat"):
         run_flat(args)

@@ -1,0 +1,391 @@
+// Decode attention fused with the heterogeneous dequantization: one query token per
+// sequence attends to the sequence's cached keys and values, read straight from the
+// quantized blocks (FP16 / E4M3 / E5M2 / INT4 block by block) through the descriptor
+// table, without materialising FP16 K/V in HBM.  This is the "fused dequant into
+// attention" step that follows the gather in the reference's plan (ADR-0004); the
+// reference has no kernel for it.
+//
+// Semantics: K and V are exactly the binary16 values kernel (1) would gather (the same
+// decoder, dequantize_reference_to_fp16 per row), taken for the valid tokens of each
+// block in sequence order.  For query head qh and its KV head h = qh / G:
+//   s_t = softmax_scale * <q, k_t>,  p = softmax(s),  out = sum_t p_t v_t,
+// in binary32 arithmetic (exp2 with the scale folded in), the result rounded to binary16.
+// A sequence without valid tokens gives zeros.
+//
+// Structure: one CTA per (sequence, KV head), 8 warps taking the sequence's blocks
+// round-robin.  Per block and warp: 2 lanes per token compute the G scores of 16 tokens
+// at a time (each lane half of head_dim, queries from shared memory), an online-softmax
+// update, then the lanes split head_dim to accumulate p * v for the G queries.  The 8
+// warps' partial (max, sum, out) are merged in shared memory at the end.
+#include <cuda_fp16.h>
+#include <cuda_runtime.h>
+
+#include <cmath>
+#include <cstdint>
+
+#include "codec.cuh"
+#include "common.cuh"
+#include "hlkv.h"
+
+namespace hlkv {
+namespace {
+
+constexpr float kLog2e = 1.4426950408889634f;
+
+struct DevPool {
+  const uint8_t* base;
+  uint64_t slot_bytes;
+  uint32_t num_slots;
+};
+
+struct AttnParams {
+  DevPool pool[4];
+  uint64_t code_bytes[4];
+  const uint4* table;
+  const uint32_t* arena;
+  const uint2* segs;
+  const uint16_t* q;
+  uint16_t* out;
+  uint32_t* err;
+  uint32_t table_size, arena_size, nseq;
+  uint32_t T, H, layout_id, q_heads;
+  float qscale;  // softmax_scale * log2(e)
+};
+
+// The checks of kernel (1) for block j of a sequence; returns the format (4 = skip).
+__device__ __forceinline__ uint32_t resolve_block(const AttnParams& p, uint2 seg, uint32_t j,
+                                                  const uint8_t** payload, uint32_t* vt) {
+  uint32_t bad = 0, f = 4;
+  const uint64_t pos = uint64_t{seg.x} + j;
+  if (pos >= p.arena_size) {
+    bad = dev::kErrArenaRange;
+  } else {
+    const uint32_t id = __ldg(p.arena + pos);
+    if (id >= p.table_size) {
+      bad = dev::kErrBlockIdRange;
+    } else {
+      const uint4 d = __ldg(p.table + id);
+      const uint32_t ff = d.y & 0xFu, mode = (d.y >> 4) & 3u, layout = (d.y >> 6) & 0xFu,
+                     v = (d.y >> 10) & 0x3FFu;
+      if (d.w != id) bad = dev::kErrDescMismatch;
+      else if (ff == dev::kInvalidFormat) bad = dev::kErrNotExecutable;
+      else if (ff > 3 || p.pool[ff].base == nullptr || p.pool[ff].num_slots == 0) bad = dev::kErrBadFormat;
+      else if (layout != p.layout_id) bad = dev::kErrLayout;
+      else if (ff != dev::kFp16 && mode != 0) bad = dev::kErrScaleMode;
+      else if (v > p.T) bad = dev::kErrValidTokens;
+      else if (d.x >= p.pool[ff].num_slots) bad = dev::kErrSlotRange;
+      else {
+        f = ff;
+        *payload = p.pool[ff].base + uint64_t{d.x} * p.pool[ff].slot_bytes;
+        *vt = v;
+      }
+    }
+  }
+  if (bad && (threadIdx.x & 31) == 0) atomicOr(p.err, bad);
+  return f;
+}
+
+// ---- tensor-core fragments (mma.sync m16n8k16, FP16 in, FP32 accumulate) ---------------
+__device__ __forceinline__ void mma16816(float (&d)[4], const uint32_t (&a)[4], uint32_t b0, uint32_t b1) {
+  asm volatile(
+      "mma.sync.aligned.m16n8k16.row.col.f32.f16.f16.f32 {%0,%1,%2,%3}, {%4,%5,%6,%7}, {%8,%9}, "
+      "{%0,%1,%2,%3};"
+      : "+f"(d[0]), "+f"(d[1]), "+f"(d[2]), "+f"(d[3])
+      : "r"(a[0]), "r"(a[1]), "r"(a[2]), "r"(a[3]), "r"(b0), "r"(b1));
+}
+__device__ __forceinline__ void ldsm_x4(uint32_t (&r)[4], const void* smem_row) {
+  const uint32_t s = static_cast<uint32_t>(__cvta_generic_to_shared(smem_row));
+  asm volatile("ldmatrix.sync.aligned.m8n8.x4.shared.b16 {%0,%1,%2,%3}, [%4];"
+               : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]) : "r"(s));
+}
+__device__ __forceinline__ void ldsm_x4_trans(uint32_t (&r)[4], const void* smem_row) {
+  const uint32_t s = static_cast<uint32_t>(__cvta_generic_to_shared(smem_row));
+  asm volatile("ldmatrix.sync.aligned.m8n8.x4.trans.shared.b16 {%0,%1,%2,%3}, [%4];"
+               : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]) : "r"(s));
+}
+__device__ __forceinline__ uint32_t pack_half2(float lo, float hi) {
+  const __half2 h = __floats2half2_rn(lo, hi);
+  return *reinterpret_cast<const uint32_t*>(&h);
+}
+
+constexpr int kAttnWarps = 4;
+constexpr int kAttnThreads = 32 * kAttnWarps;
+
+// Per warp: a 16-token tile of K and of V (binary16, rows padded by 8 halves so that
+// ldmatrix rows fall in different banks) and P^T for the tile.
+template <int kD>
+struct WarpTiles {
+  __half k[16][kD + 8];
+  __half v[16][kD + 8];
+  __half p[8][16 + 8];
+};
+
+// Decodes tokens [t0, t0 + 16) of head h's K rows (kv 0) or V rows (kv 1), in format kF,
+// into the warp's tile; tokens >= vt become zeros.  Lane l handles 8-element chunks
+// l, l+32, ...: 16-lane groups read whole rows, coalesced.  Every load of the tile is
+// issued before the first conversion.
+template <int kD, uint32_t kF>
+__device__ __forceinline__ void stage_rows(const uint8_t* payload, const uint8_t* params, uint32_t kv,
+                                           uint32_t t0, uint32_t vt, uint32_t T, uint32_t H, uint32_t h,
+                                           __half (*tile)[kD + 8], uint32_t lane) {
+  constexpr int kChunks = kD / 8;              // chunks per row
+  constexpr int kPerLane = 16 * kChunks / 32;  // chunks per lane per tile
+  uint4 raw[kPerLane];
+  float2 prm[kPerLane];
+#pragma unroll
+  for (int i = 0; i < kPerLane; ++i) {
+    const uint32_t c = i * 32 + lane, r = c / kChunks, e = (c % kChunks) * 8;
+    const uint32_t t = t0 + r, row = (kv * T + t) * H + h;
+    const uint64_t v = (uint64_t{row} * kD + e) >> 3;  // 8-element chunk index in the slot
+    raw[i] = make_uint4(0u, 0u, 0u, 0u);
+    prm[i] = make_float2(0.0f, 0.0f);
+    if (t < vt) {
+      if constexpr (kF == dev::kFp16) {
+        raw[i] = dev::ld_stream(reinterpret_cast<const uint4*>(payload) + v);
+      } else if constexpr (kF == dev::kInt4) {
+        raw[i].x = dev::ld_stream(reinterpret_cast<const uint32_t*>(payload) + v);
+        prm[i] = __ldg(reinterpret_cast<const float2*>(params) + row);
+      } else {
+        const uint2 w = dev::ld_stream(reinterpret_cast<const uint2*>(payload) + v);
+        raw[i].x = w.x;
+        raw[i].y = w.y;
+        prm[i].x = __ldg(reinterpret_cast<const float*>(params) + row);
+      }
+    }
+  }
+#pragma unroll
+  for (int i = 0; i < kPerLane; ++i) {
+    const uint32_t c = i * 32 + lane, r = c / kChunks, e = (c % kChunks) * 8;
+    uint4 o;
+    if constexpr (kF == dev::kFp16) {
+      o = dev::canon_f16x8(raw[i]);
+    } else if constexpr (kF == dev::kInt4) {
+      o = dev::int4x8_to_f16(raw[i].x, prm[i].x, prm[i].y);
+    } else {
+      o = dev::fp8x8_to_f16<kF>(make_uint2(raw[i].x, raw[i].y), prm[i].x);
+    }
+    // tokens >= vt: zero codes with zero parameters decode to +0 in every format
+    *reinterpret_cast<uint4*>(&tile[r][e]) = o;
+  }
+}
+
+template <int kD>
+__device__ __noinline__ void stage_tiles(uint32_t f, const uint8_t* payload, const uint8_t* params,
+                                         uint32_t t0, uint32_t vt, uint32_t T, uint32_t H, uint32_t h,
+                                         WarpTiles<kD>& w, uint32_t lane) {
+  // One copy of each format's staging code (out of line, K and V in a loop): the
+  // instruction footprint stays small.
+#pragma unroll 1
+  for (uint32_t kv = 0; kv < 2; ++kv) {
+    __half(*tile)[kD + 8] = kv == 0 ? w.k : w.v;
+    switch (f) {
+      case dev::kFp16: stage_rows<kD, dev::kFp16>(payload, params, kv, t0, vt, T, H, h, tile, lane); break;
+      case dev::kE4M3: stage_rows<kD, dev::kE4M3>(payload, params, kv, t0, vt, T, H, h, tile, lane); break;
+      case dev::kE5M2: stage_rows<kD, dev::kE5M2>(payload, params, kv, t0, vt, T, H, h, tile, lane); break;
+      default: stage_rows<kD, dev::kInt4>(payload, params, kv, t0, vt, T, H, h, tile, lane); break;
+    }
+  }
+}
+
+template <int kD, int kG>
+__global__ void __launch_bounds__(kAttnThreads, 4) decode_attention_kernel(const AttnParams p) {
+  constexpr int kSteps = kD / 16;  // k-steps of Q.K and m-tiles of V^T.P
+  __shared__ __align__(16) unsigned char s_raw[kAttnWarps * sizeof(WarpTiles<kD>) >
+                                                       kAttnWarps * (kD * 8 + 16) * 4
+                                                   ? kAttnWarps * sizeof(WarpTiles<kD>)
+                                                   : kAttnWarps * (kD * 8 + 16) * 4];
+  const uint32_t seq = blockIdx.x / p.H, h = blockIdx.x % p.H;
+  const uint32_t lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+  const uint32_t grp = lane >> 2, quad = lane & 3;
+  WarpTiles<kD>& w = reinterpret_cast<WarpTiles<kD>*>(s_raw)[warp];
+
+  // B fragments of Q^T (k = head_dim, n = query head of the group; columns >= kG are 0).
+  uint32_t qb[kSteps][2];
+  {
+    const uint16_t* qrow = p.q + (uint64_t{seq} * p.q_heads + h * kG + grp) * kD;
+#pragma unroll
+    for (int k = 0; k < kSteps; ++k) {
+#pragma unroll
+      for (int j = 0; j < 2; ++j) {
+        qb[k][j] = grp < kG ? __ldg(reinterpret_cast<const uint32_t*>(qrow + k * 16 + j * 8 + quad * 2)) : 0u;
+      }
+    }
+  }
+  // O^T accumulators: m-tile mt covers head_dim rows [16 mt, 16 mt + 16); this lane holds
+  // dims 16 mt + grp (+8) for query columns 2 quad, 2 quad + 1.
+  float acc[kSteps][4];
+#pragma unroll
+  for (int mt = 0; mt < kSteps; ++mt) acc[mt][0] = acc[mt][1] = acc[mt][2] = acc[mt][3] = 0.0f;
+  float m[2] = {-INFINITY, -INFINITY}, l[2] = {0.0f, 0.0f};
+
+  const uint2 seg = p.segs[seq];
+  const uint32_t T = p.T, H = p.H;
+  for (uint32_t j = warp; j < seg.y; j += kAttnWarps) {
+    const uint8_t* payload = nullptr;
+    uint32_t vt = 0;
+    const uint32_t f = resolve_block(p, seg, j, &payload, &vt);
+    if (f > 3 || vt == 0) continue;
+    const uint8_t* params = payload + p.code_bytes[f];
+    for (uint32_t t0 = 0; t0 < vt; t0 += 16) {
+      stage_tiles<kD>(f, payload, params, t0, vt, T, H, h, w, lane);
+      __syncwarp();
+      // S^T (16 tokens x 8 query columns) = K . Q^T
+      float s[4] = {0.0f, 0.0f, 0.0f, 0.0f};
+#pragma unroll
+      for (int k = 0; k < kSteps; ++k) {
+        uint32_t a[4];
+        ldsm_x4(a, &w.k[(lane & 7) + ((lane >> 3) & 1) * 8][k * 16 + (lane >> 4) * 8]);
+        mma16816(s, a, qb[k][0], qb[k][1]);
+      }
+      // online softmax per query column; this lane: tokens grp, grp + 8; columns 2quad, 2quad+1
+      const bool v0 = t0 + grp < vt, v1 = t0 + grp + 8 < vt;
+      float pr[4];
+#pragma unroll
+      for (int c = 0; c < 2; ++c) {
+        const float x0 = v0 ? s[c] * p.qscale : -INFINITY;
+        const float x1 = v1 ? s[2 + c] * p.qscale : -INFINITY;
+        float mx = fmaxf(x0, x1);
+        mx = fmaxf(mx, __shfl_xor_sync(0xFFFFFFFFu, mx, 4));
+        mx = fmaxf(mx, __shfl_xor_sync(0xFFFFFFFFu, mx, 8));
+        mx = fmaxf(mx, __shfl_xor_sync(0xFFFFFFFFu, mx, 16));
+        const float mn = fmaxf(m[c], mx);  // finite: token t0 is valid
+        const float alpha = exp2f(m[c] - mn);
+        pr[c] = exp2f(x0 - mn);
+        pr[2 + c] = exp2f(x1 - mn);
+        float sum = pr[c] + pr[2 + c];
+        sum += __shfl_xor_sync(0xFFFFFFFFu, sum, 4);
+        sum += __shfl_xor_sync(0xFFFFFFFFu, sum, 8);
+        sum += __shfl_xor_sync(0xFFFFFFFFu, sum, 16);
+        l[c] = l[c] * alpha + sum;
+        m[c] = mn;
+#pragma unroll
+        for (int mt = 0; mt < kSteps; ++mt) {
+          acc[mt][c] *= alpha;
+          acc[mt][2 + c] *= alpha;
+        }
+      }
+      // P^T -> shared (query column major), read back as the B fragment of V^T . P
+      w.p[quad * 2][grp] = __float2half_rn(pr[0]);
+      w.p[quad * 2 + 1][grp] = __float2half_rn(pr[1]);
+      w.p[quad * 2][grp + 8] = __float2half_rn(pr[2]);
+      w.p[quad * 2 + 1][grp + 8] = __float2half_rn(pr[3]);
+      __syncwarp();
+      const uint32_t pb0 = *reinterpret_cast<const uint32_t*>(&w.p[grp][quad * 2]);
+      const uint32_t pb1 = *reinterpret_cast<const uint32_t*>(&w.p[grp][quad * 2 + 8]);
+      // O^T (head_dim x 8) += V^T . P
+#pragma unroll
+      for (int mt = 0; mt < kSteps; ++mt) {
+        uint32_t a[4];
+        ldsm_x4_trans(a, &w.v[(lane & 7) + (lane >> 4) * 8][mt * 16 + ((lane >> 3) & 1) * 8]);
+        mma16816(acc[mt], a, pb0, pb1);
+      }
+      __syncwarp();  // the tiles are rewritten next
+    }
+  }
+
+  // ---- merge the warps: per query column the max, the sum and the head_dim outputs ----
+  __syncthreads();  // the tiles are dead; their space holds the merge buffers
+  float* s_o = reinterpret_cast<float*>(s_raw);                 // [warp][8][kD]
+  float* s_ml = s_o + kAttnWarps * 8 * kD;                      // [warp][8][2]
+#pragma unroll
+  for (int mt = 0; mt < kSteps; ++mt) {
+#pragma unroll
+    for (int c = 0; c < 2; ++c) {
+      s_o[(warp * 8 + quad * 2 + c) * kD + mt * 16 + grp] = acc[mt][c];
+      s_o[(warp * 8 + quad * 2 + c) * kD + mt * 16 + grp + 8] = acc[mt][2 + c];
+    }
+  }
+  if (grp == 0) {
+#pragma unroll
+    for (int c = 0; c < 2; ++c) {
+      s_ml[(warp * 8 + quad * 2 + c) * 2] = m[c];
+      s_ml[(warp * 8 + quad * 2 + c) * 2 + 1] = l[c];
+    }
+  }
+  __syncthreads();
+  for (uint32_t i = threadIdx.x; i < kG * kD; i += kAttnThreads) {
+    const uint32_t g = i / kD, e = i % kD;
+    float M = -INFINITY;
+#pragma unroll
+    for (int wi = 0; wi < kAttnWarps; ++wi) M = fmaxf(M, s_ml[(wi * 8 + g) * 2]);
+    float L = 0.0f, O = 0.0f;
+    if (M != -INFINITY) {
+#pragma unroll
+      for (int wi = 0; wi < kAttnWarps; ++wi) {
+        const float mw = s_ml[(wi * 8 + g) * 2];
+        const float a = mw == -INFINITY ? 0.0f : exp2f(mw - M);
+        L = fmaf(s_ml[(wi * 8 + g) * 2 + 1], a, L);
+        O = fmaf(s_o[(wi * 8 + g) * kD + e], a, O);
+      }
+    }
+    const float r = L > 0.0f ? O / L : 0.0f;
+    p.out[(uint64_t{seq} * p.q_heads + h * kG + g) * kD + e] = __half_as_ushort(__float2half_rn(r));
+  }
+}
+
+template <int kD>
+cudaError_t launch_for_group(uint32_t group, const AttnParams& p, unsigned grid, cudaStream_t s) {
+  switch (group) {
+    case 1: decode_attention_kernel<kD, 1><<<grid, kAttnThreads, 0, s>>>(p); break;
+    case 2: decode_attention_kernel<kD, 2><<<grid, kAttnThreads, 0, s>>>(p); break;
+    case 4: decode_attention_kernel<kD, 4><<<grid, kAttnThreads, 0, s>>>(p); break;
+    default: decode_attention_kernel<kD, 8><<<grid, kAttnThreads, 0, s>>>(p); break;
+  }
+  return cudaGetLastError();
+}
+
+}  // namespace
+}  // namespace hlkv
+
+extern "C" int hlkv_decode_attention(const HlkvPools* pools, const HlkvLayout* layout,
+                                     const HlkvExecDescriptor* d_table, uint32_t table_size,
+                                     const uint32_t* d_arena, uint32_t arena_size,
+                                     const HlkvSegment* d_segs, uint32_t nseq, const uint16_t* d_q,
+                                     uint32_t q_heads, float softmax_scale, uint16_t* d_out,
+                                     uint32_t* d_err, hlkv_stream_t stream) {
+  using namespace hlkv;
+  if (pools == nullptr || !layout_ok(layout) || d_err == nullptr) return HLKV_INVALID_ARGUMENT;
+  if (layout->head_dim != 64 && layout->head_dim != 128) return HLKV_INVALID_ARGUMENT;
+  const uint32_t H = layout->kv_heads;
+  if (q_heads == 0 || q_heads % H != 0) return HLKV_INVALID_ARGUMENT;
+  const uint32_t group = q_heads / H;
+  if (group != 1 && group != 2 && group != 4 && group != 8) return HLKV_INVALID_ARGUMENT;
+  if (!(softmax_scale > 0.0f) || !std::isfinite(softmax_scale)) return HLKV_INVALID_ARGUMENT;
+  if (nseq == 0) return HLKV_OK;
+  if (d_segs == nullptr || d_q == nullptr || d_out == nullptr ||
+      (table_size > 0 && d_table == nullptr) || (arena_size > 0 && d_arena == nullptr)) {
+    return HLKV_INVALID_ARGUMENT;
+  }
+  if (uint64_t{nseq} * H > 0x7FFFFFFFull) return HLKV_INVALID_ARGUMENT;
+  AttnParams p{};
+  const uint64_t elems = uint64_t{2} * layout->block_tokens * H * layout->head_dim;
+  for (int f = 0; f < 4; ++f) {
+    const HlkvPool& q = pools->pool[f];
+    p.code_bytes[f] = layout_code_bytes(f, elems);
+    if (q.base == nullptr || q.num_slots == 0) continue;
+    if ((reinterpret_cast<uintptr_t>(q.base) & 15u) != 0 || (q.slot_bytes & 15u) != 0 ||
+        q.slot_bytes < hlkv_layout_slot_bytes(f, layout)) {
+      return HLKV_INVALID_ARGUMENT;
+    }
+    p.pool[f] = DevPool{static_cast<const uint8_t*>(q.base), q.slot_bytes, q.num_slots};
+  }
+  p.table = reinterpret_cast<const uint4*>(d_table);
+  p.arena = d_arena;
+  p.segs = reinterpret_cast<const uint2*>(d_segs);
+  p.q = d_q;
+  p.out = d_out;
+  p.err = d_err;
+  p.table_size = table_size;
+  p.arena_size = arena_size;
+  p.nseq = nseq;
+  p.T = layout->block_tokens;
+  p.H = H;
+  p.layout_id = layout->layout_id;
+  p.q_heads = q_heads;
+  p.qscale = softmax_scale * kLog2e;
+  const cudaStream_t s = reinterpret_cast<cudaStream_t>(stream);
+  const unsigned grid = nseq * H;
+  const cudaError_t e = layout->head_dim == 64 ? launch_for_group<64>(group, p, grid, s)
+                                               : launch_for_group<128>(group, p, grid, s);
+  return cuda_status(e);
+}

@@ -131,6 +131,8 @@ SIGNATURES: list[tuple[str, object, list]] = [
     ("hlkv_last_cuda_error", _int, []),
     ("hlkv_gather_dequant", _int, [_P(Pools), _P(Layout), _vp, _u32, _vp, _u32, _vp, _u32, _vp,
                                    _vp, _vp, _vp]),
+    ("hlkv_decode_attention", _int, [_P(Pools), _P(Layout), _vp, _u32, _vp, _u32, _vp, _u32, _vp,
+                                     _u32, C.c_float, _vp, _vp, _vp]),
     ("hlkv_transcode", _int, [_P(Pools), _P(Layout), _vp, _u32, _vp, _vp]),
     ("hlkv_append_encode", _int, [_P(Pools), _P(Layout), _vp, _u32, _vp, _u32, _vp, _vp, _vp]),
     ("hlkv_apply_delta", _int, [_vp, _u32, _vp, _u32, _vp, _u32, _vp, _u32, _vp, _vp]),
@@ -495,6 +497,19 @@ def append_encode(pools: Pools, layout: Layout, table_ptr: int, table_size: int,
     st = lib().hlkv_append_encode(C.byref(pools), C.byref(layout), table_ptr or None, table_size,
                                   _ptr(targets), n, _ptr(tokens), _ptr(err), _stream_handle(stream))
     check(st, "hlkv_append_encode")
+    return st
+
+
+def decode_attention(pools: Pools, layout: Layout, table_ptr: int, table_size: int, arena_ptr: int,
+                     arena_size: int, segs, q, q_heads: int, softmax_scale: float, out, err,
+                     stream=None) -> int:
+    """Decode attention over the quantized blocks.  q, out: device 16-bit tensors
+    [nseq, q_heads, head_dim]; segs: device int32 [nseq, 2]."""
+    nseq = int(segs.shape[0])
+    st = lib().hlkv_decode_attention(C.byref(pools), C.byref(layout), table_ptr or None, table_size,
+                                     arena_ptr or None, arena_size, _ptr(segs), nseq, _ptr(q), q_heads,
+                                     softmax_scale, _ptr(out), _ptr(err), _stream_handle(stream))
+    check(st, "hlkv_decode_attention")
     return st
 
 

@@ -191,6 +191,26 @@ int hlkv_apply_delta(HlkvExecDescriptor* d_table, uint32_t table_size, uint32_t*
                      uint32_t n_desc, const HlkvIdPatch* d_id_patches, uint32_t n_id,
                      uint32_t* d_err, hlkv_stream_t stream);
 
+/* ---- decode attention over the quantized blocks ------------------------------------------ */
+/*
+ * One query token per sequence attends to the sequence's cached K and V, read from the
+ * quantized blocks through the descriptor table (no FP16 K/V written to HBM).  K and V are
+ * exactly the binary16 values hlkv_gather_dequant would write (the reference's
+ * dequantize_reference_to_fp16), for the valid tokens of each block in sequence order.
+ * For query head qh and KV head h = qh / (q_heads / kv_heads):
+ *   out[i][qh] = softmax_t(softmax_scale * <q[i][qh], k_t>) . v_t
+ * in binary32 arithmetic, rounded to binary16; zeros for a sequence without valid tokens.
+ * d_q and d_out are binary16 [nseq][q_heads][head_dim].  head_dim 64 or 128; q_heads /
+ * kv_heads in {1, 2, 4, 8}; softmax_scale finite and > 0.  Blocks failing kernel (1)'s checks
+ * are left out with their HLKV_ERR_* bits.  The reference has no attention kernel; this is
+ * the fused dequant + attention step its plan names (ADR-0004).
+ */
+int hlkv_decode_attention(const HlkvPools* pools, const HlkvLayout* layout,
+                          const HlkvExecDescriptor* d_table, uint32_t table_size,
+                          const uint32_t* d_arena, uint32_t arena_size, const HlkvSegment* d_segs,
+                          uint32_t nseq, const uint16_t* d_q, uint32_t q_heads, float softmax_scale,
+                          uint16_t* d_out, uint32_t* d_err, hlkv_stream_t stream);
+
 /* ---- format-change transcode ------------------------------------------------------------ */
 typedef struct {
   uint32_t from_format; /* the block's current format and slot ...                  */

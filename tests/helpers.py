@@ -56,3 +56,44 @@ def assert_bits_equal(got: np.ndarray, want: np.ndarray, what: str = "") -> None
         i = bad[0]
         raise AssertionError(f"{what}: {bad.size} of {got.size} differ; first at {i}: "
                              f"got {got[i]:#06x} want {want[i]:#06x}")
+
+
+def oracle_attention(oracle, wl, q: np.ndarray, scale: float, table=None, arena=None, segs=None):
+    """Decode attention in float64 over the oracle's gather of the same tables: K and V
+    are the binary16 values of the valid tokens of each block, in sequence order.
+    q: float array [nseq, q_heads, D].  Returns (float64 [nseq, q_heads, D], gather error bits)."""
+    table = device_table_words(wl) if table is None else table
+    segs = wl.segs_host if segs is None else segs
+    T, H, D = wl.T, wl.H, wl.D
+    nblk = int(segs[:, 1].sum())
+    out, err = oracle_gather(oracle, wl, out_elems=nblk * wl.block_elems, table=table, arena=arena,
+                             segs=segs)
+    blocks = out.view(np.float16).astype(np.float64).reshape(nblk, 2, T, H, D)
+    arena = device_arena(wl) if arena is None else arena
+    nseq, qh = q.shape[0], q.shape[1]
+    g = qh // H
+    res = np.zeros((nseq, qh, D))
+    b0 = 0
+    for i, (off, ln) in enumerate(segs):
+        ks, vs = [], []
+        for j in range(ln):
+            pos = off + j
+            ok = pos < arena.size and arena[pos] < table.shape[0]
+            vt = int(table[arena[pos]][1] >> 10) & 0x3FF if ok else 0
+            fmt = int(table[arena[pos]][1] & 0xF) if ok else 15
+            if fmt <= 3 and vt <= T:
+                ks.append(blocks[b0 + j, 0, :vt])
+                vs.append(blocks[b0 + j, 1, :vt])
+        b0 += ln
+        if not ks:
+            continue
+        K = np.concatenate(ks)  # [tokens, H, D]
+        V = np.concatenate(vs)
+        if K.shape[0] == 0:
+            continue
+        for hq in range(qh):
+            h = hq // g
+            s = scale * (K[:, h, :] @ q[i, hq].astype(np.float64))
+            p = np.exp(s - s.max())
+            res[i, hq] = (p[:, None] * V[:, h, :]).sum(0) / p.sum()
+    return res, err

@@ -1,0 +1,92 @@
+"""Decode attention fused with the heterogeneous dequantization (hlkv_decode_attention)
+against float64 attention over the oracle's bit-exact gather of the same blocks.  The
+kernel computes in binary32 and rounds to binary16: the tolerance below is 2 binary16 ulps
+of the result plus 1e-3 of the value scale."""
+import numpy as np
+import pytest
+
+from helpers import oracle_attention
+
+pytestmark = pytest.mark.gpu
+
+
+def _close(got, want, vscale):
+    tol = 2 * 2.0 ** -11 * np.abs(want) + 1e-3 * vscale
+    bad = np.abs(got - want) > tol
+    assert not bad.any(), (int(bad.sum()), got[bad][:4], want[bad][:4])
+
+
+def _run(hlkv, wl, q_heads, scale, seed, segs=None):
+    import torch
+    rng = np.random.default_rng(seed)
+    segs_host = wl.segs_host if segs is None else segs
+    nseq = len(segs_host)
+    q = rng.standard_normal((nseq, q_heads, wl.D)).astype(np.float16)
+    d_q = torch.from_numpy(q.view(np.int16)).cuda()
+    d_segs = wl.segs if segs is None else torch.from_numpy(segs.astype(np.int32)).cuda()
+    out = torch.full((nseq, q_heads, wl.D), 0x7777, dtype=torch.int32, device="cuda").to(torch.int16)
+    err = torch.zeros(1, dtype=torch.int32, device="cuda")
+    hlkv.decode_attention(wl.hlkv_pools(), wl.layout, wl.dt.table_ptr, wl.dt.table_size,
+                          wl.dt.arena_ptr, wl.dt.arena_size, d_segs, d_q, q_heads, scale, out, err)
+    torch.cuda.synchronize()
+    return q, out.cpu().numpy().view(np.float16).astype(np.float64), int(err.item())
+
+
+@pytest.mark.parametrize("T,H,D,group", [(16, 8, 128, 4), (16, 2, 64, 1), (4, 2, 128, 8), (32, 1, 64, 2)])
+def test_attention_matches_oracle(hlkv_lib, oracle, cuda_device, T, H, D, group):
+    from hlkv.workload import build_workload, mixed_formats
+    fm = mixed_formats(5, [3, 17, 1, 40, 9], probs=(0.25, 0.35, 0.15, 0.25), seed=T + D)
+    rng = np.random.default_rng(D)
+    vt = [[T] * (len(r) - 1) + [int(rng.integers(1, T + 1))] for r in fm]
+    vt[1][4] = 0   # a block without valid tokens inside a sequence
+    wl = build_workload(fm, T=T, H=H, D=D, seed=T * H, valid_tokens=vt)
+    scale = 1.0 / np.sqrt(D)
+    q, got, err = _run(hlkv_lib, wl, H * group, scale, seed=H + group)
+    want, oerr = oracle_attention(oracle, wl, q.astype(np.float64), scale)
+    assert err == oerr == 0
+    _close(got, want, vscale=20.0)
+
+
+def test_attention_empty_sequence_and_bad_blocks(hlkv_lib, oracle, cuda_device):
+    """A sequence of length 0 gives zeros; a descriptor that fails kernel (1)'s checks is left
+    out of its sequence with its error bit, as the oracle's gather leaves it out."""
+    from hlkv.workload import build_workload
+    from helpers import device_arena, device_table_words
+    import torch
+    T, H, D = 16, 2, 128
+    wl = build_workload([[1, 3, 0], [3, 3], [0]], T=T, H=H, D=D, seed=4)
+    segs = wl.segs_host.copy()
+    segs[2, 1] = 0                     # empty sequence
+    # make sequence 1's first block non-executable on the device (format 15)
+    table = device_table_words(wl).copy()
+    bid = int(device_arena(wl)[segs[1, 0]])
+    table[bid, 1] = (int(table[bid, 1]) & 0xFFFFFFF0) | 15
+    d_table = torch.from_numpy(table.view(np.int32).reshape(-1)).cuda()
+    import hlkv
+    rng = np.random.default_rng(3)
+    q = rng.standard_normal((3, 2 * H, D)).astype(np.float16)
+    out = torch.full((3, 2 * H, D), 0x7777, dtype=torch.int32, device="cuda").to(torch.int16)
+    err = torch.zeros(1, dtype=torch.int32, device="cuda")
+    hlkv_lib.decode_attention(wl.hlkv_pools(), wl.layout, d_table.data_ptr(), wl.dt.table_size,
+                              wl.dt.arena_ptr, wl.dt.arena_size,
+                              torch.from_numpy(segs.astype(np.int32)).cuda(),
+                              torch.from_numpy(q.view(np.int16)).cuda(), 2 * H, 0.125, out, err)
+    torch.cuda.synchronize()
+    got = out.cpu().numpy().view(np.float16).astype(np.float64)
+    want, oerr = oracle_attention(oracle, wl, q.astype(np.float64), 0.125, table=table, segs=segs)
+    assert int(err.item()) == oerr == 1
+    assert np.all(got[2] == 0)
+    _close(got, want, vscale=20.0)
+
+
+def test_attention_rejects_bad_arguments(hlkv_lib, cuda_device):
+    import ctypes as C
+    import hlkv
+    lay = hlkv.Layout(16, 8, 128, 1)
+    pools = hlkv.Pools()
+    L = hlkv.lib()
+    err = C.c_void_p(8)
+    for qh, sc, l2 in ((12, 1.0, lay), (8 * 16, 1.0, lay), (8, 0.0, lay), (8, float("inf"), lay),
+                       (8, 1.0, hlkv.Layout(16, 8, 256, 1))):
+        assert L.hlkv_decode_attention(C.byref(pools), C.byref(l2), None, 0, None, 0, C.c_void_p(8), 1,
+                                       C.c_void_p(8), qh, sc, C.c_void_p(8), err, None) == hlkv.INVALID_ARGUMENT
