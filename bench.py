@@ -158,7 +158,7 @@ class ClockSampler:
     (NVML calls made from the benchmarked process contend with its CUDA calls).
     Sample times are time.time(); summary() takes the same clock."""
 
-    def __init__(self, index: int, period_s: float = 0.01):
+    def __init__(self, index: int, period_s: float = 0.002):
         # NVML enumerates all GPUs; map the CUDA index through CUDA_VISIBLE_DEVICES.
         vis = os.environ.get("CUDA_VISIBLE_DEVICES")
         self.index = int(vis.split(",")[index]) if vis and vis.split(",")[0].isdigit() else index
