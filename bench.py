@@ -83,6 +83,13 @@ WORKLOADS = {
                        attn=True, q_heads=32,
                        name="decode attention fused with dequant over the mixed cache: 64 seq x 2048 "
                             "tok, 8 KV heads x 128, 32 query heads, FP16 .25 / E4M3 .5 / INT4 .25"),
+    # Decode attention over one layer of the long-context cache (config 5's shape: 16 seq x
+    # 131072 tokens, INT4 .85 / E4M3 .10 / FP16 .05) with Llama-3-70B's 64 query heads:
+    # few sequences, so each (sequence, KV head) is split over many CTAs.
+    "attn_long": dict(nseq=16, blocks=8192, probs=(0.05, 0.10, 0.0, 0.85), scaling="strong",
+                      attn=True, q_heads=64,
+                      name="decode attention fused with dequant, long context: 16 seq x 131072 tok "
+                           "(one layer), 8 KV heads x 128, 64 query heads, INT4 .85 / E4M3 .10 / FP16 .05"),
     # Config 1's data as one contiguous E4M3 array (8,388,608 values, 128-value groups):
     # the drop-in hlkv_dequantize_fp8_to_fp16 against the reference's own GPU kernel.
     "flat_e4m3": dict(n=8_388_608, group=128, fmt=1, scaling="weak", flat=True,
@@ -735,9 +742,22 @@ def run_attention(args) -> None:
     stream = torch.cuda.current_stream()
     scale = 1.0 / float(np.sqrt(D))
 
+    # With at least two (sequence, KV head) units per SM the grid already fills the GPU and a
+    # split only adds the merge; with fewer, each unit is split so that about 32 CTAs per SM
+    # are launched (long sequences, few of them).
+    sms = torch.cuda.get_device_properties(torch.cuda.current_device()).multi_processor_count
+    units = nseq * wl.H
+    auto = 1 if units >= 2 * sms else max(1, -(-32 * sms // units))
+    splits = args.splits if args.splits else auto
+    ws = None
+    if splits > 1:
+        ws = torch.empty(hlkv.decode_attention_workspace_bytes(nseq, wl.H, D, splits), dtype=torch.uint8,
+                         device="cuda")
+
     def step():
-        hlkv.decode_attention(pools, wl.layout, wl.dt.table_ptr, wl.dt.table_size, wl.dt.arena_ptr,
-                              wl.dt.arena_size, wl.segs, q, qh, scale, out, err, stream=stream)
+        hlkv.decode_attention_split(pools, wl.layout, wl.dt.table_ptr, wl.dt.table_size, wl.dt.arena_ptr,
+                                    wl.dt.arena_size, wl.segs, q, qh, scale, splits, ws, out, err,
+                                    stream=stream)
 
     # Algorithmic bytes: codes + row parameters of the K and V rows read, 20 B of descriptor
     # and arena entry per block, the queries read and the outputs written.
@@ -779,13 +799,15 @@ def run_attention(args) -> None:
             "data": "synthetic (seeded N(0,1) + outlier channels; N(0,1) queries)",
             "config": {"workload": spec["name"], "bytes_per_step_per_gpu": nbytes,
                        "kv_tokens_per_step_per_gpu": tokens, "query_heads": qh,
+                       "splits_per_sequence_head": splits,
                        "l2": "L2 flushed between launches" if flush is not None else "no flush needed",
                        "parallelism": f"sequence-sharded x{world}, no collective on the data path"},
             "kv_tokens_per_s": round(world * tokens * args.steps / (total_ms / 1e3), 1),
             "roofline": {"bound": "hbm", "achieved": round(nbytes / (mean_ms / 1e3) / 1e9, 2), "peak": peak,
                          "unit": "GB/s", "frac": round(nbytes / (mean_ms / 1e3) / 1e9 / peak, 4),
                          "peak_source": f"{peak_kind} (MEASURED_PEAKS.json hbm_gbs)", "traffic": None,
-                         "kernel": "decode_attention_kernel<128,4>", "launch_ms": round(mean_ms, 5)},
+                         "kernel": f"decode_attention_kernel<128,{qh // wl.H}> (+ merge)",
+                         "launch_ms": round(mean_ms, 5)},
             "e2e": {"value": None, "unit": "GB/s", "h2d_bytes_per_step": None, "d2h_bytes_per_step": None,
                     "reason": "the cache is resident in HBM; end to end is measured on 'mixed'"},
             "gpu_launches": args.steps,
@@ -1188,6 +1210,8 @@ def main() -> None:
     ap.add_argument("--workload", choices=sorted(WORKLOADS), default="mixed")
     ap.add_argument("--e2e-steps", type=int, default=10)
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--splits", type=int, default=0,
+                    help="attention workloads: CTAs per (sequence, KV head); 0 = none with >= 2 units per SM, else about 32 CTAs per SM")
     args = ap.parse_args()
     args.warmup = max(args.warmup, 3)
     if args.impl == "hlkv" and WORKLOADS[args.workload].get("decode"):

@@ -49,8 +49,15 @@ struct AttnParams {
   uint32_t* err;
   uint32_t table_size, arena_size, nseq;
   uint32_t T, H, layout_id, q_heads;
-  float qscale;  // softmax_scale * log2(e)
+  float qscale;     // softmax_scale * log2(e)
+  uint32_t splits;  // CTAs per (sequence, KV head), each over a contiguous share of the blocks
+  float* ws;        // splits > 1: per CTA, kPart floats of partial results
 };
+
+// Partial result of one CTA for its (sequence, KV head) and share of the blocks: the max
+// (exp2 domain) and the sum per query column, then the unnormalised outputs.
+template <int kD>
+constexpr uint32_t kPart = 8 + 8 + 8 * kD;
 
 // The checks of kernel (1) for block j of a sequence; returns the format (4 = skip).
 __device__ __forceinline__ uint32_t resolve_block(const AttnParams& p, uint2 seg, uint32_t j,
@@ -102,10 +109,6 @@ __device__ __forceinline__ void ldsm_x4_trans(uint32_t (&r)[4], const void* smem
   const uint32_t s = static_cast<uint32_t>(__cvta_generic_to_shared(smem_row));
   asm volatile("ldmatrix.sync.aligned.m8n8.x4.trans.shared.b16 {%0,%1,%2,%3}, [%4];"
                : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]) : "r"(s));
-}
-__device__ __forceinline__ uint32_t pack_half2(float lo, float hi) {
-  const __half2 h = __floats2half2_rn(lo, hi);
-  return *reinterpret_cast<const uint32_t*>(&h);
 }
 
 constexpr int kAttnWarps = 4;
@@ -194,7 +197,8 @@ __global__ void __launch_bounds__(kAttnThreads, 4) decode_attention_kernel(const
                                                        kAttnWarps * (kD * 8 + 16) * 4
                                                    ? kAttnWarps * sizeof(WarpTiles<kD>)
                                                    : kAttnWarps * (kD * 8 + 16) * 4];
-  const uint32_t seq = blockIdx.x / p.H, h = blockIdx.x % p.H;
+  const uint32_t unit = blockIdx.x / p.splits, split = blockIdx.x % p.splits;
+  const uint32_t seq = unit / p.H, h = unit % p.H;
   const uint32_t lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
   const uint32_t grp = lane >> 2, quad = lane & 3;
   WarpTiles<kD>& w = reinterpret_cast<WarpTiles<kD>*>(s_raw)[warp];
@@ -220,7 +224,9 @@ __global__ void __launch_bounds__(kAttnThreads, 4) decode_attention_kernel(const
 
   const uint2 seg = p.segs[seq];
   const uint32_t T = p.T, H = p.H;
-  for (uint32_t j = warp; j < seg.y; j += kAttnWarps) {
+  const uint32_t b0 = static_cast<uint32_t>(uint64_t{seg.y} * split / p.splits);
+  const uint32_t b1 = static_cast<uint32_t>(uint64_t{seg.y} * (split + 1) / p.splits);
+  for (uint32_t j = b0 + warp; j < b1; j += kAttnWarps) {
     const uint8_t* payload = nullptr;
     uint32_t vt = 0;
     const uint32_t f = resolve_block(p, seg, j, &payload, &vt);
@@ -318,9 +324,41 @@ __global__ void __launch_bounds__(kAttnThreads, 4) decode_attention_kernel(const
         O = fmaf(s_o[(wi * 8 + g) * kD + e], a, O);
       }
     }
-    const float r = L > 0.0f ? O / L : 0.0f;
-    p.out[(uint64_t{seq} * p.q_heads + h * kG + g) * kD + e] = __half_as_ushort(__float2half_rn(r));
+    if (p.splits == 1) {
+      const float r = L > 0.0f ? O / L : 0.0f;
+      p.out[(uint64_t{seq} * p.q_heads + h * kG + g) * kD + e] = __half_as_ushort(__float2half_rn(r));
+    } else {
+      float* w = p.ws + uint64_t{blockIdx.x} * kPart<kD>;
+      w[16 + g * kD + e] = O;
+      if (e == 0) {
+        w[g] = M;
+        w[8 + g] = L;
+      }
+    }
   }
+}
+
+// Merges the splits' partial results of one (sequence, query head) per CTA, kD threads.
+template <int kD>
+__global__ void __launch_bounds__(kD) decode_attention_merge(const float* __restrict__ ws, uint32_t splits,
+                                                            uint32_t H, uint32_t group, uint32_t q_heads,
+                                                            uint16_t* __restrict__ out) {
+  const uint32_t seq = blockIdx.x / q_heads, qh = blockIdx.x % q_heads;
+  const uint32_t h = qh / group, g = qh % group, e = threadIdx.x;
+  const float* w = ws + uint64_t{seq * H + h} * splits * kPart<kD>;
+  float M = -INFINITY;
+  for (uint32_t s = 0; s < splits; ++s) M = fmaxf(M, w[uint64_t{s} * kPart<kD> + g]);
+  float L = 0.0f, O = 0.0f;
+  if (M != -INFINITY) {
+    for (uint32_t s = 0; s < splits; ++s) {
+      const float* ps = w + uint64_t{s} * kPart<kD>;
+      const float a = ps[g] == -INFINITY ? 0.0f : exp2f(ps[g] - M);
+      L = fmaf(ps[8 + g], a, L);
+      O = fmaf(ps[16 + g * kD + e], a, O);
+    }
+  }
+  const float r = L > 0.0f ? O / L : 0.0f;
+  out[(uint64_t{seq} * q_heads + qh) * kD + e] = __half_as_ushort(__float2half_rn(r));
 }
 
 template <int kD>
@@ -335,15 +373,12 @@ cudaError_t launch_for_group(uint32_t group, const AttnParams& p, unsigned grid,
 }
 
 }  // namespace
-}  // namespace hlkv
 
-extern "C" int hlkv_decode_attention(const HlkvPools* pools, const HlkvLayout* layout,
-                                     const HlkvExecDescriptor* d_table, uint32_t table_size,
-                                     const uint32_t* d_arena, uint32_t arena_size,
-                                     const HlkvSegment* d_segs, uint32_t nseq, const uint16_t* d_q,
-                                     uint32_t q_heads, float softmax_scale, uint16_t* d_out,
-                                     uint32_t* d_err, hlkv_stream_t stream) {
-  using namespace hlkv;
+int launch_attention(const HlkvPools* pools, const HlkvLayout* layout, const HlkvExecDescriptor* d_table,
+                     uint32_t table_size, const uint32_t* d_arena, uint32_t arena_size,
+                     const HlkvSegment* d_segs, uint32_t nseq, const uint16_t* d_q, uint32_t q_heads,
+                     float softmax_scale, uint32_t splits, void* d_ws, size_t ws_bytes, uint16_t* d_out,
+                     uint32_t* d_err, hlkv_stream_t stream) {
   if (pools == nullptr || !layout_ok(layout) || d_err == nullptr) return HLKV_INVALID_ARGUMENT;
   if (layout->head_dim != 64 && layout->head_dim != 128) return HLKV_INVALID_ARGUMENT;
   const uint32_t H = layout->kv_heads;
@@ -351,12 +386,21 @@ extern "C" int hlkv_decode_attention(const HlkvPools* pools, const HlkvLayout* l
   const uint32_t group = q_heads / H;
   if (group != 1 && group != 2 && group != 4 && group != 8) return HLKV_INVALID_ARGUMENT;
   if (!(softmax_scale > 0.0f) || !std::isfinite(softmax_scale)) return HLKV_INVALID_ARGUMENT;
+  if (splits == 0) return HLKV_INVALID_ARGUMENT;
   if (nseq == 0) return HLKV_OK;
   if (d_segs == nullptr || d_q == nullptr || d_out == nullptr ||
       (table_size > 0 && d_table == nullptr) || (arena_size > 0 && d_arena == nullptr)) {
     return HLKV_INVALID_ARGUMENT;
   }
-  if (uint64_t{nseq} * H > 0x7FFFFFFFull) return HLKV_INVALID_ARGUMENT;
+  if (uint64_t{nseq} * H * splits > 0x7FFFFFFFull || uint64_t{nseq} * q_heads > 0x7FFFFFFFull) {
+    return HLKV_INVALID_ARGUMENT;
+  }
+  if (splits > 1) {
+    if (d_ws == nullptr || (reinterpret_cast<uintptr_t>(d_ws) & 15u) != 0) return HLKV_INVALID_ARGUMENT;
+    if (ws_bytes < hlkv_decode_attention_workspace_bytes(nseq, H, layout->head_dim, splits)) {
+      return HLKV_BUFFER_TOO_SMALL;
+    }
+  }
   AttnParams p{};
   const uint64_t elems = uint64_t{2} * layout->block_tokens * H * layout->head_dim;
   for (int f = 0; f < 4; ++f) {
@@ -383,9 +427,50 @@ extern "C" int hlkv_decode_attention(const HlkvPools* pools, const HlkvLayout* l
   p.layout_id = layout->layout_id;
   p.q_heads = q_heads;
   p.qscale = softmax_scale * kLog2e;
+  p.splits = splits;
+  p.ws = splits > 1 ? static_cast<float*>(d_ws) : nullptr;
   const cudaStream_t s = reinterpret_cast<cudaStream_t>(stream);
-  const unsigned grid = nseq * H;
-  const cudaError_t e = layout->head_dim == 64 ? launch_for_group<64>(group, p, grid, s)
-                                               : launch_for_group<128>(group, p, grid, s);
+  const unsigned grid = nseq * H * splits;
+  cudaError_t e = layout->head_dim == 64 ? launch_for_group<64>(group, p, grid, s)
+                                         : launch_for_group<128>(group, p, grid, s);
+  if (e == cudaSuccess && splits > 1) {
+    if (layout->head_dim == 64) {
+      decode_attention_merge<64><<<nseq * q_heads, 64, 0, s>>>(p.ws, splits, H, group, q_heads, d_out);
+    } else {
+      decode_attention_merge<128><<<nseq * q_heads, 128, 0, s>>>(p.ws, splits, H, group, q_heads, d_out);
+    }
+    e = cudaGetLastError();
+  }
   return cuda_status(e);
+}
+
+}  // namespace hlkv
+
+extern "C" size_t hlkv_decode_attention_workspace_bytes(uint32_t nseq, uint32_t kv_heads, uint32_t head_dim,
+                                                        uint32_t splits) {
+  if (head_dim != 64 && head_dim != 128) return 0;
+  const uint64_t part = head_dim == 64 ? hlkv::kPart<64> : hlkv::kPart<128>;
+  return splits <= 1 ? 0 : static_cast<size_t>(uint64_t{nseq} * kv_heads * splits * part * sizeof(float));
+}
+
+extern "C" int hlkv_decode_attention(const HlkvPools* pools, const HlkvLayout* layout,
+                                     const HlkvExecDescriptor* d_table, uint32_t table_size,
+                                     const uint32_t* d_arena, uint32_t arena_size,
+                                     const HlkvSegment* d_segs, uint32_t nseq, const uint16_t* d_q,
+                                     uint32_t q_heads, float softmax_scale, uint16_t* d_out,
+                                     uint32_t* d_err, hlkv_stream_t stream) {
+  return hlkv::launch_attention(pools, layout, d_table, table_size, d_arena, arena_size, d_segs, nseq, d_q,
+                                q_heads, softmax_scale, 1, nullptr, 0, d_out, d_err, stream);
+}
+
+extern "C" int hlkv_decode_attention_split(const HlkvPools* pools, const HlkvLayout* layout,
+                                           const HlkvExecDescriptor* d_table, uint32_t table_size,
+                                           const uint32_t* d_arena, uint32_t arena_size,
+                                           const HlkvSegment* d_segs, uint32_t nseq, const uint16_t* d_q,
+                                           uint32_t q_heads, float softmax_scale, uint32_t splits,
+                                           void* d_workspace, size_t workspace_bytes, uint16_t* d_out,
+                                           uint32_t* d_err, hlkv_stream_t stream) {
+  return hlkv::launch_attention(pools, layout, d_table, table_size, d_arena, arena_size, d_segs, nseq, d_q,
+                                q_heads, softmax_scale, splits, d_workspace, workspace_bytes, d_out, d_err,
+                                stream);
 }

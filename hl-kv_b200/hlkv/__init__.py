@@ -133,6 +133,9 @@ SIGNATURES: list[tuple[str, object, list]] = [
                                    _vp, _vp, _vp]),
     ("hlkv_decode_attention", _int, [_P(Pools), _P(Layout), _vp, _u32, _vp, _u32, _vp, _u32, _vp,
                                      _u32, C.c_float, _vp, _vp, _vp]),
+    ("hlkv_decode_attention_workspace_bytes", _sz, [_u32, _u32, _u32, _u32]),
+    ("hlkv_decode_attention_split", _int, [_P(Pools), _P(Layout), _vp, _u32, _vp, _u32, _vp, _u32, _vp,
+                                           _u32, C.c_float, _u32, _vp, _sz, _vp, _vp, _vp]),
     ("hlkv_transcode", _int, [_P(Pools), _P(Layout), _vp, _u32, _vp, _vp]),
     ("hlkv_append_encode", _int, [_P(Pools), _P(Layout), _vp, _u32, _vp, _u32, _vp, _vp, _vp]),
     ("hlkv_apply_delta", _int, [_vp, _u32, _vp, _u32, _vp, _u32, _vp, _u32, _vp, _vp]),
@@ -510,6 +513,25 @@ def decode_attention(pools: Pools, layout: Layout, table_ptr: int, table_size: i
                                      arena_ptr or None, arena_size, _ptr(segs), nseq, _ptr(q), q_heads,
                                      softmax_scale, _ptr(out), _ptr(err), _stream_handle(stream))
     check(st, "hlkv_decode_attention")
+    return st
+
+
+def decode_attention_workspace_bytes(nseq: int, kv_heads: int, head_dim: int, splits: int) -> int:
+    return lib().hlkv_decode_attention_workspace_bytes(nseq, kv_heads, head_dim, splits)
+
+
+def decode_attention_split(pools: Pools, layout: Layout, table_ptr: int, table_size: int, arena_ptr: int,
+                           arena_size: int, segs, q, q_heads: int, softmax_scale: float, splits: int,
+                           workspace, out, err, stream=None) -> int:
+    """Split-KV decode attention; workspace: a device tensor of at least
+    decode_attention_workspace_bytes(...) bytes (or None when splits == 1)."""
+    nseq = int(segs.shape[0])
+    ws_bytes = 0 if workspace is None else workspace.numel() * workspace.element_size()
+    st = lib().hlkv_decode_attention_split(C.byref(pools), C.byref(layout), table_ptr or None, table_size,
+                                           arena_ptr or None, arena_size, _ptr(segs), nseq, _ptr(q), q_heads,
+                                           softmax_scale, splits, _ptr(workspace), ws_bytes, _ptr(out),
+                                           _ptr(err), _stream_handle(stream))
+    check(st, "hlkv_decode_attention_split")
     return st
 
 

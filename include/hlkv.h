@@ -211,6 +211,24 @@ int hlkv_decode_attention(const HlkvPools* pools, const HlkvLayout* layout,
                           uint32_t nseq, const uint16_t* d_q, uint32_t q_heads, float softmax_scale,
                           uint16_t* d_out, uint32_t* d_err, hlkv_stream_t stream);
 
+/*
+ * The same attention with each (sequence, KV head) split over `splits` CTAs, each taking a
+ * contiguous share of the sequence's blocks: for few or long sequences, where one CTA per
+ * (sequence, KV head) leaves SMs idle.  Each CTA writes its partial max, sum and outputs to
+ * d_workspace (caller-owned, 16-byte aligned, at least
+ * hlkv_decode_attention_workspace_bytes(nseq, kv_heads, head_dim, splits) bytes); a second
+ * launch merges them.  splits == 1 needs no workspace and equals hlkv_decode_attention.
+ * Calls that overlap on the GPU must not share a workspace.
+ */
+size_t hlkv_decode_attention_workspace_bytes(uint32_t nseq, uint32_t kv_heads, uint32_t head_dim,
+                                             uint32_t splits);
+int hlkv_decode_attention_split(const HlkvPools* pools, const HlkvLayout* layout,
+                                const HlkvExecDescriptor* d_table, uint32_t table_size,
+                                const uint32_t* d_arena, uint32_t arena_size, const HlkvSegment* d_segs,
+                                uint32_t nseq, const uint16_t* d_q, uint32_t q_heads, float softmax_scale,
+                                uint32_t splits, void* d_workspace, size_t workspace_bytes,
+                                uint16_t* d_out, uint32_t* d_err, hlkv_stream_t stream);
+
 /* ---- format-change transcode ------------------------------------------------------------ */
 typedef struct {
   uint32_t from_format; /* the block's current format and slot ...                  */

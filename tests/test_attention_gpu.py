@@ -90,3 +90,53 @@ def test_attention_rejects_bad_arguments(hlkv_lib, cuda_device):
                        (8, 1.0, hlkv.Layout(16, 8, 256, 1))):
         assert L.hlkv_decode_attention(C.byref(pools), C.byref(l2), None, 0, None, 0, C.c_void_p(8), 1,
                                        C.c_void_p(8), qh, sc, C.c_void_p(8), err, None) == hlkv.INVALID_ARGUMENT
+
+
+@pytest.mark.parametrize("splits", [2, 3, 7, 64])
+def test_split_attention_matches_oracle(hlkv_lib, oracle, cuda_device, splits):
+    """Split-KV attention (partials in a caller workspace, then a merge launch) against the same
+    oracle; splits beyond a sequence's block count leave empty shares."""
+    import torch
+    from hlkv.workload import build_workload, mixed_formats
+    T, H, D, group = 16, 4, 128, 2
+    fm = mixed_formats(4, [1, 23, 9, 40], probs=(0.25, 0.35, 0.15, 0.25), seed=splits)
+    rng = np.random.default_rng(splits)
+    vt = [[T] * (len(r) - 1) + [int(rng.integers(1, T + 1))] for r in fm]
+    wl = build_workload(fm, T=T, H=H, D=D, seed=splits, valid_tokens=vt)
+    qh = H * group
+    q = rng.standard_normal((4, qh, D)).astype(np.float16)
+    ws = torch.empty(hlkv_lib.decode_attention_workspace_bytes(4, H, D, splits), dtype=torch.uint8,
+                     device="cuda")
+    outs = []
+    for call in range(2):  # two calls in a row on the same workspace
+        out = torch.full((4, qh, D), 0x7777, dtype=torch.int32, device="cuda").to(torch.int16)
+        err = torch.zeros(1, dtype=torch.int32, device="cuda")
+        hlkv_lib.decode_attention_split(wl.hlkv_pools(), wl.layout, wl.dt.table_ptr, wl.dt.table_size,
+                                        wl.dt.arena_ptr, wl.dt.arena_size, wl.segs,
+                                        torch.from_numpy(q.view(np.int16)).cuda(), qh, 0.1, splits, ws,
+                                        out, err)
+        torch.cuda.synchronize()
+        assert int(err.item()) == 0
+        outs.append(out.cpu().numpy().view(np.float16).astype(np.float64))
+    assert np.array_equal(outs[0], outs[1])
+    want, oerr = oracle_attention(oracle, wl, q.astype(np.float64), 0.1)
+    assert oerr == 0
+    _close(outs[0], want, vscale=20.0)
+
+
+def test_split_attention_workspace_checks(hlkv_lib, cuda_device):
+    import ctypes as C
+    import hlkv
+    lay = hlkv.Layout(16, 8, 128, 1)
+    pools = hlkv.Pools()
+    L = hlkv.lib()
+    need = hlkv_lib.decode_attention_workspace_bytes(2, 8, 128, 4)
+    assert need == 2 * 8 * 4 * (16 + 8 * 128) * 4
+    assert hlkv_lib.decode_attention_workspace_bytes(2, 8, 128, 1) == 0
+    args = lambda splits, ws, nbytes: (C.byref(pools), C.byref(lay), None, 0, None, 0, C.c_void_p(16), 2,
+                                       C.c_void_p(16), 32, 0.1, splits, ws, nbytes, C.c_void_p(16),
+                                       C.c_void_p(16), None)
+    assert L.hlkv_decode_attention_split(*args(4, C.c_void_p(256), need - 1)) == hlkv.BUFFER_TOO_SMALL
+    assert L.hlkv_decode_attention_split(*args(4, None, need)) == hlkv.INVALID_ARGUMENT
+    assert L.hlkv_decode_attention_split(*args(4, C.c_void_p(264), need)) == hlkv.INVALID_ARGUMENT
+    assert L.hlkv_decode_attention_split(*args(0, C.c_void_p(256), need)) == hlkv.INVALID_ARGUMENT
