@@ -22,6 +22,7 @@
 
 #include <cmath>
 #include <cstdint>
+#include <mutex>
 
 #include "codec.cuh"
 #include "common.cuh"
@@ -473,4 +474,76 @@ extern "C" int hlkv_decode_attention_split(const HlkvPools* pools, const HlkvLay
   return hlkv::launch_attention(pools, layout, d_table, table_size, d_arena, arena_size, d_segs, nseq, d_q,
                                 q_heads, softmax_scale, splits, d_workspace, workspace_bytes, d_out, d_err,
                                 stream);
+}
+
+// ---- split attention without a caller workspace -------------------------------------------
+//
+// For callers that cannot allocate device memory when they call: hosts that bind this C ABI
+// with no device allocator of their own (a cgo or plain C serving loop has no caching
+// allocator to draw a workspace from), and engines that reserve all free HBM for their KV
+// pools at start-up, so that a later cudaMalloc fails.  cudaMalloc and cudaFree are also not
+// stream-ordered: a pair of them around every decode step would serialize the step against
+// all other work in flight on the device.  These callers get the split partials in a fixed
+// scratch array that is part of this library's device image instead.
+
+namespace {
+
+// HLKV_NOALLOC_SCRATCH_BYTES (16 MiB) of split partials per device: at head_dim 128 that is
+// 4033 CTAs of partials, e.g. 16 sequences x 8 KV heads x 31 splits.
+static __device__ __align__(256) unsigned char g_noalloc_scratch[HLKV_NOALLOC_SCRATCH_BYTES];
+
+constexpr int kNoallocDevices = 64;
+std::mutex g_noalloc_mu;
+void* g_noalloc_ptr[kNoallocDevices] = {};
+
+// The scratch's address on the current device.  The first call on each device looks it up
+// with cudaGetSymbolAddress, with that device current, and caches it; later calls only read
+// the cache.
+int noalloc_scratch(void** out) {
+  int dev = -1;
+  cudaError_t e = cudaGetDevice(&dev);
+  if (e != cudaSuccess) return hlkv::cuda_status(e);
+  if (dev < 0 || dev >= kNoallocDevices) return HLKV_INVALID_ARGUMENT;
+  std::lock_guard<std::mutex> lock(g_noalloc_mu);
+  if (g_noalloc_ptr[dev] == nullptr) {
+    void* ptr = nullptr;
+    e = cudaGetSymbolAddress(&ptr, g_noalloc_scratch);
+    if (e != cudaSuccess) return hlkv::cuda_status(e);
+    if (ptr == nullptr || (reinterpret_cast<uintptr_t>(ptr) & 255u) != 0) {
+      return hlkv::cuda_status(cudaErrorInvalidSymbol);
+    }
+    g_noalloc_ptr[dev] = ptr;
+  }
+  *out = g_noalloc_ptr[dev];
+  return HLKV_OK;
+}
+
+}  // namespace
+
+// Nothing in the scratch has to start at zero, so nothing is cleared: every CTA of the split
+// launch writes its whole partial (max, sum and outputs; -inf, 0 and 0 for an empty share)
+// before the merge launch reads it.  All calls on one device share the one scratch, so calls
+// that overlap on the GPU (on different streams, unordered) race on it.
+extern "C" int hlkv_decode_attention_split_noalloc(const HlkvPools* pools, const HlkvLayout* layout,
+                                                   const HlkvExecDescriptor* d_table, uint32_t table_size,
+                                                   const uint32_t* d_arena, uint32_t arena_size,
+                                                   const HlkvSegment* d_segs, uint32_t nseq,
+                                                   const uint16_t* d_q, uint32_t q_heads,
+                                                   float softmax_scale, uint32_t splits, uint16_t* d_out,
+                                                   uint32_t* d_err, hlkv_stream_t stream) {
+  if (layout != nullptr && splits > 1 && nseq > 0) {
+    const uint64_t units = uint64_t{nseq} * layout->kv_heads;
+    // Grids of 2^31 CTAs or more are rejected by launch_attention; below that the size fits.
+    if (units <= 0x7FFFFFFFull && units * splits <= 0x7FFFFFFFull &&
+        hlkv_decode_attention_workspace_bytes(nseq, layout->kv_heads, layout->head_dim, splits) >
+            HLKV_NOALLOC_SCRATCH_BYTES) {
+      return HLKV_BUFFER_TOO_SMALL;
+    }
+  }
+  void* scratch = nullptr;
+  const int st = noalloc_scratch(&scratch);
+  if (st != HLKV_OK) return st;
+  return hlkv::launch_attention(pools, layout, d_table, table_size, d_arena, arena_size, d_segs, nseq, d_q,
+                                q_heads, softmax_scale, splits, scratch, HLKV_NOALLOC_SCRATCH_BYTES, d_out,
+                                d_err, stream);
 }

@@ -136,6 +136,8 @@ SIGNATURES: list[tuple[str, object, list]] = [
     ("hlkv_decode_attention_workspace_bytes", _sz, [_u32, _u32, _u32, _u32]),
     ("hlkv_decode_attention_split", _int, [_P(Pools), _P(Layout), _vp, _u32, _vp, _u32, _vp, _u32, _vp,
                                            _u32, C.c_float, _u32, _vp, _sz, _vp, _vp, _vp]),
+    ("hlkv_decode_attention_split_noalloc", _int, [_P(Pools), _P(Layout), _vp, _u32, _vp, _u32, _vp,
+                                                   _u32, _vp, _u32, C.c_float, _u32, _vp, _vp, _vp]),
     ("hlkv_transcode", _int, [_P(Pools), _P(Layout), _vp, _u32, _vp, _vp]),
     ("hlkv_append_encode", _int, [_P(Pools), _P(Layout), _vp, _u32, _vp, _u32, _vp, _vp, _vp]),
     ("hlkv_apply_delta", _int, [_vp, _u32, _vp, _u32, _vp, _u32, _vp, _u32, _vp, _vp]),
@@ -532,6 +534,23 @@ def decode_attention_split(pools: Pools, layout: Layout, table_ptr: int, table_s
                                            softmax_scale, splits, _ptr(workspace), ws_bytes, _ptr(out),
                                            _ptr(err), _stream_handle(stream))
     check(st, "hlkv_decode_attention_split")
+    return st
+
+
+NOALLOC_SCRATCH_BYTES = 16 << 20  # HLKV_NOALLOC_SCRATCH_BYTES
+
+
+def decode_attention_split_noalloc(pools: Pools, layout: Layout, table_ptr: int, table_size: int,
+                                   arena_ptr: int, arena_size: int, segs, q, q_heads: int,
+                                   softmax_scale: float, splits: int, out, err, stream=None) -> int:
+    """Split-KV decode attention with the partials in the library's fixed per-device scratch
+    (NOALLOC_SCRATCH_BYTES); no workspace argument and no allocation."""
+    nseq = int(segs.shape[0])
+    st = lib().hlkv_decode_attention_split_noalloc(C.byref(pools), C.byref(layout), table_ptr or None,
+                                                   table_size, arena_ptr or None, arena_size, _ptr(segs),
+                                                   nseq, _ptr(q), q_heads, softmax_scale, splits, _ptr(out),
+                                                   _ptr(err), _stream_handle(stream))
+    check(st, "hlkv_decode_attention_split_noalloc")
     return st
 
 

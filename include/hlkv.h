@@ -229,6 +229,28 @@ int hlkv_decode_attention_split(const HlkvPools* pools, const HlkvLayout* layout
                                 uint32_t splits, void* d_workspace, size_t workspace_bytes,
                                 uint16_t* d_out, uint32_t* d_err, hlkv_stream_t stream);
 
+/*
+ * hlkv_decode_attention_split with its partials in a fixed scratch array of this library
+ * (HLKV_NOALLOC_SCRATCH_BYTES per device, part of its device image) instead of a caller
+ * workspace: for callers that cannot allocate device memory when they call (a host binding
+ * this ABI with no device allocator of its own; an engine that gave all free HBM to its KV
+ * pools).  No counterpart in the reference.  The call allocates nothing.
+ * - A split whose workspace (hlkv_decode_attention_workspace_bytes) exceeds
+ *   HLKV_NOALLOC_SCRATCH_BYTES is rejected with HLKV_BUFFER_TOO_SMALL; nothing is launched.
+ * - The scratch of the current device is used (the stream must belong to it).  The first call
+ *   on each device looks up the scratch's address (cudaGetSymbolAddress) and caches it; make
+ *   that first call before any stream capture.
+ * - All calls on a device share the scratch: calls that overlap on the GPU race.  Order them
+ *   (one stream, or events).
+ */
+#define HLKV_NOALLOC_SCRATCH_BYTES (16u << 20)
+int hlkv_decode_attention_split_noalloc(const HlkvPools* pools, const HlkvLayout* layout,
+                                        const HlkvExecDescriptor* d_table, uint32_t table_size,
+                                        const uint32_t* d_arena, uint32_t arena_size,
+                                        const HlkvSegment* d_segs, uint32_t nseq, const uint16_t* d_q,
+                                        uint32_t q_heads, float softmax_scale, uint32_t splits,
+                                        uint16_t* d_out, uint32_t* d_err, hlkv_stream_t stream);
+
 /* ---- format-change transcode ------------------------------------------------------------ */
 typedef struct {
   uint32_t from_format; /* the block's current format and slot ...                  */
