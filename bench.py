@@ -592,6 +592,8 @@ def run_decode(args) -> None:
     rows_in = 2 * H * D * 2
     enc_out = {int(hlkv.FP8_E4M3): 2 * H * D + 2 * H * 4, int(hlkv.INT4): 2 * H * D // 2 + 2 * H * 8}
     ev = [[torch.cuda.Event(enable_timing=True) for _ in range(3)] for _ in range(steps_total)]
+    for e in ev:
+        e[1].record(stream)  # torch creates the CUDA event at its first record
     host = {"table_s": 0.0, "sync_s": 0.0}
     nbytes = {"encode": 0, "delta": 0}
 
@@ -608,13 +610,11 @@ def run_decode(args) -> None:
         dt.collect(table)  # host half of the delta protocol: nothing queued on the GPU yet
         h2 = time.perf_counter()
         ev[k][0].record(stream)
-        d_targets[b].copy_(pinned[b], non_blocking=True)
-        copied[b].record(stream)
-        dt.flush(stream)  # upload + kernel (3)
-        ev[k][1].record(stream)
-        hlkv.append_encode(pools, layout, dt.table_ptr, dt.table_size, d_targets[b], tokens[k % 4],
-                           err, stream=stream)
+        # targets H2D, delta upload + kernel (3), ev[k][1], kernel (2): one native call
+        hlkv.decode_step_queue(dt, pools, layout, pinned[b], d_targets[b], tokens[k % 4], err,
+                               encode_event=ev[k][1], stream=stream)
         ev[k][2].record(stream)
+        copied[b].record(stream)
         tail_fmt = np.where(tg[:, 1] == 0, new_fmt[k], tail_fmt)
         if timed:
             host["table_s"] += h1 - h0
@@ -677,8 +677,9 @@ def run_decode(args) -> None:
                          "launch_ms": round(enc_mean, 5)},
             "e2e": {"value": round(job_bytes * args.steps / (wall_ms / 1e3) / 1e9, 2), "unit": "GB/s",
                     "h2d_bytes_per_step": n * 8, "d2h_bytes_per_step": 0,
-                    "path": "host table ops + collect_delta -> H2D of targets and delta -> "
-                            "apply_delta -> append_encode, wall clock per step (tokens resident)"},
+                    "path": "host table ops + collect_delta -> hlkv_decode_step_queue (H2D of "
+                            "targets and delta -> apply_delta -> append_encode), wall clock per step "
+                            "(tokens resident)"},
             "gpu_launches": 2 * args.steps,  # apply_delta + append_encode per step
             "clocks": clocks.summary(c0, c1),
             "cpu_baseline": cpu,

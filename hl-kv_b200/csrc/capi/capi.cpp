@@ -345,6 +345,34 @@ int hlkv_device_tables_flush(hlkv_device_tables* dt, hlkv_stream_t stream) {
   return static_cast<int>(dt->dt.flush(reinterpret_cast<cudaStream_t>(stream)).status);
 }
 
+int hlkv_decode_step_queue(hlkv_device_tables* dt, const HlkvPools* pools, const HlkvLayout* layout,
+                           const HlkvAppendTarget* h_targets, HlkvAppendTarget* d_targets, uint32_t n,
+                           const uint16_t* d_tokens, uint32_t* d_err, void* encode_event,
+                           hlkv_stream_t stream) {
+  if (dt == nullptr || pools == nullptr || layout == nullptr || d_err == nullptr) return HLKV_INVALID_ARGUMENT;
+  if (n > 0 && (h_targets == nullptr || d_targets == nullptr || d_tokens == nullptr)) {
+    return HLKV_INVALID_ARGUMENT;
+  }
+  const cudaStream_t s = reinterpret_cast<cudaStream_t>(stream);
+  // Kernel (3) copies the targets while it applies the delta, reading h_targets in place
+  // (page-locked host memory is device-readable at its device address): no upload copy.
+  const void* src = nullptr;
+  if (n > 0) {
+    cudaPointerAttributes attr{};
+    if (cudaPointerGetAttributes(&attr, h_targets) != cudaSuccess || attr.devicePointer == nullptr) {
+      (void)cudaGetLastError();
+      return HLKV_INVALID_ARGUMENT;  // pageable memory: not readable by a kernel
+    }
+    src = attr.devicePointer;
+  }
+  if (const int f = static_cast<int>(dt->dt.flush(s, src, d_targets, n).status); f != HLKV_OK) return f;
+  if (encode_event != nullptr) {
+    if (cudaEventRecord(static_cast<cudaEvent_t>(encode_event), s) != cudaSuccess) return HLKV_CUDA_ERROR;
+  }
+  return hlkv_append_encode(pools, layout, hlkv_device_tables_table(dt), dt->dt.table_size(), d_targets, n,
+                            d_tokens, d_err, stream);
+}
+
 const HlkvExecDescriptor* hlkv_device_tables_table(const hlkv_device_tables* dt) {
   return reinterpret_cast<const HlkvExecDescriptor*>(dt->dt.table());
 }

@@ -7,9 +7,12 @@
 // values of the inputs, stored at row (kv*T + token)*H + h of the block's
 // layout (codes first, then the per-row parameters).
 //
-// A row is handled by D/8 lanes (16 for D = 128), 8 elements per lane from one
-// 16-byte load; the per-row encode (group statistics by shuffle reductions, the
-// reference's scale rules, RNE codes) is dev::encode_row in row_encode.cuh.
+// A row is handled by D/16 lanes (8 for D = 128), 16 elements per lane from two
+// 16-byte loads (chunks l and l + D/16 of the row, so each warp-wide load is
+// contiguous); the per-row encode (group statistics by shuffle reductions, the
+// reference's scale rules, RNE codes) is dev::encode_row in row_encode.cuh.  Two
+// chunks per lane halve the per-row work (target and descriptor loads and checks,
+// index arithmetic, scale division) per element against one chunk per lane.
 #include <cuda_runtime.h>
 
 #include <cstdint>
@@ -42,12 +45,14 @@ struct Params {
   uint32_t table_size, T, H, layout_id;
 };
 
+constexpr int kChunks = 2;  // 8-value chunks per lane
+
 template <int kD>
 __global__ void __launch_bounds__(kThreads) append_encode_kernel(const Params p) {
-  constexpr int kLanes = kD / 8;
+  constexpr int kLanes = kD / (8 * kChunks);
   constexpr int kRowsPerIter = kThreads / kLanes;
   const uint32_t lane = threadIdx.x % kLanes;
-  const uint32_t mask = dev::row_mask<kD>();
+  const uint32_t mask = dev::row_mask<kD, kChunks>();
   for (uint32_t g = blockIdx.x * kRowsPerIter + threadIdx.x / kLanes; g < p.rows_total;
        g += gridDim.x * kRowsPerIter) {
     // Everything below is uniform over the lanes of row g.
@@ -57,7 +62,9 @@ __global__ void __launch_bounds__(kThreads) append_encode_kernel(const Params p)
 
     // The token row does not depend on the descriptor: both loads go out together.
     const uint2 t = __ldg(p.targets + k);
-    const uint4 raw = __ldcs(p.tokens + uint64_t{g} * kLanes + lane);
+    uint4 raw[kChunks];
+#pragma unroll
+    for (int c = 0; c < kChunks; ++c) raw[c] = __ldcs(p.tokens + uint64_t{g} * (kD / 8) + c * kLanes + lane);
     uint32_t bad = 0, f = 0, slot = 0;
     const uint32_t id = t.x, tok = t.y;
     if (id >= p.table_size) {
@@ -82,7 +89,7 @@ __global__ void __launch_bounds__(kThreads) append_encode_kernel(const Params p)
 
     const uint32_t row = (kv * p.T + tok) * p.H + h;
     uint8_t* payload = p.pool[f].base + uint64_t{slot} * p.pool[f].slot_bytes;
-    const uint32_t e = dev::encode_row<kD>(f, raw, lane, mask, payload, row, p.code_bytes[f]);
+    const uint32_t e = dev::encode_row<kD, kChunks>(f, raw, lane, mask, payload, row, p.code_bytes[f]);
     if (e != 0 && lane == 0) atomicOr(p.err, e);
   }
 }
@@ -127,7 +134,7 @@ extern "C" int hlkv_append_encode(const HlkvPools* pools, const HlkvLayout* layo
   p.H = layout->kv_heads;
   p.layout_id = layout->layout_id;
   const cudaStream_t s = reinterpret_cast<cudaStream_t>(stream);
-  const int lanes = static_cast<int>(layout->head_dim / 8);
+  const int lanes = static_cast<int>(layout->head_dim / (8 * kChunks));
   const uint64_t rows_per_cta = kThreads / lanes;
   const uint64_t want = (p.rows_total + rows_per_cta - 1) / rows_per_cta;
   const uint64_t cap = uint64_t{static_cast<uint32_t>(sm_count())} * 16;

@@ -99,7 +99,8 @@ __global__ void __launch_bounds__(kThreads) transcode_kernel(const Params p) {
       }
     }
     uint8_t* dst = p.pool[tf].base + uint64_t{ts} * p.pool[tf].slot_bytes;
-    const uint32_t e = dev::encode_row<kD>(tf, raw, lane, mask, dst, r, p.code_bytes[tf]);
+    const uint4 chunk[1] = {raw};
+    const uint32_t e = dev::encode_row<kD>(tf, chunk, lane, mask, dst, r, p.code_bytes[tf]);
     if (e != 0 && lane == 0) atomicOr(p.err, e);
   }
 }

@@ -10,6 +10,10 @@
 
 namespace hlkv {
 int cuda_status(cudaError_t e) noexcept;
+int launch_apply_delta(uint4* table, uint32_t table_size, uint32_t* arena, uint32_t arena_size,
+                       const uint4* desc, uint32_t n_desc, const uint2* ids, uint32_t n_id,
+                       const uint2* copy_src, uint2* copy_dst, uint32_t n_copy, uint32_t* err,
+                       cudaStream_t s);
 }
 
 namespace hl::kv {
@@ -63,7 +67,6 @@ DeviceTables::~DeviceTables() {
   if (d_table_ != nullptr) (void)cudaFree(d_table_);
   if (d_arena_ != nullptr) (void)cudaFree(d_arena_);
   if (d_err_ != nullptr) (void)cudaFree(d_err_);
-  if (d_staging_ != nullptr) (void)cudaFree(d_staging_);
   if (h_staging_ != nullptr) (void)cudaFreeHost(h_staging_);
 }
 
@@ -79,13 +82,17 @@ DeviceStatus DeviceTables::stage(const alloc::ExecDelta& delta) {
   if (bytes > staging_bytes_) {
     std::size_t cap = staging_bytes_ == 0 ? std::size_t{64} << 10 : staging_bytes_;
     while (cap < bytes) cap *= 2;
-    if (d_staging_ != nullptr) (void)cudaFree(d_staging_);
     if (h_staging_ != nullptr) (void)cudaFreeHost(h_staging_);
-    d_staging_ = nullptr;
     h_staging_ = nullptr;
+    staging_dev_ = nullptr;
     staging_bytes_ = 0;
     if (const cudaError_t e = cudaMallocHost(&h_staging_, cap); e != cudaSuccess) return from_cuda(e);
-    if (const cudaError_t e = cudaMalloc(&d_staging_, cap); e != cudaSuccess) return from_cuda(e);
+    // Kernel (3) reads the staged patches in place: the device address of the pinned
+    // buffer (its host address under unified addressing).
+    cudaPointerAttributes attr{};
+    if (const cudaError_t e = cudaPointerGetAttributes(&attr, h_staging_); e != cudaSuccess) return from_cuda(e);
+    if (attr.devicePointer == nullptr) return from_cuda(cudaErrorNotSupported);
+    staging_dev_ = attr.devicePointer;
     staging_bytes_ = cap;
   }
   auto* h = static_cast<unsigned char*>(h_staging_);
@@ -125,35 +132,60 @@ DeviceStatus DeviceTables::collect(alloc::HeteroBlockTable& table) {
   return stage(delta_);
 }
 
-DeviceStatus DeviceTables::flush(cudaStream_t stream) {
-  if (!pending_) return {};
-  pending_ = false;
-  return upload_and_apply(delta_, stream);
+DeviceStatus DeviceTables::flush(cudaStream_t stream) { return flush(stream, nullptr, nullptr, 0); }
+
+DeviceStatus DeviceTables::flush(cudaStream_t stream, const void* copy_src, void* copy_dst,
+                                 std::uint32_t n_copy) {
+  if (pending_) {
+    pending_ = false;
+    return upload_and_apply(delta_, stream, copy_src, copy_dst, n_copy);
+  }
+  if (n_copy == 0) return {};
+  DeviceGuard g(device_);
+  if (!g.ok()) return from_cuda(cudaErrorInvalidDevice);
+  if (DeviceStatus s = ensure_error_word(stream); !s.ok()) return s;
+  return launch(nullptr, 0, nullptr, 0, copy_src, copy_dst, n_copy, stream);
 }
 
 DeviceStatus DeviceTables::apply(const alloc::ExecDelta& delta, cudaStream_t stream) {
   if (DeviceStatus s = stage(delta); !s.ok()) return s;
-  return upload_and_apply(delta, stream);
+  return upload_and_apply(delta, stream, nullptr, nullptr, 0);
 }
 
-DeviceStatus DeviceTables::upload_and_apply(const alloc::ExecDelta& delta, cudaStream_t stream) {
+DeviceStatus DeviceTables::ensure_error_word(cudaStream_t stream) {
+  if (d_err_ != nullptr) return {};
+  if (const cudaError_t e = device_alloc(&d_err_, sizeof(std::uint32_t)); e != cudaSuccess) {
+    d_err_ = nullptr;
+    return from_cuda(e);
+  }
+  if (const cudaError_t e = cudaMemsetAsync(d_err_, 0, sizeof(std::uint32_t), stream); e != cudaSuccess) {
+    return from_cuda(e);
+  }
+  if (const cudaError_t e = cudaEventCreateWithFlags(&staging_free_, cudaEventDisableTiming); e != cudaSuccess) {
+    staging_free_ = nullptr;
+    return from_cuda(e);
+  }
+  return {};
+}
+
+DeviceStatus DeviceTables::launch(const void* desc, std::uint32_t n_desc, const void* ids, std::uint32_t n_id,
+                                  const void* copy_src, void* copy_dst, std::uint32_t n_copy,
+                                  cudaStream_t stream) {
+  const int st = hlkv::launch_apply_delta(
+      reinterpret_cast<uint4*>(d_table_), table_size_, d_arena_, arena_size_, static_cast<const uint4*>(desc),
+      n_desc, static_cast<const uint2*>(ids), n_id, static_cast<const uint2*>(copy_src),
+      static_cast<uint2*>(copy_dst), n_copy, d_err_, stream);
+  if (st != HLKV_OK) {
+    return DeviceStatus{static_cast<QuantStatus>(st), static_cast<cudaError_t>(hlkv_last_cuda_error())};
+  }
+  return {};
+}
+
+DeviceStatus DeviceTables::upload_and_apply(const alloc::ExecDelta& delta, cudaStream_t stream,
+                                            const void* copy_src, void* copy_dst, std::uint32_t n_copy) {
   DeviceGuard g(device_);
   if (!g.ok()) return from_cuda(cudaErrorInvalidDevice);
-  if (d_err_ == nullptr) {
-    if (const cudaError_t e = device_alloc(&d_err_, sizeof(std::uint32_t)); e != cudaSuccess) {
-      d_err_ = nullptr;
-      return from_cuda(e);
-    }
-    if (const cudaError_t e = cudaMemsetAsync(d_err_, 0, sizeof(std::uint32_t), stream);
-        e != cudaSuccess) {
-      return from_cuda(e);
-    }
-    if (const cudaError_t e = cudaEventCreateWithFlags(&staging_free_, cudaEventDisableTiming);
-        e != cudaSuccess) {
-      staging_free_ = nullptr;
-      return from_cuda(e);
-    }
-  }
+  if (DeviceStatus s = ensure_error_word(stream); !s.ok()) return s;
   if (delta.descriptor_table_size != table_size_) {
     // A table has a fixed size; this happens once, on the first delta.
     if (const cudaError_t e = cudaStreamSynchronize(stream); e != cudaSuccess) return from_cuda(e);
@@ -170,8 +202,11 @@ DeviceStatus DeviceTables::upload_and_apply(const alloc::ExecDelta& delta, cudaS
     table_size_ = delta.descriptor_table_size;
   }
   if (delta.arena_size > arena_capacity_) {
+    // Room for a quarter more than asked, and at least double the old capacity, so that
+    // growth (an allocation, a copy and a stream drain) stays rare.
     std::uint64_t cap = arena_capacity_ == 0 ? 1024 : 2ull * arena_capacity_;
-    if (cap < delta.arena_size) cap = delta.arena_size;
+    const std::uint64_t want = std::uint64_t{delta.arena_size} + delta.arena_size / 4;
+    if (cap < want) cap = want;
     if (cap > 0xFFFFFFFFull) cap = 0xFFFFFFFFull;
     std::uint32_t* fresh = nullptr;
     if (const cudaError_t e = device_alloc(&fresh, cap * 4); e != cudaSuccess) return from_cuda(e);
@@ -193,22 +228,16 @@ DeviceStatus DeviceTables::upload_and_apply(const alloc::ExecDelta& delta, cudaS
   arena_size_ = delta.arena_size;
 
   const std::size_t n_desc = delta.descriptor_patches.size(), n_id = delta.id_patches.size();
-  const std::size_t bytes = 16 * n_desc + 8 * n_id;
-  if (bytes == 0) return {};
-  if (const cudaError_t e = cudaMemcpyAsync(d_staging_, h_staging_, bytes, cudaMemcpyHostToDevice, stream);
-      e != cudaSuccess) {
-    return from_cuda(e);
+  if (n_desc + n_id == 0) {
+    return n_copy == 0 ? DeviceStatus{} : launch(nullptr, 0, nullptr, 0, copy_src, copy_dst, n_copy, stream);
   }
-  auto* d = static_cast<unsigned char*>(d_staging_);
-  const int st = hlkv_apply_delta(
-      reinterpret_cast<HlkvExecDescriptor*>(d_table_), table_size_, d_arena_, arena_size_,
-      reinterpret_cast<const HlkvExecDescriptor*>(d), static_cast<std::uint32_t>(n_desc),
-      reinterpret_cast<const HlkvIdPatch*>(d + 16 * n_desc), static_cast<std::uint32_t>(n_id), d_err_,
-      reinterpret_cast<hlkv_stream_t>(stream));
-  if (st != HLKV_OK) {
-    return DeviceStatus{static_cast<QuantStatus>(st), static_cast<cudaError_t>(hlkv_last_cuda_error())};
+  auto* d = static_cast<const unsigned char*>(staging_dev_);
+  if (DeviceStatus s = launch(d, static_cast<std::uint32_t>(n_desc), d + 16 * n_desc,
+                              static_cast<std::uint32_t>(n_id), copy_src, copy_dst, n_copy, stream);
+      !s.ok()) {
+    return s;
   }
-  // Both staging buffers are free again once kernel (3) has run.
+  // The staging buffer is free again once kernel (3) has read it.
   if (const cudaError_t e = cudaEventRecord(staging_free_, stream); e != cudaSuccess) return from_cuda(e);
   return {};
 }

@@ -187,6 +187,7 @@ SIGNATURES: list[tuple[str, object, list]] = [
     ("hlkv_device_tables_sync", _int, [_vp, _vp, _vp]),
     ("hlkv_device_tables_collect", _int, [_vp, _vp]),
     ("hlkv_device_tables_flush", _int, [_vp, _vp]),
+    ("hlkv_decode_step_queue", _int, [_vp, _P(Pools), _P(Layout), _vp, _vp, _u32, _vp, _vp, _vp, _vp]),
     ("hlkv_device_tables_table", _vp, [_vp]),
     ("hlkv_device_tables_table_size", _u32, [_vp]),
     ("hlkv_device_tables_arena", _vp, [_vp]),
@@ -502,6 +503,19 @@ def append_encode(pools: Pools, layout: Layout, table_ptr: int, table_size: int,
     st = lib().hlkv_append_encode(C.byref(pools), C.byref(layout), table_ptr or None, table_size,
                                   _ptr(targets), n, _ptr(tokens), _ptr(err), _stream_handle(stream))
     check(st, "hlkv_append_encode")
+    return st
+
+
+def decode_step_queue(dt: "DeviceTables", pools: Pools, layout: Layout, h_targets, d_targets, tokens, err,
+                      encode_event=None, stream=None) -> int:
+    """Device half of a decode step, queued from native code: targets H2D (h_targets: pinned
+    host int32 [n, 2], as table.append_tokens wrote them), the collected delta's upload and
+    kernel (3), then kernel (2) into d_targets' blocks.  encode_event: a recorded
+    torch.cuda.Event (or None) to record just before kernel (2)."""
+    n = int(d_targets.shape[0])
+    st = lib().hlkv_decode_step_queue(dt.h, C.byref(pools), C.byref(layout), _ptr(h_targets), _ptr(d_targets),
+                                      n, _ptr(tokens), _ptr(err), encode_event, _stream_handle(stream))
+    check(st, "hlkv_decode_step_queue")
     return st
 
 

@@ -8,13 +8,15 @@
 // stream order on the caller's stream:
 //   1. table.collect_delta() on the host;
 //   2. grow the device arena when delta.arena_size exceeds its capacity (a
-//      larger allocation, the old contents copied device-to-device, then the
-//      old buffer freed after the stream drains); the descriptor table is
-//      allocated once at max_blocks entries;
-//   3. copy the patches into pinned staging and upload them;
-//   4. run kernel (3) (hlkv_apply_delta).
-// collect() is the host part (1 and the copy of 3) and flush() the queued part, so
-// host table work can run while the stream is busy.
+//      larger allocation with a quarter to spare, the old contents copied
+//      device-to-device, then the old buffer freed after the stream drains);
+//      the descriptor table is allocated once at max_blocks entries;
+//   3. copy the patches into pinned staging;
+//   4. run kernel (3) (hlkv_apply_delta), which reads the staged patches in
+//      place: under unified addressing a kernel reads page-locked host memory
+//      directly, so no upload copy is queued.
+// collect() is the host part (1 and 3) and flush() the queued part, so host table
+// work can run while the stream is busy.
 // Kernels issued later on the same stream see the updated tables.  One
 // DeviceTables per table and device, used from the table's first delta on;
 // not thread-safe (like the table).
@@ -44,9 +46,14 @@ class DeviceTables {
   /// copies them into pinned staging.  Queues nothing; it waits only until the previous
   /// flush's upload and kernel (3) are done with the staging buffers.
   [[nodiscard]] DeviceStatus collect(alloc::HeteroBlockTable& table);
-  /// Device half of sync(): queues the upload and kernel (3) for what collect()
-  /// gathered, on `stream`.  A no-op when nothing is pending.
+  /// Device half of sync(): queues kernel (3) for what collect() gathered, on
+  /// `stream`.  A no-op when nothing is pending.
   [[nodiscard]] DeviceStatus flush(cudaStream_t stream);
+  /// flush(stream), and the same kernel (3) launch copies n_copy 8-byte words from
+  /// copy_src (device-readable: device memory or page-locked host memory) to copy_dst
+  /// (device memory).  The decode step moves its append targets this way.
+  [[nodiscard]] DeviceStatus flush(cudaStream_t stream, const void* copy_src, void* copy_dst,
+                                   std::uint32_t n_copy);
   /// Uploads and applies an already collected delta.
   [[nodiscard]] DeviceStatus apply(const alloc::ExecDelta& delta, cudaStream_t stream);
 
@@ -59,7 +66,12 @@ class DeviceTables {
 
  private:
   [[nodiscard]] DeviceStatus stage(const alloc::ExecDelta& delta);
-  [[nodiscard]] DeviceStatus upload_and_apply(const alloc::ExecDelta& delta, cudaStream_t stream);
+  [[nodiscard]] DeviceStatus upload_and_apply(const alloc::ExecDelta& delta, cudaStream_t stream,
+                                              const void* copy_src, void* copy_dst, std::uint32_t n_copy);
+  [[nodiscard]] DeviceStatus ensure_error_word(cudaStream_t stream);
+  [[nodiscard]] DeviceStatus launch(const void* desc, std::uint32_t n_desc, const void* ids, std::uint32_t n_id,
+                                    const void* copy_src, void* copy_dst, std::uint32_t n_copy,
+                                    cudaStream_t stream);
 
   int device_ = 0;
   alloc::BlockExecDescriptor* d_table_ = nullptr;
@@ -68,10 +80,10 @@ class DeviceTables {
   std::uint32_t arena_size_ = 0;
   std::uint32_t arena_capacity_ = 0;
   std::uint32_t* d_err_ = nullptr;
-  void* h_staging_ = nullptr;   // pinned
-  void* d_staging_ = nullptr;
+  void* h_staging_ = nullptr;    // pinned
+  void* staging_dev_ = nullptr;  // its device address (not an allocation)
   std::size_t staging_bytes_ = 0;
-  cudaEvent_t staging_free_ = nullptr;  // recorded after kernel (3), the last reader of both buffers
+  cudaEvent_t staging_free_ = nullptr;  // recorded after kernel (3), the staging's reader
   alloc::ExecDelta delta_;    // collected, not yet flushed
   alloc::ExecDelta scratch_;  // the next collect_delta() before merging into delta_
   bool pending_ = false;

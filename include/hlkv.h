@@ -429,6 +429,23 @@ uint32_t hlkv_device_tables_arena_size(const hlkv_device_tables* dt);
 /* Device word the sync's kernel (3) reports into (zeroed at creation). */
 uint32_t* hlkv_device_tables_error_word(const hlkv_device_tables* dt);
 
+/*
+ * The device half of one decode step, two launches queued on `stream` from native code:
+ * kernel (3) applies the delta staged by hlkv_device_tables_collect (as
+ * hlkv_device_tables_flush) and, in the same launch, copies the n append targets that
+ * hlkv_table_append_tokens wrote to h_targets into d_targets; then encode_event (a
+ * cudaEvent_t, or NULL) is recorded and d_tokens[k] is encoded into target k through the
+ * device tables (hlkv_append_encode).  h_targets must be page-locked host memory (or device
+ * memory), which the kernel reads in place (HLKV_INVALID_ARGUMENT for pageable memory), and
+ * must stay untouched until the stream has passed kernel (3).  Returns the first failing
+ * status; what was queued before it stays queued.  No counterpart in the reference: the
+ * device side of the decode loop its plan describes.
+ */
+int hlkv_decode_step_queue(hlkv_device_tables* dt, const HlkvPools* pools, const HlkvLayout* layout,
+                           const HlkvAppendTarget* h_targets, HlkvAppendTarget* d_targets, uint32_t n,
+                           const uint16_t* d_tokens, uint32_t* d_err, void* encode_event,
+                           hlkv_stream_t stream);
+
 #ifdef __cplusplus
 }
 #endif

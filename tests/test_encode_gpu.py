@@ -125,3 +125,108 @@ def test_append_then_gather_round_trip(hlkv_lib, oracle, cuda_device):
     want, oerr = oracle_gather(oracle, wl)
     assert int(e.item()) == 0 and oerr == 0
     assert np.array_equal(out.cpu().numpy().view(np.uint16), want)
+
+
+@pytest.mark.parametrize("D", [64, 128, 256])
+def test_append_rejects_every_nonfinite_pattern(hlkv_lib, oracle, cuda_device, D):
+    """Rows holding +-Inf, +-NaN (quiet, signalling-pattern, all-ones) at positions in either
+    8-value chunk of a lane and either half of a word are rejected in E4M3, E5M2 and INT4
+    blocks; rows at the finite extremes (+-65504, the largest subnormal) are encoded."""
+    from hlkv.workload import build_workload
+    T, H = 4, 2
+    wl = build_workload([[1, 2, 3]], T=T, H=H, D=D, seed=D, outlier_channels=0)
+    ids = _all_ids(wl)
+    specials = [0x7C00, 0xFC00, 0x7E00, 0xFE00, 0x7C01, 0xFFFF, 0x7FFF, 0xFC01]
+    where = [0, 1, 9, D // 2 + 3, D - 1, D - 2, 16 + 7, D // 2 - 8]
+    targets = []
+    for bid in ids:
+        for t in range(T):
+            targets.append((bid, t))
+    targets = np.array(targets, dtype=np.uint32)
+    tokens = _tokens(len(targets), H, D, seed=D + 1)
+    bits = tokens.view(np.uint16)
+    rng = np.random.default_rng(D)
+    for k in range(len(targets)):
+        for kv in range(2):
+            for h in range(H):
+                r = (k * 2 + kv) * H + h
+                if r % 3 == 0:
+                    bits[k, kv, h, where[r % len(where)]] = specials[r % len(specials)]
+                elif r % 3 == 1:
+                    bits[k, kv, h, rng.integers(0, D)] = rng.choice([0x7BFF, 0xFBFF, 0x03FF, 0x83FF])
+    before = host_pools(wl)
+    table = device_table_words(wl)
+    err = _run(hlkv_lib, wl, targets, tokens)
+    oerr = oracle.append_encode(before, T, H, D, 1, table, targets, bits)
+    assert oerr == 1 << 9
+    assert err == oerr
+    after = host_pools(wl)
+    for f in before:
+        bad = np.nonzero(after[f][0] != before[f][0])[0]
+        assert bad.size == 0, f"format {f}: {bad.size} bytes differ, first at {bad[:4]}"
+
+
+def test_decode_step_queue_matches_oracle(hlkv_lib, oracle, cuda_device):
+    """hlkv_decode_step_queue over several decode steps (T = 4, so new blocks open): after
+    each step the device descriptor table mirrors the host table, every pool byte equals the
+    oracle's append of the same tokens at the same targets, and the final gather through the
+    device tables equals the oracle's."""
+    import torch
+    from helpers import oracle_gather
+    from hlkv.workload import build_workload
+    T, H, D = 4, 2, 128
+    wl = build_workload([[1, 3], [3], [1, 1, 3]], T=T, H=H, D=D, seed=11,
+                        valid_tokens=[[4, 1], [3], [4, 4, 0]], spare_slots=16)
+    n = len(wl.seqs)
+    h_targets = torch.empty((n, 2), dtype=torch.int32).pin_memory()
+    d_targets = torch.empty((n, 2), dtype=torch.int32, device="cuda")
+    err = torch.zeros(1, dtype=torch.int32, device="cuda")
+    rng = np.random.default_rng(12)
+    for step in range(9):
+        fm = rng.choice([1, 3], size=n).astype(np.uint32)
+        st, tg, done = wl.table.append_tokens(wl.seqs, fm, 1, out=h_targets.numpy().view(np.uint32))
+        assert st == 0 and done == n
+        targets = tg.copy()
+        tokens = _tokens(n, H, D, seed=100 + step)
+        before = host_pools(wl)
+        wl.dt.collect(wl.table)
+        hlkv_lib.decode_step_queue(wl.dt, wl.hlkv_pools(), wl.layout, h_targets, d_targets,
+                                   torch.from_numpy(tokens.view(np.int16).copy()).cuda(), err)
+        torch.cuda.synchronize()
+        assert int(err.item()) == 0
+        assert np.array_equal(d_targets.cpu().numpy().view(np.uint32), targets)
+        table = device_table_words(wl)
+        for s in wl.seqs:
+            for bid in wl.table.sequence_block_ids(s)[1]:
+                assert np.array_equal(table[bid], np.asarray(wl.table.device_descriptor(bid), np.uint32))
+        oerr = oracle.append_encode(before, T, H, D, 1, table, targets, tokens.view(np.uint16))
+        assert oerr == 0
+        after = host_pools(wl)
+        for f in before:
+            bad = np.nonzero(after[f][0] != before[f][0])[0]
+            assert bad.size == 0, f"step {step} format {f}: {bad.size} bytes differ"
+    import ctypes as C
+    import hlkv
+    from helpers import device_arena
+    # pageable host memory cannot be read by kernel (3): rejected before anything is queued
+    pageable = np.zeros((n, 2), np.uint32)
+    st = hlkv.lib().hlkv_decode_step_queue(wl.dt.h, C.byref(wl.hlkv_pools()), C.byref(wl.layout),
+                                           pageable.ctypes.data, d_targets.data_ptr(), n,
+                                           d_targets.data_ptr(), err.data_ptr(), None, None)
+    assert st == hlkv.INVALID_ARGUMENT
+    st, segs_host = wl.table.batch_segments(wl.seqs)
+    assert st == hlkv.Status.OK
+    wl.dt.sync(wl.table)
+    wl.segs_host = segs_host
+    wl.segs = torch.from_numpy(segs_host.astype(np.int32).reshape(-1, 2)).cuda()
+    arena = device_arena(wl)
+    for s, (off, ln) in zip(wl.seqs, segs_host):
+        assert list(arena[off:off + ln]) == list(wl.table.sequence_block_ids(s)[1])
+    out = torch.empty(wl.total_blocks * wl.block_elems, dtype=torch.int16, device="cuda")
+    e = torch.zeros(1, dtype=torch.int32, device="cuda")
+    hlkv_lib.gather_dequant(wl.hlkv_pools(), wl.layout, wl.dt.table_ptr, wl.dt.table_size,
+                            wl.dt.arena_ptr, wl.dt.arena_size, wl.segs, out, e)
+    torch.cuda.synchronize()
+    want, oerr = oracle_gather(oracle, wl)
+    assert int(e.item()) == 0 and oerr == 0
+    assert np.array_equal(out.cpu().numpy().view(np.uint16), want)
