@@ -366,6 +366,68 @@ Status HeteroBlockTable::release_sequence(SequenceHandle seq) {
   return Status::kOk;
 }
 
+Status HeteroBlockTable::append_tokens(std::span<const SequenceHandle> seqs,
+                                       std::span<const FormatId> new_formats, std::uint32_t layout,
+                                       std::span<TokenTarget> out, std::size_t& n_done) {
+  n_done = 0;
+  const std::size_t n = seqs.size();
+  if (new_formats.size() < n || out.size() < n) return Status::kInvalidArgument;
+  // Each sequence is a chain of dependent random reads (its Seq record, the arena entry of
+  // its tail, the tail's record and dirty flag).  Prefetches for sequences further ahead, one
+  // link of the chain per distance, keep several chains' misses in flight at once.
+  constexpr std::size_t kAheadSeq = 24, kAheadTail = 16, kAheadRecord = 8;
+  auto seq_at = [&](std::size_t k) -> const Seq* {
+    const std::uint32_t id = seqs[k].id;
+    return id < seqs_.size() ? &seqs_[id] : nullptr;
+  };
+  auto tail_of = [&](const Seq* q) -> const std::uint32_t* {
+    return q != nullptr && q->seg.capacity > 0 && q->seg.length > 0
+               ? arena_.view(q->seg).data() + (q->seg.length - 1)
+               : nullptr;
+  };
+  for (std::size_t i = 0; i < n; ++i) {
+    if (i + kAheadSeq < n) {
+      if (const Seq* q = seq_at(i + kAheadSeq)) __builtin_prefetch(q);
+    }
+    if (i + kAheadTail < n) {
+      if (const std::uint32_t* t = tail_of(seq_at(i + kAheadTail))) __builtin_prefetch(t);
+    }
+    if (i + kAheadRecord < n) {
+      if (const std::uint32_t* t = tail_of(seq_at(i + kAheadRecord)); t != nullptr && *t < records_.size()) {
+        __builtin_prefetch(&records_[*t], 1);
+        __builtin_prefetch(&is_dirty_[*t], 1);
+      }
+    }
+
+    const SequenceHandle sh = seqs[i];
+    if (const Status s = verify(sh); s != Status::kOk) return s;
+    if (const std::uint32_t* t = tail_of(&seqs_[sh.id]); t != nullptr) {
+      const std::uint32_t tail = *t;
+      // lookup(handle_of(tail)): a free (or out-of-range) tail is an invalid handle.
+      if (tail >= records_.size() || records_[tail].state() == BlockState::kFree) return Status::kInvalidHandle;
+      BlockDescriptor& d = records_[tail];
+      const std::uint32_t vt = d.exec.valid_tokens();
+      if (vt < block_tokens_) {
+        if (d.state() != BlockState::kOpen) return Status::kInvalidState;  // set_valid_tokens
+        d.exec.set_valid_tokens(vt + 1);
+        touch(tail);
+        out[i] = TokenTarget{tail, vt};
+        n_done = i + 1;
+        continue;
+      }
+    }
+    AllocRequest req;
+    req.format = new_formats[i];
+    req.valid_tokens = 1;
+    req.layout = layout;
+    const Result<BlockHandle> r = append_block(sh, req);
+    if (!r.ok()) return r.status();
+    out[i] = TokenTarget{r.value().id, 0};
+    n_done = i + 1;
+  }
+  return Status::kOk;
+}
+
 Result<std::span<const std::uint32_t>> HeteroBlockTable::sequence_block_ids(
     SequenceHandle seq) const {
   if (const Status s = verify(seq); s != Status::kOk) return s;

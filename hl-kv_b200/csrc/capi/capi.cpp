@@ -1,5 +1,6 @@
 // extern "C" layer of include/hlkv.h over the C++ host objects, and the C++
 // hl::quant::cuda entry points over the C kernels' launchers.
+#include <cstddef>
 #include <cstring>
 #include <new>
 #include <span>
@@ -25,6 +26,10 @@ struct hlkv_device_tables {
 static_assert(sizeof(HlkvExecDescriptor) == sizeof(BlockExecDescriptor));
 static_assert(sizeof(HlkvIdPatch) == sizeof(IdPatch));
 static_assert(sizeof(HlkvSegment) == sizeof(SequenceSegment));
+static_assert(sizeof(HlkvHandle) == sizeof(SequenceHandle) && offsetof(HlkvHandle, generation) ==
+                                                                  offsetof(SequenceHandle, generation));
+static_assert(sizeof(HlkvAppendTarget) == sizeof(TokenTarget) &&
+              offsetof(HlkvAppendTarget, token) == offsetof(TokenTarget, token));
 static_assert(static_cast<int>(Status::kCapacityExceeded) == HLKV_STATUS_CAPACITY_EXCEEDED);
 
 namespace {
@@ -204,35 +209,20 @@ int hlkv_table_append_tokens(hlkv_table* t, const HlkvHandle* seqs, size_t n,
   if (n > 0 && (seqs == nullptr || new_formats == nullptr || out == nullptr)) {
     return HLKV_STATUS_INVALID_ARGUMENT;
   }
-  const std::uint32_t T = t->t.block_tokens();
-  for (size_t i = 0; i < n; ++i) {
-    const SequenceHandle seq = sh(seqs[i]);
-    const Result<std::span<const std::uint32_t>> ids = t->t.sequence_block_ids(seq);
-    if (!ids.ok()) return st(ids.status());
-    if (!ids.value().empty()) {
-      const std::uint32_t tail = ids.value().back();
-      const BlockHandle h = t->t.handle_of(tail);
-      const Result<BlockDescriptor> d = t->t.lookup(h);
-      if (!d.ok()) return st(d.status());
-      const std::uint32_t vt = d.value().exec.valid_tokens();
-      if (vt < T) {
-        const Status s = t->t.set_valid_tokens(h, vt + 1);
-        if (s != Status::kOk) return st(s);
-        out[i] = HlkvAppendTarget{tail, vt};
-        if (n_done != nullptr) *n_done = i + 1;
-        continue;
-      }
-    }
-    AllocRequest req;
-    req.format = fmt(new_formats[i]);
-    req.valid_tokens = 1;
-    req.layout = layout;
-    const Result<BlockHandle> r = t->t.append_block(seq, req);
-    if (!r.ok()) return st(r.status());
-    out[i] = HlkvAppendTarget{r.value().id, 0};
-    if (n_done != nullptr) *n_done = i + 1;
-  }
-  return HLKV_STATUS_OK;
+  // Reused per thread: no allocation once they have grown to the batch size.
+  thread_local std::vector<SequenceHandle> hs;
+  thread_local std::vector<FormatId> fs;
+  thread_local std::vector<TokenTarget> tg;
+  hs.resize(n);
+  fs.resize(n);
+  tg.resize(n);
+  if (n > 0) std::memcpy(hs.data(), seqs, n * sizeof(SequenceHandle));
+  for (size_t i = 0; i < n; ++i) fs[i] = fmt(new_formats[i]);
+  size_t done = 0;
+  const Status s = t->t.append_tokens(hs, fs, layout, tg, done);
+  if (done > 0) std::memcpy(out, tg.data(), done * sizeof(HlkvAppendTarget));
+  if (n_done != nullptr) *n_done = done;
+  return st(s);
 }
 
 int hlkv_table_build_exec_table(const hlkv_table* t, const HlkvHandle* seqs, size_t n,

@@ -69,6 +69,12 @@ struct AllocRequest {
   std::uint32_t scale_ref = 0;
 };
 
+/// Where a decode step's new token goes: token slot `token` of block `block_id`.
+struct TokenTarget {
+  std::uint32_t block_id;
+  std::uint32_t token;
+};
+
 /// Both slots of a format change in flight.
 struct FormatChange {
   FormatId from_format;
@@ -153,6 +159,14 @@ class HeteroBlockTable {
   [[nodiscard]] Result<BlockHandle> append_block(SequenceHandle seq, const AllocRequest& request);
   [[nodiscard]] Status append_shared_block(SequenceHandle seq, BlockHandle block);
   [[nodiscard]] Status release_sequence(SequenceHandle seq);
+  /// Decode-step driver (no counterpart in the reference): one more token per sequence.
+  /// While the tail block has room, set_valid_tokens(tail, vt + 1) and out[i] = {tail, vt};
+  /// otherwise append_block(seqs[i], {new_formats[i], 1 valid token, layout}) and
+  /// out[i] = {new block, 0}.  The same state, delta and statuses as those public calls made
+  /// one sequence at a time; stops at the first failure, n_done = sequences completed.
+  [[nodiscard]] Status append_tokens(std::span<const SequenceHandle> seqs,
+                                     std::span<const FormatId> new_formats, std::uint32_t layout,
+                                     std::span<TokenTarget> out, std::size_t& n_done);
   [[nodiscard]] Result<std::span<const std::uint32_t>> sequence_block_ids(
       SequenceHandle seq) const;
   [[nodiscard]] Status build_exec_table(std::span<const SequenceHandle> seqs,
