@@ -15,8 +15,10 @@
 // quantize_reference rejects it (nothing written, HLKV_ERR_NONFINITE); a job with a bad
 // format, slot or valid_tokens is skipped with its bit.
 //
-// One row per D/8 lanes, 8 values per lane: a 16/8/4-byte load of source codes plus the
-// row parameters, register decode, then dev::encode_row.  HBM-bound like kernel (2).
+// One row per D/16 lanes, two chunks of 8 values per lane (chunks l and l + D/16 of the
+// row, so each warp-wide load is contiguous): per chunk a 16/8/4-byte load of source codes,
+// plus the row parameters, register decode, then dev::encode_row.  Two chunks per lane
+// halve the per-row work (job load and checks, index arithmetic) per value.
 #include <cuda_runtime.h>
 
 #include <cstdint>
@@ -47,12 +49,14 @@ struct Params {
   FastDiv div_rows, div_h, div_t;
 };
 
+constexpr int kChunks = 2;  // 8-value chunks per lane
+
 template <int kD>
 __global__ void __launch_bounds__(kThreads) transcode_kernel(const Params p) {
-  constexpr int kLanes = kD / 8;
+  constexpr int kLanes = kD / (8 * kChunks);
   constexpr int kRowsPerIter = kThreads / kLanes;
   const uint32_t lane = threadIdx.x % kLanes;
-  const uint32_t mask = dev::row_mask<kD>();
+  const uint32_t mask = dev::row_mask<kD, kChunks>();
   for (uint32_t g = blockIdx.x * kRowsPerIter + threadIdx.x / kLanes; g < p.rows_total;
        g += gridDim.x * kRowsPerIter) {
     // Uniform over the lanes of row g.
@@ -76,31 +80,48 @@ __global__ void __launch_bounds__(kThreads) transcode_kernel(const Params p) {
     const uint32_t rh = p.div_h.div(r);             // r / H
     const uint32_t tok = rh - p.div_t.div(rh) * p.T;  // (r / H) % T
     const uint8_t* src = p.pool[ff].base + uint64_t{fs} * p.pool[ff].slot_bytes;
-    uint4 raw = make_uint4(0u, 0u, 0u, 0u);
+    uint4 raw[kChunks];
+#pragma unroll
+    for (int c = 0; c < kChunks; ++c) raw[c] = make_uint4(0u, 0u, 0u, 0u);
     if (tok < vt) {
       const uint8_t* prm = src + p.code_bytes[ff];
       switch (ff) {
-        case dev::kFp16:
-          raw = dev::canon_f16x8(dev::ld_stream(reinterpret_cast<const uint4*>(src + uint64_t{r} * kD * 2) + lane));
+        case dev::kFp16: {
+          const uint4* row = reinterpret_cast<const uint4*>(src + uint64_t{r} * kD * 2);
+          uint4 v[kChunks];
+#pragma unroll
+          for (int c = 0; c < kChunks; ++c) v[c] = dev::ld_stream(row + c * kLanes + lane);
+#pragma unroll
+          for (int c = 0; c < kChunks; ++c) raw[c] = dev::canon_f16x8(v[c]);
           break;
+        }
         case dev::kE4M3:
         case dev::kE5M2: {
-          const uint2 c = dev::ld_stream(reinterpret_cast<const uint2*>(src + uint64_t{r} * kD) + lane);
+          const uint2* row = reinterpret_cast<const uint2*>(src + uint64_t{r} * kD);
+          uint2 v[kChunks];
+#pragma unroll
+          for (int c = 0; c < kChunks; ++c) v[c] = dev::ld_stream(row + c * kLanes + lane);
           const float s = __ldg(reinterpret_cast<const float*>(prm) + r);
-          raw = ff == dev::kE4M3 ? dev::fp8x8_to_f16<dev::kE4M3>(c, s) : dev::fp8x8_to_f16<dev::kE5M2>(c, s);
+#pragma unroll
+          for (int c = 0; c < kChunks; ++c) {
+            raw[c] = ff == dev::kE4M3 ? dev::fp8x8_to_f16<dev::kE4M3>(v[c], s) : dev::fp8x8_to_f16<dev::kE5M2>(v[c], s);
+          }
           break;
         }
         default: {
-          const uint32_t w = dev::ld_stream(reinterpret_cast<const uint32_t*>(src + uint64_t{r} * (kD / 2)) + lane);
+          const uint32_t* row = reinterpret_cast<const uint32_t*>(src + uint64_t{r} * (kD / 2));
+          uint32_t v[kChunks];
+#pragma unroll
+          for (int c = 0; c < kChunks; ++c) v[c] = dev::ld_stream(row + c * kLanes + lane);
           const float2 sb = __ldg(reinterpret_cast<const float2*>(prm) + r);
-          raw = dev::int4x8_to_f16(w, sb.x, sb.y);
+#pragma unroll
+          for (int c = 0; c < kChunks; ++c) raw[c] = dev::int4x8_to_f16(v[c], sb.x, sb.y);
           break;
         }
       }
     }
     uint8_t* dst = p.pool[tf].base + uint64_t{ts} * p.pool[tf].slot_bytes;
-    const uint4 chunk[1] = {raw};
-    const uint32_t e = dev::encode_row<kD>(tf, chunk, lane, mask, dst, r, p.code_bytes[tf]);
+    const uint32_t e = dev::encode_row<kD, kChunks>(tf, raw, lane, mask, dst, r, p.code_bytes[tf]);
     if (e != 0 && lane == 0) atomicOr(p.err, e);
   }
 }
@@ -139,7 +160,7 @@ extern "C" int hlkv_transcode(const HlkvPools* pools, const HlkvLayout* layout,
   p.T = layout->block_tokens;
   p.H = layout->kv_heads;
   const cudaStream_t s = reinterpret_cast<cudaStream_t>(stream);
-  const uint64_t rows_per_cta = kThreads / (layout->head_dim / 8);
+  const uint64_t rows_per_cta = kThreads / (layout->head_dim / (8 * kChunks));
   const uint64_t want = (p.rows_total + rows_per_cta - 1) / rows_per_cta;
   const uint64_t cap = uint64_t{static_cast<uint32_t>(sm_count())} * 16;
   const unsigned grid = static_cast<unsigned>(want < cap ? want : cap);
