@@ -14,7 +14,8 @@
 //   3. copy the patches into pinned staging;
 //   4. run kernel (3) (hlkv_apply_delta), which reads the staged patches in
 //      place: under unified addressing a kernel reads page-locked host memory
-//      directly, so no upload copy is queued.
+//      directly, so no upload copy is queued.  Deltas of 1 MiB or more are
+//      first copied to the device in one transfer, which is faster for them.
 // collect() is the host part (1 and 3) and flush() the queued part, so host table
 // work can run while the stream is busy.
 // Kernels issued later on the same stream see the updated tables.  One
@@ -80,9 +81,12 @@ class DeviceTables {
   std::uint32_t arena_size_ = 0;
   std::uint32_t arena_capacity_ = 0;
   std::uint32_t* d_err_ = nullptr;
+  static constexpr std::size_t kCopyDeltaBytes = std::size_t{1} << 20;  // copied, not read in place
   void* h_staging_ = nullptr;    // pinned
   void* staging_dev_ = nullptr;  // its device address (not an allocation)
   std::size_t staging_bytes_ = 0;
+  unsigned char* d_staging_ = nullptr;  // device copy of large deltas
+  std::size_t d_staging_bytes_ = 0;
   cudaEvent_t staging_free_ = nullptr;  // recorded after kernel (3), the staging's reader
   alloc::ExecDelta delta_;    // collected, not yet flushed
   alloc::ExecDelta scratch_;  // the next collect_delta() before merging into delta_

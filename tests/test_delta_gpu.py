@@ -142,3 +142,35 @@ def test_collect_flush_split_merges_pending_changes(hlkv_lib, cuda_device):
             assert list(arena[off:off + ln]) == t.sequence_block_ids(s)[1], rnd
     dt.flush()  # nothing pending: a no-op
     assert d2h(dt.error_word_ptr, 4).view(np.uint32)[0] == 0
+
+
+def test_large_first_sync_then_small_deltas(hlkv_lib, cuda_device):
+    """A table of 80,000 block ids: its first delta (every descriptor, 1.28 MB) is copied to
+    the device before kernel (3); the small deltas after it are read in place from pinned
+    staging.  After each sync the device tables equal the host's."""
+    h = hlkv_lib
+    n_ids = 80_000
+    t = h.Table(n_ids, [(1, 2048, 40_000), (3, 1088, 40_000)])
+    dt = h.DeviceTables()
+    rng = np.random.default_rng(5)
+    seqs = [t.create_sequence()[1] for _ in range(64)]
+    for s in seqs:
+        for _ in range(int(rng.integers(1, 200))):
+            assert t.append_block(s, int(rng.choice([1, 3])), 16)[0] == 0
+    assert t.pending()[0] >= 65_536  # at least 1 MiB of descriptor patches
+    for step in range(4):
+        if step:
+            for s in seqs[: 8 * step]:
+                st, ids = t.sequence_block_ids(s)
+                assert t.set_valid_tokens(t.handle_of(ids[-1]), int(rng.integers(1, 17))) == 0
+                assert t.append_block(s, 1, 3)[0] == 0
+        dt.sync(t)
+        import torch
+        torch.cuda.synchronize()
+        table, arena = _device_state(dt)
+        want = np.array([np.asarray(t.device_descriptor(i), np.uint32) for i in range(n_ids)])
+        assert np.array_equal(table, want), step
+        st, segs = t.batch_segments(seqs)
+        for s, (off, ln) in zip(seqs, segs):
+            assert list(arena[off:off + ln]) == list(t.sequence_block_ids(s)[1]), step
+    assert int(d2h(dt.error_word_ptr, 4).view(np.uint32)[0]) == 0
