@@ -89,7 +89,7 @@ __device__ __forceinline__ uint32_t resolve_block(const AttnParams& p, uint2 seg
       }
     }
   }
-  if (bad && (threadIdx.x & 31) == 0) atomicOr(p.err, bad);
+  if (bad) atomicOr(p.err, bad);
   return f;
 }
 
@@ -173,6 +173,26 @@ __device__ __forceinline__ void stage_rows(const uint8_t* payload, const uint8_t
   }
 }
 
+// Pulls the first tile of a block's K and V rows of head h (tokens 0..15), and their row
+// parameters, into L2 while the warp still works on its current block: lane l covers the
+// row of kv l / 16, token l % 16.  Only called for blocks that passed resolve_block, so
+// every address lies inside the block's slot.
+template <int kD>
+__device__ __forceinline__ void prefetch_block(const uint8_t* payload, uint64_t code_bytes, uint32_t f,
+                                               uint32_t vt, uint32_t T, uint32_t H, uint32_t h,
+                                               uint32_t lane) {
+  const uint32_t kv = lane >> 4, t = lane & 15;
+  if (t >= vt) return;
+  const uint32_t row = (kv * T + t) * H + h;
+  const uint32_t row_bytes = f == dev::kFp16 ? kD * 2 : f == dev::kInt4 ? kD / 2 : kD;
+  const uint8_t* a = payload + uint64_t{row} * row_bytes;
+  for (uint32_t o = 0; o < row_bytes; o += 128) asm volatile("prefetch.global.L2 [%0];" ::"l"(a + o));
+  if (f != dev::kFp16) {
+    const uint8_t* q = payload + code_bytes + uint64_t{row} * (f == dev::kInt4 ? 8u : 4u);
+    asm volatile("prefetch.global.L2 [%0];" ::"l"(q));
+  }
+}
+
 template <int kD>
 __device__ __noinline__ void stage_tiles(uint32_t f, const uint8_t* payload, const uint8_t* params,
                                          uint32_t t0, uint32_t vt, uint32_t T, uint32_t H, uint32_t h,
@@ -198,6 +218,8 @@ __global__ void __launch_bounds__(kAttnThreads, 4) decode_attention_kernel(const
                                                        kAttnWarps * (kD * 8 + 16) * 4
                                                    ? kAttnWarps * sizeof(WarpTiles<kD>)
                                                    : kAttnWarps * (kD * 8 + 16) * 4];
+  __shared__ const uint8_t* s_payload[kAttnThreads];
+  __shared__ uint32_t s_fv[kAttnThreads];  // format | valid_tokens << 8 (format 4: skip)
   const uint32_t unit = blockIdx.x / p.splits, split = blockIdx.x % p.splits;
   const uint32_t seq = unit / p.H, h = unit % p.H;
   const uint32_t lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
@@ -227,11 +249,28 @@ __global__ void __launch_bounds__(kAttnThreads, 4) decode_attention_kernel(const
   const uint32_t T = p.T, H = p.H;
   const uint32_t b0 = static_cast<uint32_t>(uint64_t{seg.y} * split / p.splits);
   const uint32_t b1 = static_cast<uint32_t>(uint64_t{seg.y} * (split + 1) / p.splits);
-  for (uint32_t j = b0 + warp; j < b1; j += kAttnWarps) {
-    const uint8_t* payload = nullptr;
-    uint32_t vt = 0;
-    const uint32_t f = resolve_block(p, seg, j, &payload, &vt);
+  // Blocks are resolved (arena -> descriptor -> checks) a batch at a time, one block per
+  // thread, so the dependent lookups of a batch overlap instead of preceding each block's
+  // payload reads.  Warp w then takes blocks w, w + 4, ... of the batch.
+  for (uint32_t base = b0; base < b1; base += kAttnThreads) {
+    const uint32_t nb = min(b1 - base, static_cast<uint32_t>(kAttnThreads));
+    __syncthreads();  // the previous batch is no longer read
+    if (threadIdx.x < nb) {
+      const uint8_t* payload = nullptr;
+      uint32_t vt = 0;
+      const uint32_t f = resolve_block(p, seg, base + threadIdx.x, &payload, &vt);
+      s_payload[threadIdx.x] = payload;
+      s_fv[threadIdx.x] = f | vt << 8;
+    }
+    __syncthreads();
+  for (uint32_t i = warp; i < nb; i += kAttnWarps) {
+    if (i + kAttnWarps < nb) {  // this warp's next block, into L2
+      const uint32_t fn = s_fv[i + kAttnWarps] & 0xFFu, vn = s_fv[i + kAttnWarps] >> 8;
+      if (fn <= 3 && vn > 0) prefetch_block<kD>(s_payload[i + kAttnWarps], p.code_bytes[fn], fn, vn, T, H, h, lane);
+    }
+    const uint32_t f = s_fv[i] & 0xFFu, vt = s_fv[i] >> 8;
     if (f > 3 || vt == 0) continue;
+    const uint8_t* payload = s_payload[i];
     const uint8_t* params = payload + p.code_bytes[f];
     for (uint32_t t0 = 0; t0 < vt; t0 += 16) {
       stage_tiles<kD>(f, payload, params, t0, vt, T, H, h, w, lane);
@@ -288,6 +327,7 @@ __global__ void __launch_bounds__(kAttnThreads, 4) decode_attention_kernel(const
       }
       __syncwarp();  // the tiles are rewritten next
     }
+  }
   }
 
   // ---- merge the warps: per query column the max, the sum and the head_dim outputs ----
