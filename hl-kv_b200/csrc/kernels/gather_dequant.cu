@@ -181,8 +181,8 @@ __device__ __forceinline__ void stream_block(const Params& p, const Item& it, ui
       if (live & (1u << u)) {
         switch (f) {
           case dev::kFp16: o = dev::canon_f16x8(raw[u]); break;
-          case dev::kE4M3: o = dev::fp8x8_to_f16<dev::kE4M3>(make_uint2(raw[u].x, raw[u].y), prm[u].x); break;
-          case dev::kE5M2: o = dev::fp8x8_to_f16<dev::kE5M2>(make_uint2(raw[u].x, raw[u].y), prm[u].x); break;
+          case dev::kE4M3: o = dev::fp8x8_to_f16_bits<dev::kE4M3>(make_uint2(raw[u].x, raw[u].y), prm[u].x); break;
+          case dev::kE5M2: o = dev::fp8x8_to_f16_bits<dev::kE5M2>(make_uint2(raw[u].x, raw[u].y), prm[u].x); break;
           default: o = dev::int4x8_to_f16(raw[u].x, prm[u].x, prm[u].y); break;
         }
       }
