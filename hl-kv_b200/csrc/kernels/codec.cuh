@@ -201,6 +201,35 @@ __device__ __forceinline__ uint4 fp8x8_to_f16(uint2 c, float scale) {
   return make_uint4(r[0], r[1], r[2], r[3]);
 }
 
+// ---- block-wide parameters --------------------------------------------------------------
+
+// The dequantization parameters {scale, bias} that a quantized block's descriptor carries
+// for all its rows, by scale mode (ScaleMode, block_descriptor.hpp:61-72):
+//   1 kInlineF32: the binary32 bits of scale_ref (inline_scale_f32), bias 0;
+//   2 kInlineF16Pair: binary16 scale in bits 0..15 and bias in bits 16..31, widened exactly.
+__device__ __forceinline__ float2 block_params_value(uint32_t mode, uint32_t scale_ref) {
+  if (mode == 1) return make_float2(__uint_as_float(scale_ref), 0.0f);
+  return make_float2(__half2float(__ushort_as_half(static_cast<unsigned short>(scale_ref & 0xFFFFu))),
+                     __half2float(__ushort_as_half(static_cast<unsigned short>(scale_ref >> 16))));
+}
+
+// The block is then one group of the reference's dequantize_reference_to_fp16, which
+// rejects non-finite parameters and a nonzero FP8 bias.  Tested on the bits: a value is
+// finite when its exponent field is not all ones; a binary16 bias is 0 when its low 15
+// bits are.
+__device__ __forceinline__ bool block_params_ok(uint32_t f, uint32_t mode, uint32_t scale_ref) {
+  if (mode == 1) return ((scale_ref >> 23) & 0xFFu) != 0xFFu;
+  return ((scale_ref >> 10) & 0x1Fu) != 0x1Fu && ((scale_ref >> 26) & 0x1Fu) != 0x1Fu &&
+         (f == kInt4 || (scale_ref & 0x7FFF0000u) == 0u);
+}
+
+// Both of the above: false when rejected, else the parameters in *out.
+__device__ __forceinline__ bool block_params(uint32_t f, uint32_t mode, uint32_t scale_ref, float2* out) {
+  if (!block_params_ok(f, mode, scale_ref)) return false;
+  *out = block_params_value(mode, scale_ref);
+  return true;
+}
+
 // ---- INT4 decode -----------------------------------------------------------------------------
 
 // q (0..15) as binary32, exactly: (2^23 + q) - 2^23.

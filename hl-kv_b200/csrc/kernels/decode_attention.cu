@@ -62,7 +62,8 @@ constexpr uint32_t kPart = 8 + 8 + 8 * kD;
 
 // The checks of kernel (1) for block j of a sequence; returns the format (4 = skip).
 __device__ __forceinline__ uint32_t resolve_block(const AttnParams& p, uint2 seg, uint32_t j,
-                                                  const uint8_t** payload, uint32_t* vt) {
+                                                  const uint8_t** payload, uint32_t* vt, uint32_t* wide,
+                                                  uint32_t* sref) {
   uint32_t bad = 0, f = 4;
   const uint64_t pos = uint64_t{seg.x} + j;
   if (pos >= p.arena_size) {
@@ -79,13 +80,16 @@ __device__ __forceinline__ uint32_t resolve_block(const AttnParams& p, uint2 seg
       else if (ff == dev::kInvalidFormat) bad = dev::kErrNotExecutable;
       else if (ff > 3 || p.pool[ff].base == nullptr || p.pool[ff].num_slots == 0) bad = dev::kErrBadFormat;
       else if (layout != p.layout_id) bad = dev::kErrLayout;
-      else if (ff != dev::kFp16 && mode != 0) bad = dev::kErrScaleMode;
+      else if (ff != dev::kFp16 && (mode > 2 || (mode != 0 && !dev::block_params_ok(ff, mode, d.z))))
+        bad = dev::kErrScaleMode;
       else if (v > p.T) bad = dev::kErrValidTokens;
       else if (d.x >= p.pool[ff].num_slots) bad = dev::kErrSlotRange;
       else {
         f = ff;
         *payload = p.pool[ff].base + uint64_t{d.x} * p.pool[ff].slot_bytes;
         *vt = v;
+        *wide = ff != dev::kFp16 ? mode : 0u;  // 0: per-row parameters
+        *sref = d.z;
       }
     }
   }
@@ -128,10 +132,12 @@ struct WarpTiles {
 // into the warp's tile; tokens >= vt become zeros.  Lane l handles 8-element chunks
 // l, l+32, ...: 16-lane groups read whole rows, coalesced.  Every load of the tile is
 // issued before the first conversion.
-template <int kD, uint32_t kF>
-__device__ __forceinline__ void stage_rows(const uint8_t* payload, const uint8_t* params, uint32_t kv,
-                                           uint32_t t0, uint32_t vt, uint32_t T, uint32_t H, uint32_t h,
-                                           __half (*tile)[kD + 8], uint32_t lane) {
+// kWide: the block's parameters are the block-wide pair wp for every row, instead of the
+// per-row ones at params (a separate instance, so the per-row code has no test of it).
+template <int kD, uint32_t kF, bool kWide>
+__device__ __forceinline__ void stage_rows(const uint8_t* payload, const uint8_t* params, float2 wp,
+                                           uint32_t kv, uint32_t t0, uint32_t vt, uint32_t T, uint32_t H,
+                                           uint32_t h, __half (*tile)[kD + 8], uint32_t lane) {
   constexpr int kChunks = kD / 8;              // chunks per row
   constexpr int kPerLane = 16 * kChunks / 32;  // chunks per lane per tile
   uint4 raw[kPerLane];
@@ -148,12 +154,12 @@ __device__ __forceinline__ void stage_rows(const uint8_t* payload, const uint8_t
         raw[i] = dev::ld_stream(reinterpret_cast<const uint4*>(payload) + v);
       } else if constexpr (kF == dev::kInt4) {
         raw[i].x = dev::ld_stream(reinterpret_cast<const uint32_t*>(payload) + v);
-        prm[i] = __ldg(reinterpret_cast<const float2*>(params) + row);
+        prm[i] = kWide ? wp : __ldg(reinterpret_cast<const float2*>(params) + row);
       } else {
         const uint2 w = dev::ld_stream(reinterpret_cast<const uint2*>(payload) + v);
         raw[i].x = w.x;
         raw[i].y = w.y;
-        prm[i].x = __ldg(reinterpret_cast<const float*>(params) + row);
+        prm[i].x = kWide ? wp.x : __ldg(reinterpret_cast<const float*>(params) + row);
       }
     }
   }
@@ -203,10 +209,26 @@ __device__ __noinline__ void stage_tiles(uint32_t f, const uint8_t* payload, con
   for (uint32_t kv = 0; kv < 2; ++kv) {
     __half(*tile)[kD + 8] = kv == 0 ? w.k : w.v;
     switch (f) {
-      case dev::kFp16: stage_rows<kD, dev::kFp16>(payload, params, kv, t0, vt, T, H, h, tile, lane); break;
-      case dev::kE4M3: stage_rows<kD, dev::kE4M3>(payload, params, kv, t0, vt, T, H, h, tile, lane); break;
-      case dev::kE5M2: stage_rows<kD, dev::kE5M2>(payload, params, kv, t0, vt, T, H, h, tile, lane); break;
-      default: stage_rows<kD, dev::kInt4>(payload, params, kv, t0, vt, T, H, h, tile, lane); break;
+      case dev::kFp16: stage_rows<kD, dev::kFp16, false>(payload, params, make_float2(0.0f, 0.0f), kv, t0, vt, T, H, h, tile, lane); break;
+      case dev::kE4M3: stage_rows<kD, dev::kE4M3, false>(payload, params, make_float2(0.0f, 0.0f), kv, t0, vt, T, H, h, tile, lane); break;
+      case dev::kE5M2: stage_rows<kD, dev::kE5M2, false>(payload, params, make_float2(0.0f, 0.0f), kv, t0, vt, T, H, h, tile, lane); break;
+      default: stage_rows<kD, dev::kInt4, false>(payload, params, make_float2(0.0f, 0.0f), kv, t0, vt, T, H, h, tile, lane); break;
+    }
+  }
+}
+
+// The same for a quantized block with block-wide parameters {scale, bias}.
+template <int kD>
+__device__ __noinline__ void stage_tiles_wide(uint32_t f, const uint8_t* payload, float2 prm, uint32_t t0,
+                                              uint32_t vt, uint32_t T, uint32_t H, uint32_t h,
+                                              WarpTiles<kD>& w, uint32_t lane) {
+#pragma unroll 1
+  for (uint32_t kv = 0; kv < 2; ++kv) {
+    __half(*tile)[kD + 8] = kv == 0 ? w.k : w.v;
+    switch (f) {
+      case dev::kE4M3: stage_rows<kD, dev::kE4M3, true>(payload, nullptr, prm, kv, t0, vt, T, H, h, tile, lane); break;
+      case dev::kE5M2: stage_rows<kD, dev::kE5M2, true>(payload, nullptr, prm, kv, t0, vt, T, H, h, tile, lane); break;
+      default: stage_rows<kD, dev::kInt4, true>(payload, nullptr, prm, kv, t0, vt, T, H, h, tile, lane); break;
     }
   }
 }
@@ -219,7 +241,8 @@ __global__ void __launch_bounds__(kAttnThreads, 4) decode_attention_kernel(const
                                                    ? kAttnWarps * sizeof(WarpTiles<kD>)
                                                    : kAttnWarps * (kD * 8 + 16) * 4];
   __shared__ const uint8_t* s_payload[kAttnThreads];
-  __shared__ uint32_t s_fv[kAttnThreads];  // format | valid_tokens << 8 (format 4: skip)
+  __shared__ uint32_t s_fv[kAttnThreads];  // format | valid_tokens << 8 | scale mode << 30 (format 4: skip)
+  __shared__ uint32_t s_sref[kAttnThreads];  // scale_ref of blocks with block-wide parameters
   const uint32_t unit = blockIdx.x / p.splits, split = blockIdx.x % p.splits;
   const uint32_t seq = unit / p.H, h = unit % p.H;
   const uint32_t lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
@@ -258,22 +281,26 @@ __global__ void __launch_bounds__(kAttnThreads, 4) decode_attention_kernel(const
     if (threadIdx.x < nb) {
       const uint8_t* payload = nullptr;
       uint32_t vt = 0;
-      const uint32_t f = resolve_block(p, seg, base + threadIdx.x, &payload, &vt);
+      uint32_t wide = 0, sref = 0;
+      const uint32_t f = resolve_block(p, seg, base + threadIdx.x, &payload, &vt, &wide, &sref);
       s_payload[threadIdx.x] = payload;
-      s_fv[threadIdx.x] = f | vt << 8;
+      s_fv[threadIdx.x] = f | vt << 8 | wide << 30;
+      s_sref[threadIdx.x] = sref;
     }
     __syncthreads();
   for (uint32_t i = warp; i < nb; i += kAttnWarps) {
     if (i + kAttnWarps < nb) {  // this warp's next block, into L2
-      const uint32_t fn = s_fv[i + kAttnWarps] & 0xFFu, vn = s_fv[i + kAttnWarps] >> 8;
+      const uint32_t fn = s_fv[i + kAttnWarps] & 0xFFu, vn = (s_fv[i + kAttnWarps] >> 8) & 0x3FFu;
       if (fn <= 3 && vn > 0) prefetch_block<kD>(s_payload[i + kAttnWarps], p.code_bytes[fn], fn, vn, T, H, h, lane);
     }
-    const uint32_t f = s_fv[i] & 0xFFu, vt = s_fv[i] >> 8;
+    const uint32_t f = s_fv[i] & 0xFFu, vt = (s_fv[i] >> 8) & 0x3FFu;
     if (f > 3 || vt == 0) continue;
+    const uint32_t wmode = s_fv[i] >> 30;  // 0: per-row parameters
     const uint8_t* payload = s_payload[i];
     const uint8_t* params = payload + p.code_bytes[f];
     for (uint32_t t0 = 0; t0 < vt; t0 += 16) {
-      stage_tiles<kD>(f, payload, params, t0, vt, T, H, h, w, lane);
+      if (wmode != 0) stage_tiles_wide<kD>(f, payload, dev::block_params_value(wmode, s_sref[i]), t0, vt, T, H, h, w, lane);
+      else stage_tiles<kD>(f, payload, params, t0, vt, T, H, h, w, lane);
       __syncwarp();
       // S^T (16 tokens x 8 query columns) = K . Q^T
       float s[4] = {0.0f, 0.0f, 0.0f, 0.0f};

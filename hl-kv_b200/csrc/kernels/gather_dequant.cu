@@ -71,18 +71,20 @@ struct Params {
 struct Item {
   const uint8_t* payload;
   uint16_t* out;
-  uint32_t fmt;         // 0..3, or kSkip
+  uint32_t fmt;         // 0..3 (| kWide: block-wide parameters in prm), or kSkip
   uint32_t valid_rows;  // rows per K/V half holding valid tokens: valid_tokens * H
   uint32_t tile_begin;  // warp tiles [tile_begin, tile_end) of the block are streamed
   uint32_t tile_end;
+  float2 prm;           // block-wide {scale, bias} (scale modes 1 and 2)
 };
 constexpr uint32_t kSkip = 0xFFu;
+constexpr uint32_t kWide = 0x100u;
 
 // Resolves block j of sequence `seq` into an Item; on a failed check the item
 // is skipped and its bit reported.  Check order matches the oracle's
 // resolve_block().
 __device__ Item resolve(const Params& p, uint32_t seq, uint64_t j, uint64_t blocks_before) {
-  Item it{nullptr, nullptr, kSkip, 0, 0, 0};
+  Item it{nullptr, nullptr, kSkip, 0, 0, 0, make_float2(0.0f, 0.0f)};
   uint32_t bad = 0;
   const uint64_t base = p.out_offsets ? p.out_offsets[seq] : blocks_before * p.block_elems;
   if (base & 7u) {
@@ -103,13 +105,14 @@ __device__ Item resolve(const Params& p, uint32_t seq, uint64_t j, uint64_t bloc
         else if (f == dev::kInvalidFormat) bad = dev::kErrNotExecutable;
         else if (f > 3 || p.pool[f].base == nullptr || p.pool[f].num_slots == 0) bad = dev::kErrBadFormat;
         else if (layout != p.layout_id) bad = dev::kErrLayout;
-        else if (f != dev::kFp16 && mode != 0) bad = dev::kErrScaleMode;
+        else if (f != dev::kFp16 && (mode > 2 || (mode != 0 && !dev::block_params(f, mode, d.z, &it.prm))))
+          bad = dev::kErrScaleMode;
         else if (vt > p.T) bad = dev::kErrValidTokens;
         else if (d.x >= p.pool[f].num_slots) bad = dev::kErrSlotRange;
         else {
           it.payload = p.pool[f].base + uint64_t{d.x} * p.pool[f].slot_bytes;
           it.out = p.out + base + j * p.block_elems;
-          it.fmt = f;
+          it.fmt = f | (f != dev::kFp16 && mode != 0 ? kWide : 0u);
           it.valid_rows = vt * p.H;
         }
       }
@@ -140,7 +143,8 @@ __device__ __forceinline__ void stream_block(const Params& p, const Item& it, ui
   const uint32_t lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
   const uint32_t nchunks = static_cast<uint32_t>(p.block_elems >> 3);
   const uint32_t rpk = p.rows_per_kv;
-  const uint32_t f = it.fmt;
+  const uint32_t f = it.fmt & 0xFFu;
+  const bool wide = (it.fmt & kWide) != 0;  // the same item for every warp of the CTA
   const uint8_t* payload = it.payload;
   const uint8_t* params = payload + p.code_bytes[f];
   uint4* out = reinterpret_cast<uint4*>(it.out);
@@ -163,12 +167,12 @@ __device__ __forceinline__ void stream_block(const Params& p, const Item& it, ui
           raw[u] = dev::ld_stream(reinterpret_cast<const uint4*>(payload) + v);
         } else if (f == dev::kInt4) {
           raw[u].x = dev::ld_stream(reinterpret_cast<const uint32_t*>(payload) + v);
-          prm[u] = __ldg(reinterpret_cast<const float2*>(params) + row);
+          prm[u] = wide ? it.prm : __ldg(reinterpret_cast<const float2*>(params) + row);
         } else {
           const uint2 c = dev::ld_stream(reinterpret_cast<const uint2*>(payload) + v);
           raw[u].x = c.x;
           raw[u].y = c.y;
-          prm[u].x = __ldg(reinterpret_cast<const float*>(params) + row);
+          prm[u].x = wide ? it.prm.x : __ldg(reinterpret_cast<const float*>(params) + row);
         }
       }
     }

@@ -4,7 +4,11 @@
 // blocks FP16 -> FP8 -> INT4.
 //
 // Job k moves the block in slot from_slot of pool from_format into slot to_slot of pool
-// to_format.  Per row (one parameter group of D values, layout as in kernel (1)):
+// to_format.  The source block's parameters are per row, or block-wide when the job carries
+// its descriptor's scale mode 1 or 2 and scale_ref (as kernel (1) reads them; mode 3 and
+// parameters the reference's dequantizer rejects skip the job with HLKV_ERR_SCALE_MODE).
+// The destination is written with per-row parameters (commit it with scale mode kNone).
+// Per row (one parameter group of D values, layout as in kernel (1)):
 //   rows of tokens < valid_tokens: decoded exactly as kernel (1) decodes them (the
 //     reference's dequantize_reference_to_fp16, cpu_dequant.cpp:127-141), then encoded
 //     as kernel (2) encodes an appended FP16 row (quantize_reference on those values);
@@ -63,11 +67,16 @@ __global__ void __launch_bounds__(kThreads) transcode_kernel(const Params p) {
     const uint32_t k = p.div_rows.div(g);
     const uint32_t r = g - k * p.rows_per_block;
     const uint4 j0 = __ldg(p.jobs + 2 * uint64_t{k});
-    const uint32_t vt = __ldg(p.jobs + 2 * uint64_t{k} + 1).x;
+    const uint4 j1 = __ldg(p.jobs + 2 * uint64_t{k} + 1);  // {valid_tokens, from_scale_mode, from_scale_ref, 0}
+    const uint32_t vt = j1.x;
     const uint32_t ff = j0.x, fs = j0.y, tf = j0.z, ts = j0.w;
+    const uint32_t fmode = ff == dev::kFp16 ? 0u : j1.y;
+    float2 wprm = make_float2(0.0f, 0.0f);
     uint32_t bad = 0;
     if (ff > 3 || tf > 3 || p.pool[ff].base == nullptr || p.pool[tf].base == nullptr) {
       bad = dev::kErrBadFormat;
+    } else if (fmode > 2 || (fmode != 0 && !dev::block_params(ff, fmode, j1.z, &wprm))) {
+      bad = dev::kErrScaleMode;
     } else if (fs >= p.pool[ff].num_slots || ts >= p.pool[tf].num_slots) {
       bad = dev::kErrSlotRange;
     } else if (vt > p.T) {
@@ -101,7 +110,7 @@ __global__ void __launch_bounds__(kThreads) transcode_kernel(const Params p) {
           uint2 v[kChunks];
 #pragma unroll
           for (int c = 0; c < kChunks; ++c) v[c] = dev::ld_stream(row + c * kLanes + lane);
-          const float s = __ldg(reinterpret_cast<const float*>(prm) + r);
+          const float s = fmode != 0 ? wprm.x : __ldg(reinterpret_cast<const float*>(prm) + r);
 #pragma unroll
           for (int c = 0; c < kChunks; ++c) {
             raw[c] = ff == dev::kE4M3 ? dev::fp8x8_to_f16<dev::kE4M3>(v[c], s) : dev::fp8x8_to_f16<dev::kE5M2>(v[c], s);
@@ -113,7 +122,7 @@ __global__ void __launch_bounds__(kThreads) transcode_kernel(const Params p) {
           uint32_t v[kChunks];
 #pragma unroll
           for (int c = 0; c < kChunks; ++c) v[c] = dev::ld_stream(row + c * kLanes + lane);
-          const float2 sb = __ldg(reinterpret_cast<const float2*>(prm) + r);
+          const float2 sb = fmode != 0 ? wprm : __ldg(reinterpret_cast<const float2*>(prm) + r);
 #pragma unroll
           for (int c = 0; c < kChunks; ++c) raw[c] = dev::int4x8_to_f16(v[c], sb.x, sb.y);
           break;

@@ -73,7 +73,9 @@ enum {
   HLKV_ERR_BLOCK_ID_RANGE = 1u << 4,  /* arena entry / target id >= table_size        */
   HLKV_ERR_VALID_TOKENS = 1u << 5,    /* valid_tokens > block_tokens                  */
   HLKV_ERR_LAYOUT = 1u << 6,          /* descriptor layout tag != layout->layout_id   */
-  HLKV_ERR_SCALE_MODE = 1u << 7,      /* quantized block with scale_mode != kNone     */
+  HLKV_ERR_SCALE_MODE = 1u << 7,      /* quantized block with scale mode 3 (external)
+                                         or block-wide parameters that are non-finite
+                                         or give FP8 a nonzero bias                  */
   HLKV_ERR_DESC_MISMATCH = 1u << 8,   /* table[id].block_id != id                     */
   HLKV_ERR_NONFINITE = 1u << 9,       /* a group with a non-finite value was skipped  */
   HLKV_ERR_TOKEN_RANGE = 1u << 10,    /* append target token >= block_tokens          */
@@ -144,9 +146,12 @@ int hlkv_last_cuda_error(void);
  *           sum of the lengths * block_elems when d_out_offsets is NULL.
  * Rows of tokens < valid_tokens are decoded per hl::quant's
  * dequantize_reference_to_fp16 (cpu_dequant.cpp:127-141), bit for bit; rows of
- * later tokens are written as +0.  A block failing a check is skipped and its
- * bit set in *d_err.  The reference has no gather; its per-block semantics are
- * the reference's CPU decoder.
+ * later tokens are written as +0.  A quantized block's parameters are per row
+ * (after its codes) for scale mode 0, or block-wide from the descriptor
+ * (block_descriptor.hpp:61-72): mode 1 scale = the binary32 bits of scale_ref, bias
+ * 0; mode 2 scale and bias = the binary16 halves of scale_ref (bits 0..15, 16..31).
+ * A block failing a check is skipped and its bit set in *d_err.  The reference has
+ * no gather; its per-block semantics are the reference's CPU decoder.
  */
 int hlkv_gather_dequant(const HlkvPools* pools, const HlkvLayout* layout,
                         const HlkvExecDescriptor* d_table, uint32_t table_size,
@@ -258,7 +263,9 @@ typedef struct {
   uint32_t to_format;   /* ... and the target pool and slot (begin_format_change)     */
   uint32_t to_slot;
   uint32_t valid_tokens; /* rows of later tokens are encoded from zeros              */
-  uint32_t reserved[3];  /* 0 */
+  uint32_t from_scale_mode; /* the source descriptor's scale mode (0, 1 or 2) ...      */
+  uint32_t from_scale_ref;  /* ... and scale_ref: block-wide source parameters          */
+  uint32_t reserved;        /* 0 */
 } HlkvTranscodeJob;
 
 /*
@@ -268,9 +275,11 @@ typedef struct {
  * (dequantize_reference_to_fp16) and encoded as kernel (2) encodes an appended row
  * (quantize_reference on those binary16 values); rows of later tokens encoded from +0.
  * Jobs come from hlkv_table_begin_format_change; commit the changes (and flush the
- * delta) after this call on the same stream.  Source and destination slots must not
- * overlap.  d_jobs 16-byte aligned.  Bad jobs and non-finite rows are skipped with
- * their HLKV_ERR_* bits.
+ * delta) after this call on the same stream, with scale mode kNone: the destination
+ * carries per-row parameters.  A source block with block-wide parameters (its
+ * descriptor's scale mode 1 or 2) passes that mode and scale_ref in the job.  Source and
+ * destination slots must not overlap.  d_jobs 16-byte aligned.  Bad jobs and non-finite
+ * rows are skipped with their HLKV_ERR_* bits.
  */
 int hlkv_transcode(const HlkvPools* pools, const HlkvLayout* layout, const HlkvTranscodeJob* d_jobs,
                    uint32_t n, uint32_t* d_err, hlkv_stream_t stream);

@@ -351,14 +351,43 @@ static size_t slot_need(int f, const orc_geom* g) {
 }
 
 /*
+ * The dequantization parameters {scale, bias} of row r of a quantized block, by the
+ * descriptor's scale_mode (ScaleMode, block_descriptor.hpp:61-72):
+ *   0 kNone: per row, stored after the codes (FP8: binary32 scale; INT4: scale, bias);
+ *   1 kInlineF32: one scale for the whole block, the binary32 bits of scale_ref
+ *     (BlockExecDescriptor::inline_scale_f32, block_descriptor.hpp:179-182), bias 0;
+ *   2 kInlineF16Pair: binary16 scale in bits 0..15 and bias in bits 16..31 of scale_ref
+ *     (hl_allocator_abi.md:62), widened exactly.
+ * With a block-wide mode the block is one group of dequantize_reference_to_fp16
+ * (cpu_dequant.cpp:127-141) with these parameters; FP8 decoding reads the scale only.
+ */
+static void row_params(int f, uint32_t mode, uint32_t scale_ref, const uint8_t* payload,
+                       size_t code_bytes, size_t r, float p[2]) {
+  p[0] = 0.0f;
+  p[1] = 0.0f;
+  if (mode == 1) {
+    memcpy(&p[0], &scale_ref, 4);
+  } else if (mode == 2) {
+    p[0] = mf_decode(scale_ref & 0xFFFFu, &kSpecFp16);
+    p[1] = mf_decode(scale_ref >> 16, &kSpecFp16);
+  } else if (f == F_E4M3 || f == F_E5M2) {
+    memcpy(&p[0], payload + code_bytes + 4 * r, 4);
+  } else if (f == F_INT4) {
+    memcpy(p, payload + code_bytes + 8 * r, 8);
+  }
+}
+
+/*
  * Resolves block j of a segment to its payload, or returns the first failing
  * check as an error bit (0 = ok).  Check order is part of the contract: the
- * kernels report the same single bit per block.
+ * kernels report the same single bit per block.  Quantized blocks may carry
+ * block-wide parameters (scale modes 1 and 2); scale mode 3 (kExternal, an index
+ * into a scale pool the ABI does not pass) is rejected.
  */
 static uint32_t resolve_block(const orc_pool* pools, const orc_geom* g, const uint32_t* table,
                               uint32_t table_size, const uint32_t* arena, uint32_t arena_size,
                               uint64_t arena_pos, int* fmt, const uint8_t** payload,
-                              uint32_t* valid) {
+                              uint32_t* valid, uint32_t* scale_mode, uint32_t* scale_ref) {
   if (arena_pos >= arena_size) return E_ARENA_RANGE;
   const uint32_t id = arena[arena_pos];
   if (id >= table_size) return E_BLOCK_ID_RANGE;
@@ -370,18 +399,27 @@ static uint32_t resolve_block(const orc_pool* pools, const orc_geom* g, const ui
   if (f == F_INVALID) return E_NOT_EXECUTABLE;
   if (f > 3 || pools[f].base == NULL || pools[f].num_slots == 0) return E_BAD_FORMAT;
   if (layout != g->layout_id) return E_LAYOUT;
-  if (f != F_FP16 && mode != 0) return E_SCALE_MODE;
+  if (f != F_FP16 && mode > 2) return E_SCALE_MODE;
+  if (f != F_FP16 && mode != 0) {
+    /* Block-wide parameters must be what dequantize_reference accepts
+       (cpu_dequant.hpp:33, cpu_dequant.cpp:85): finite scale and bias, FP8 bias 0. */
+    float p[2];
+    row_params((int)f, mode, d[2], NULL, 0, 0, p);
+    if (!isfinite(p[0]) || !isfinite(p[1]) || (f != F_INT4 && p[1] != 0.0f)) return E_SCALE_MODE;
+  }
   if (vt > g->T) return E_VALID_TOKENS;
   if (slot >= pools[f].num_slots) return E_SLOT_RANGE;
   *fmt = (int)f;
   *payload = pools[f].base + (size_t)slot * pools[f].slot_bytes;
   *valid = vt;
+  *scale_mode = f == F_FP16 ? 0u : mode;
+  *scale_ref = d[2];
   return 0;
 }
 
 /* Decodes one resolved block into out[0 .. 2*T*H*D). */
-static void decode_block(int f, const uint8_t* payload, uint32_t vt, const orc_geom* g,
-                         uint16_t* out) {
+static void decode_block(int f, const uint8_t* payload, uint32_t vt, uint32_t mode,
+                         uint32_t scale_ref, const orc_geom* g, uint16_t* out) {
   const size_t rows = (size_t)2 * g->T * g->H, D = g->D, rows_per_kv = (size_t)g->T * g->H;
   const size_t code_bytes = fmt_packed_bytes(f, rows * D);
   for (size_t r = 0; r < rows; ++r) {
@@ -391,11 +429,11 @@ static void decode_block(int f, const uint8_t* payload, uint32_t vt, const orc_g
       memset(o, 0, 2 * D);
       continue;
     }
-    float p[2] = {0.0f, 0.0f};
+    float p[2];
     const uint8_t* codes = payload + fmt_packed_bytes(f, r * D);
-    if (f == F_E4M3 || f == F_E5M2) memcpy(&p[0], payload + code_bytes + 4 * r, 4);
-    if (f == F_INT4) memcpy(p, payload + code_bytes + 8 * r, 8);
-    /* One group per row: dequantize_reference_to_fp16 on D elements. */
+    row_params(f, mode, scale_ref, payload, code_bytes, r, p);
+    /* One group per row, or one per block with the same parameters in every row:
+       dequantize_reference_to_fp16 on D elements. */
     for (size_t i = 0; i < D; ++i)
       o[i] = (uint16_t)mf_encode(dq_value(f, codes, i, p, D), &kSpecFp16);
   }
@@ -428,12 +466,12 @@ static void* gather_worker(void* arg) {
     if (base % 8 != 0) { jb->err |= E_OUT_ALIGN; continue; }
     int f = 0;
     const uint8_t* payload = NULL;
-    uint32_t vt = 0;
+    uint32_t vt = 0, mode = 0, sref = 0;
     const uint32_t e = resolve_block(jb->pools, jb->g, jb->table, jb->table_size, jb->arena,
                                      jb->arena_size, (uint64_t)jb->segs[2 * seq] + j, &f,
-                                     &payload, &vt);
+                                     &payload, &vt, &mode, &sref);
     if (e) { jb->err |= e; continue; }
-    decode_block(f, payload, vt, jb->g, jb->out + base + j * belems);
+    decode_block(f, payload, vt, mode, sref, jb->g, jb->out + base + j * belems);
   }
   return NULL;
 }
@@ -558,9 +596,10 @@ ORC_API uint32_t orc_append_encode(const orc_pool* pools, uint32_t T, uint32_t H
 }
 
 /* ---- format-change transcode (device half of hetero_block_table.cpp:251-287) ---------------- */
-/* Job k: {from_format, from_slot, to_format, to_slot, valid_tokens, 0, 0, 0}.  Each row of a
- * valid token is decoded with dequantize_reference_to_fp16 (cpu_dequant.cpp:127-141) from the
- * source slot and re-encoded with quantize_reference (cpu_quant.cpp:97-170) on the binary32
+/* Job k: {from_format, from_slot, to_format, to_slot, valid_tokens, from_scale_mode,
+ * from_scale_ref, 0}.  Each row of a valid token is decoded with dequantize_reference_to_fp16
+ * (cpu_dequant.cpp:127-141) from the source slot, with the source block's parameters
+ * (row_params: per row, or block-wide by its scale mode; mode 3 is rejected) and re-encoded with quantize_reference (cpu_quant.cpp:97-170) on the binary32
  * values of those binary16 results into the destination slot; rows of later tokens are
  * encoded from +0.  A rejected row leaves the destination row untouched (E_NONFINITE). */
 ORC_API uint32_t orc_transcode(const orc_pool* pools, uint32_t T, uint32_t H, uint32_t D,
@@ -574,7 +613,14 @@ ORC_API uint32_t orc_transcode(const orc_pool* pools, uint32_t T, uint32_t H, ui
   for (uint32_t k = 0; k < n; ++k) {
     const uint32_t* j = jobs + 8 * (size_t)k;
     const uint32_t ff = j[0], fs = j[1], tf = j[2], ts = j[3], vt = j[4];
+    const uint32_t fmode = ff == F_FP16 ? 0u : j[5], fref = j[6]; /* the source's scale mode */
     if (ff > 3 || tf > 3 || pools[ff].base == NULL || pools[tf].base == NULL) { err |= E_BAD_FORMAT; continue; }
+    if (fmode > 2) { err |= E_SCALE_MODE; continue; }
+    if (fmode != 0) {
+      float q[2];
+      row_params((int)ff, fmode, fref, NULL, 0, 0, q);
+      if (!isfinite(q[0]) || !isfinite(q[1]) || (ff != F_INT4 && q[1] != 0.0f)) { err |= E_SCALE_MODE; continue; }
+    }
     if (fs >= pools[ff].num_slots || ts >= pools[tf].num_slots) { err |= E_SLOT_RANGE; continue; }
     if (vt > T) { err |= E_VALID_TOKENS; continue; }
     const uint8_t* src = pools[ff].base + (size_t)fs * pools[ff].slot_bytes;
@@ -584,9 +630,8 @@ ORC_API uint32_t orc_transcode(const orc_pool* pools, uint32_t T, uint32_t H, ui
     for (size_t r = 0; r < rows; ++r) {
       const uint32_t tok = (uint32_t)((r / H) % T);
       if (tok < vt) {
-        float p[2] = {0.0f, 0.0f};
-        if (ff == F_E4M3 || ff == F_E5M2) memcpy(&p[0], src + src_codes + 4 * r, 4);
-        if (ff == F_INT4) memcpy(p, src + src_codes + 8 * r, 8);
+        float p[2];
+        row_params((int)ff, fmode, fref, src, src_codes, r, p);
         const int st = orc_dequantize_to_fp16((int)ff, src + fmt_packed_bytes((int)ff, r * D),
                                               fmt_packed_bytes((int)ff, D), D, p,
                                               ff == F_FP16 ? 0 : 1, ff == F_FP16 ? 0 : D, half, D);

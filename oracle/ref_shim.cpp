@@ -101,7 +101,7 @@ std::uint32_t resolve(const RefPool* pools, std::uint32_t T, std::uint32_t layou
   if (d.format() == a::kInvalidFormat) return 1u << 0;
   if (f > 3 || pools[f].base == nullptr || pools[f].num_slots == 0) return 1u << 1;
   if (d.layout() != layout_id) return 1u << 6;
-  if (f != 0 && d.scale_mode() != a::ScaleMode::kNone) return 1u << 7;
+  if (f != 0 && d.scale_mode() == a::ScaleMode::kExternal) return 1u << 7;
   if (d.valid_tokens() > T) return 1u << 5;
   if (d.slot >= pools[f].num_slots) return 1u << 2;
   *out = &d;
@@ -146,6 +146,26 @@ REF_API std::uint32_t ref_gather_dequant(const RefPool* pools, std::uint32_t T, 
       const std::uint8_t* payload = pools[fi].base + std::size_t{d->slot} * pools[fi].slot_bytes;
       const std::size_t code_bytes = packed(f, belems);
       std::uint16_t* o = out + base + j * belems;
+      const bool block_wide = fi != 0 && (d->scale_mode() == a::ScaleMode::kInlineF32 ||
+                                          d->scale_mode() == a::ScaleMode::kInlineF16Pair);
+      if (block_wide) {
+        // One group for the whole block: parameters the reference's dequantizer rejects
+        // (non-finite, or an FP8 bias) reject the block, output untouched.
+        q::AffineParams bp{0.0f, 0.0f};
+        if (d->scale_mode() == a::ScaleMode::kInlineF32) {
+          bp.scale = d->inline_scale_f32();
+        } else {
+          bp.scale = q::decode_fp16(static_cast<std::uint16_t>(d->scale_ref & 0xFFFFu));
+          bp.bias = q::decode_fp16(static_cast<std::uint16_t>(d->scale_ref >> 16));
+        }
+        std::vector<std::uint16_t> probe(D);
+        if (q::dequantize_reference_to_fp16(f, std::span<const std::byte>(reinterpret_cast<const std::byte*>(payload), packed(f, D)),
+                                            D, std::span<const q::AffineParams>(&bp, 1), D,
+                                            std::span<std::uint16_t>(probe)) != q::QuantStatus::kOk) {
+          err |= 1u << 7;
+          continue;
+        }
+      }
       for (std::size_t r = 0; r < rows; ++r) {
         const std::size_t r_in_kv = r < rows_per_kv ? r : r - rows_per_kv;
         if (r_in_kv >= std::size_t{d->valid_tokens()} * H) {
@@ -155,7 +175,18 @@ REF_API std::uint32_t ref_gather_dequant(const RefPool* pools, std::uint32_t T, 
         const auto* codes = reinterpret_cast<const std::byte*>(payload + packed(f, r * D));
         q::AffineParams p{0.0f, 0.0f};
         std::size_t np = 0, group = 0;
-        if (fi == 1 || fi == 2) {
+        if (block_wide && d->scale_mode() == a::ScaleMode::kInlineF32) {
+          // one binary32 scale for the whole block: the reference's own accessor
+          p.scale = d->inline_scale_f32();
+          np = 1;
+          group = D;
+        } else if (block_wide) {
+          // binary16 scale in bits 0..15, bias in 16..31 (hl_allocator_abi.md, scale modes)
+          p.scale = q::decode_fp16(static_cast<std::uint16_t>(d->scale_ref & 0xFFFFu));
+          p.bias = q::decode_fp16(static_cast<std::uint16_t>(d->scale_ref >> 16));
+          np = 1;
+          group = D;
+        } else if (fi == 1 || fi == 2) {
           std::memcpy(&p.scale, payload + code_bytes + 4 * r, 4);
           np = 1;
           group = D;

@@ -97,3 +97,30 @@ def oracle_attention(oracle, wl, q: np.ndarray, scale: float, table=None, arena=
             p = np.exp(s - s.max())
             res[i, hq] = (p[:, None] * V[:, h, :]).sum(0) / p.sum()
     return res, err
+
+
+def block_wide_scale_refs(rng, n: int, moderate: bool = False):
+    """(scale_mode, scale_ref) pairs for block-wide parameters: binary32 scales (mode 1) and
+    binary16 (scale, bias) pairs (mode 2).  By default they include zeros, negatives, tiny,
+    huge, Inf and NaN (some of which the decoder must reject); `moderate` keeps scales in
+    [-0.125, 1] with bias 0, so that codes written for per-row scales decode to finite
+    binary16 values (E5M2 codes reach 57344)."""
+    if moderate:
+        f32 = np.array([0.25, 0.5, 0.75, 1.0, 0.375], np.float32)
+        f16 = np.array([0.25, 0.5, 1.0, 0.875, -0.125, 0.0], np.float16)
+    else:
+        f32 = np.array([0.013, 1.0, -2.5, 0.0, -0.0, 3e-39, 1e-30, 7e4, 1e30, np.inf, np.nan, 448.0 / 17],
+                       np.float32)
+        f16 = np.array([0.01, 1.0, -0.75, 0.0, -0.0, 6e-8, 65504, np.inf, -np.inf, np.nan, 3.5, -100.0],
+                       np.float16)
+    out = []
+    for _ in range(n):
+        mode = int(rng.integers(1, 3))
+        if mode == 1:
+            ref = int(f32[rng.integers(f32.size)].view(np.uint32))
+        else:
+            lo = f16[rng.integers(f16.size)]
+            hi = f16[rng.integers(f16.size)] if not moderate else np.float16(0.0)
+            ref = int(lo.view(np.uint16)) | int(hi.view(np.uint16)) << 16
+        out.append((mode, ref))
+    return out

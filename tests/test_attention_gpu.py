@@ -140,3 +140,28 @@ def test_split_attention_workspace_checks(hlkv_lib, cuda_device):
     assert L.hlkv_decode_attention_split(*args(4, None, need)) == hlkv.INVALID_ARGUMENT
     assert L.hlkv_decode_attention_split(*args(4, C.c_void_p(264), need)) == hlkv.INVALID_ARGUMENT
     assert L.hlkv_decode_attention_split(*args(0, C.c_void_p(256), need)) == hlkv.INVALID_ARGUMENT
+
+
+@pytest.mark.parametrize("T,H,D,group", [(16, 8, 128, 4), (4, 2, 64, 2)])
+def test_attention_block_wide_scales(hlkv_lib, oracle, cuda_device, T, H, D, group):
+    """Blocks with block-wide parameters (scale modes 1 and 2) enter the attention with the
+    values kernel (1) decodes for them; against the same float64 oracle."""
+    from helpers import block_wide_scale_refs
+    from hlkv.workload import build_workload, mixed_formats
+    fm = mixed_formats(4, [6, 13, 2, 21], probs=(0.2, 0.35, 0.15, 0.3), seed=T + D + 1)
+    rng = np.random.default_rng(D + 1)
+    vt = [[T] * (len(r) - 1) + [int(rng.integers(1, T + 1))] for r in fm]
+    wl = build_workload(fm, T=T, H=H, D=D, seed=T * H + 1, valid_tokens=vt)
+    ids = []
+    for s in wl.seqs:
+        ids += wl.table.sequence_block_ids(s)[1]
+    refs = block_wide_scale_refs(rng, len(ids), moderate=True)
+    for k, bid in enumerate(ids):
+        if k % 3 != 2:
+            assert wl.table.set_scale(wl.table.handle_of(bid), *refs[k]) == 0
+    wl.dt.sync(wl.table)
+    scale = 1.0 / np.sqrt(D)
+    q, got, err = _run(hlkv_lib, wl, H * group, scale, seed=D)
+    want, oerr = oracle_attention(oracle, wl, q.astype(np.float64), scale)
+    assert err == oerr == 0
+    _close(got, want, vscale=40.0)

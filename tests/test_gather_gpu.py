@@ -170,7 +170,7 @@ def test_error_bits_and_skips(hlkv_lib, oracle, cuda_device):
         add_record(0xFFFFFFFF, 15),                                   # not executable
         add_record(0, pack_info(5, 0, 1, 4)),                         # unknown format
         add_record(0, pack_info(FP8_E4M3, 0, 2, 4)),                  # layout mismatch
-        add_record(0, pack_info(FP8_E4M3, 1, 1, 4)),                  # scale mode
+        add_record(0, pack_info(FP8_E4M3, 3, 1, 4)),                  # scale mode 3 (external)
         add_record(0, pack_info(INT4, 0, 1, 5)),                      # valid_tokens > T
         add_record(999, pack_info(FP16, 0, 1, 4)),                    # slot out of range
         add_record(0, pack_info(FP16, 0, 1, 4), block_id_field=7),    # block_id mismatch
@@ -225,3 +225,37 @@ def test_repeatable(hlkv_lib, small_mixed):
     a, _ = _run(hlkv_lib, small_mixed)
     b, _ = _run(hlkv_lib, small_mixed)
     assert np.array_equal(a, b)
+
+
+@pytest.mark.parametrize("T,H,D", [(16, 8, 128), (4, 2, 64), (2, 2, 256)])
+def test_block_wide_scale_modes(hlkv_lib, oracle, cuda_device, T, H, D):
+    """Blocks whose descriptors carry block-wide parameters (scale mode 1: binary32 scale in
+    scale_ref; mode 2: binary16 scale and bias) decode with those for every row; scale mode 3
+    and parameters the reference's dequantizer rejects (non-finite, FP8 bias) skip the block
+    with HLKV_ERR_SCALE_MODE.  Bit-exact against the oracle, which the reference-built
+    gather pins (tests/test_oracle_golden.py)."""
+    from helpers import block_wide_scale_refs
+    from hlkv.workload import build_workload, mixed_formats
+    rng = np.random.default_rng(T * D)
+    lens = [5, 9, 3, 11]
+    fm = mixed_formats(len(lens), lens, probs=(0.2, 0.3, 0.2, 0.3), seed=D)
+    vt = [[int(rng.integers(1, T + 1)) for _ in range(n)] for n in lens]
+    wl = build_workload(fm, T=T, H=H, D=D, seed=D + 1, valid_tokens=vt)
+    ids = []
+    for s in wl.seqs:
+        ids += wl.table.sequence_block_ids(s)[1]
+    refs = block_wide_scale_refs(rng, len(ids))
+    for k, bid in enumerate(ids):
+        if k % 3 == 2:
+            continue  # per-row parameters
+        mode, sref = (3, 12) if k == 4 else refs[k]
+        assert wl.table.set_scale(wl.table.handle_of(bid), mode, sref) == 0
+    wl.dt.sync(wl.table)
+    out, err = _run(hlkv_lib, wl)
+    want, oerr = oracle_gather(oracle, wl, fill=0xABCD)
+    assert err == oerr and err & (1 << 7)
+    assert_bits_equal(out, want)
+    # block-wide blocks were decoded, not only skipped
+    decoded = sum(1 for k in range(len(ids)) if k % 3 != 2)
+    per_block = out.reshape(len(ids), -1)
+    assert (per_block != 0xABCD).all(axis=1).sum() >= decoded // 2

@@ -9,6 +9,8 @@ import math
 import os
 
 import numpy as np
+
+from helpers import block_wide_scale_refs
 import pytest
 
 GOLDEN = os.path.join(os.path.dirname(os.path.abspath(__file__)), "golden", "golden.npz")
@@ -302,6 +304,52 @@ def test_gather_oracle_matches_reference_gather(oracle, ref):
     eb = ref.gather_dequant(pools, T, H, D, 1, table, arena, segs, b, threads=3)
     assert ea == eb and ea & 8 and ea & 1
     assert np.array_equal(a, b)
+
+
+def test_gather_with_block_wide_scales_matches_reference(oracle, ref):
+    """Descriptors with scale modes kInlineF32 / kInlineF16Pair (block_descriptor.hpp:61-72):
+    the block's rows decode with the descriptor's parameters instead of the per-row ones, as
+    one group of the reference's dequantize_reference_to_fp16 (the reference-built gather uses
+    the reference's own inline_scale_f32 and decode_fp16); kExternal is rejected (bit 7)."""
+    rng = np.random.default_rng(33)
+    T, H, D = 4, 2, 64
+    rows, elems = 2 * T * H, 2 * T * H * D
+    pools = {}
+    for f in (0, 1, 2, 3):
+        ns = 6
+        sb = (oracle.slot_bytes_needed(f, T, H, D) + 15) // 16 * 16
+        buf = rng.integers(0, 256, size=(ns, sb), dtype=np.uint8)  # any codes decode
+        if f == 3:  # finite per-row parameters for the per-row blocks
+            code = oracle.slot_bytes_needed(3, T, H, D) - 8 * rows
+            prm = (rng.standard_normal((ns, 2 * rows)) * 2).astype(np.float32)
+            buf[:, code:code + 8 * rows] = prm.view(np.uint8)
+        elif f in (1, 2):
+            code = oracle.slot_bytes_needed(f, T, H, D) - 4 * rows
+            prm = np.abs(rng.standard_normal((ns, rows))).astype(np.float32)
+            buf[:, code:code + 4 * rows] = prm.view(np.uint8)
+        pools[f] = (buf.reshape(-1), sb, ns)
+    n_blocks = 40
+    table = np.zeros((n_blocks, 4), np.uint32)
+    refs = block_wide_scale_refs(rng, n_blocks)
+    for i in range(n_blocks):
+        f = int(rng.integers(0, 4))
+        mode, sref = refs[i] if i % 4 else (0, 0)
+        info = f | mode << 4 | (1 << 6) | (int(rng.integers(0, T + 1)) << 10)
+        table[i] = (int(rng.integers(0, 6)), info, sref, i)
+    table[7] = (1, 1 | 3 << 4 | 1 << 6 | T << 10, 5, 7)  # kExternal: rejected
+    arena = rng.permutation(n_blocks).astype(np.uint32)
+    segs = np.array([[0, 13], [13, 0], [13, 27]], np.uint32)
+    total = int(segs[:, 1].sum())
+    a = np.full(total * elems, 0x1111, np.uint16)
+    b = np.full(total * elems, 0x1111, np.uint16)
+    ea = oracle.gather_dequant(pools, T, H, D, 1, table, arena, segs, a)
+    eb = ref.gather_dequant(pools, T, H, D, 1, table, arena, segs, b, threads=3)
+    assert ea == eb == 1 << 7
+    assert np.array_equal(a, b)
+    # both the rejected blocks (untouched) and decoded block-wide blocks are present
+    per_block = a.reshape(total, elems)
+    assert (per_block == 0x1111).all(axis=1).sum() >= 2
+    assert (per_block != 0x1111).all(axis=1).sum() >= 20
 
 
 def test_quantize_rows_oracle_equals_reference(oracle, ref):

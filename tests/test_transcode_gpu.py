@@ -90,3 +90,56 @@ def test_transcode_rejects_nonfinite_rows_and_bad_jobs(hlkv_lib, oracle, cuda_de
     after = host_pools(wl)
     for f in before:
         assert np.array_equal(after[f][0], before[f][0]), f
+
+
+def test_transcode_from_block_wide_sources(hlkv_lib, oracle, cuda_device):
+    """Source blocks with block-wide parameters (their descriptors' scale modes 1 and 2,
+    passed in the job) are decoded with those parameters; a job whose source mode is 3 is
+    skipped with HLKV_ERR_SCALE_MODE.  Byte-exact against the oracle, then committed (scale
+    mode kNone) and gathered."""
+    import torch
+    from helpers import block_wide_scale_refs
+    from hlkv.workload import build_workload
+    T, H, D = 16, 4, 128
+    fm = [[1, 3, 2, 1, 3, 3], [2, 1, 3]]
+    wl = build_workload(fm, T=T, H=H, D=D, seed=17, spare_slots=16)
+    ids = []
+    for s in wl.seqs:
+        ids += wl.table.sequence_block_ids(s)[1]
+    rng = np.random.default_rng(18)
+    refs = block_wide_scale_refs(rng, len(ids), moderate=True)
+    modes = {}
+    for k, bid in enumerate(ids):
+        if k % 4 != 3:
+            assert wl.table.set_scale(wl.table.handle_of(bid), *refs[k]) == 0
+            modes[bid] = refs[k]
+    targets = {1: 3, 2: 1, 3: 1}
+    picks = [(bid, targets[int(wl.table.device_descriptor(bid)[1] & 0xF)]) for bid in ids]
+    jobs = _jobs_for(wl, picks)
+    for r, (bid, _) in enumerate(picks):
+        jobs[r, 5], jobs[r, 6] = modes.get(bid, (0, 0))
+    bad = np.array([[1, 0, 3, 0, T, 3, 7, 0]], np.uint32)  # source scale mode 3
+    jobs = np.concatenate([jobs, bad])
+    before = host_pools(wl)
+    d_jobs = torch.from_numpy(jobs.view(np.int32)).cuda()
+    err = torch.zeros(1, dtype=torch.int32, device="cuda")
+    hlkv_lib.transcode(wl.hlkv_pools(), wl.layout, d_jobs, err)
+    torch.cuda.synchronize()
+    oerr = oracle.transcode(before, T, H, D, jobs)
+    assert int(err.item()) == oerr == 1 << 7
+    after = host_pools(wl)
+    for f in before:
+        diff = np.nonzero(after[f][0] != before[f][0])[0]
+        assert diff.size == 0, f"format {f}: {diff.size} bytes differ"
+    for bid, _ in picks:
+        assert wl.table.commit_format_change(wl.table.handle_of(bid), 0, 0) == 0
+    wl.dt.sync(wl.table)
+    n = wl.total_blocks * wl.block_elems
+    out = torch.empty(n, dtype=torch.int16, device="cuda")
+    e = torch.zeros(1, dtype=torch.int32, device="cuda")
+    hlkv_lib.gather_dequant(wl.hlkv_pools(), wl.layout, wl.dt.table_ptr, wl.dt.table_size,
+                            wl.dt.arena_ptr, wl.dt.arena_size, wl.segs, out, e)
+    torch.cuda.synchronize()
+    want, gerr = oracle_gather(oracle, wl)
+    assert int(e.item()) == gerr == 0
+    assert np.array_equal(out.cpu().numpy().view(np.uint16), want)
