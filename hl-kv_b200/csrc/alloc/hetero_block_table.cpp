@@ -10,8 +10,10 @@
 // replays the same seeded call stream on both implementations and compares
 // every word.
 #include "hl_allocator/hetero_block_table.hpp"
+#include "hl_allocator/snapshot_io.hpp"
 
 #include <algorithm>
+#include <cstring>
 #include <limits>
 #include <stdexcept>
 
@@ -548,6 +550,122 @@ TableStats HeteroBlockTable::stats() const {
   st.pending_descriptor_patches = dirty_ids_.size();
   st.pending_id_patches = arena_.pending_patches();
   return st;
+}
+
+// ---- snapshot ------------------------------------------------------------------------
+//
+// Image layout (host byte order; u32 lists are a count then the values):
+//   u64 magic "HLKVSNAP", u32 image version, u32 ABI version,
+//   u32 max_blocks, u32 block_tokens, u32 blocks in use, u64 committed format changes,
+//   u32 pool count, per pool {u32 format, u32 slot_bytes, u32 capacity, u32 list free slots},
+//   the block records (32 B each), u32 list free block ids,
+//   u32 sequence count, per sequence {u32 offset, capacity, length, generation, live},
+//   u32 list free sequence ids, the id arena (IdArena::snapshot),
+//   u64 FNV-1a checksum of everything before it.
+
+namespace {
+constexpr std::uint64_t kSnapshotMagic = 0x50414E53564B4C48ull;  // bytes "HLKVSNAP" little-endian
+constexpr std::uint32_t kSnapshotVersion = 1;
+constexpr std::size_t kSeqBytes = 5 * sizeof(std::uint32_t);
+}  // namespace
+
+std::vector<std::byte> HeteroBlockTable::snapshot() const {
+  std::vector<std::byte> out;
+  detail::SnapshotWriter w(out);
+  w.u64(kSnapshotMagic);
+  w.u32(kSnapshotVersion);
+  w.u32(kAbiVersion);
+  w.u32(static_cast<std::uint32_t>(records_.size()));
+  w.u32(block_tokens_);
+  w.u32(in_use_);
+  w.u64(committed_changes_);
+  std::uint32_t n_pools = 0;
+  for (const SlotPool& p : pools_) n_pools += p.present ? 1u : 0u;
+  w.u32(n_pools);
+  for (std::uint32_t f = 0; f < kMaxFormats; ++f) {
+    const SlotPool& p = pools_[f];
+    if (!p.present) continue;
+    w.u32(f);
+    w.u32(p.slot_bytes);
+    w.u32(p.capacity);
+    w.u32s(p.lifo);
+  }
+  w.bytes(records_.data(), records_.size() * sizeof(BlockDescriptor));
+  w.u32s(free_ids_);
+  w.u32(static_cast<std::uint32_t>(seqs_.size()));
+  for (const Seq& q : seqs_) {
+    w.u32(q.seg.offset);
+    w.u32(q.seg.capacity);
+    w.u32(q.seg.length);
+    w.u32(q.generation);
+    w.u32(q.live ? 1u : 0u);
+  }
+  w.u32s(free_seqs_);
+  arena_.snapshot(w);
+  w.u64(detail::snapshot_checksum(out));
+  return out;
+}
+
+Status HeteroBlockTable::restore(std::span<const std::byte> image, std::unique_ptr<HeteroBlockTable>& out) {
+  constexpr std::size_t kSum = sizeof(std::uint64_t);
+  if (image.size() < kSum) return Status::kCorrupt;
+  const std::span<const std::byte> body = image.first(image.size() - kSum);
+  std::uint64_t sum = 0;
+  std::memcpy(&sum, image.data() + body.size(), kSum);
+  if (sum != detail::snapshot_checksum(body)) return Status::kCorrupt;
+
+  detail::SnapshotReader r(body);
+  std::uint64_t magic = 0, committed = 0;
+  std::uint32_t version = 0, abi = 0, max_blocks = 0, block_tokens = 0, in_use = 0, n_pools = 0;
+  if (!r.u64(magic) || magic != kSnapshotMagic || !r.u32(version) || version != kSnapshotVersion ||
+      !r.u32(abi) || abi != kAbiVersion || !r.u32(max_blocks) || !r.u32(block_tokens) || !r.u32(in_use) ||
+      !r.u64(committed) || !r.u32(n_pools) || n_pools > kMaxFormats) {
+    return Status::kCorrupt;
+  }
+  TableConfig config;
+  config.max_blocks = max_blocks;
+  config.block_tokens = block_tokens;
+  std::array<std::vector<std::uint32_t>, kMaxFormats> lifos;
+  for (std::uint32_t i = 0; i < n_pools; ++i) {
+    std::uint32_t f = 0, slot_bytes = 0, capacity = 0;
+    if (!r.u32(f) || f >= kMaxFormats || !r.u32(slot_bytes) || !r.u32(capacity) || !r.u32s(lifos[f], capacity)) {
+      return Status::kCorrupt;
+    }
+    config.pools.push_back(PoolConfig{FormatId{static_cast<std::uint8_t>(f)}, slot_bytes, capacity});
+  }
+  if (validate_config(config) != Status::kOk) return Status::kCorrupt;
+  // The records are in the image: bound the allocation by it.
+  if (std::size_t{max_blocks} * sizeof(BlockDescriptor) > r.remaining()) return Status::kCorrupt;
+  auto t = std::make_unique<HeteroBlockTable>(config);
+  if (!r.bytes(t->records_.data(), std::size_t{max_blocks} * sizeof(BlockDescriptor)) ||
+      !r.u32s(t->free_ids_, max_blocks)) {
+    return Status::kCorrupt;
+  }
+  t->free_ids_.reserve(max_blocks);
+  for (const PoolConfig& pc : config.pools) {
+    SlotPool& p = t->pools_[raw(pc.format)];
+    p.lifo = std::move(lifos[raw(pc.format)]);
+    p.lifo.reserve(p.capacity);  // the stacks never allocate when slots come back
+  }
+  std::uint32_t n_seqs = 0;
+  if (!r.u32(n_seqs) || std::size_t{n_seqs} * kSeqBytes > r.remaining()) return Status::kCorrupt;
+  t->seqs_.resize(n_seqs);
+  for (Seq& q : t->seqs_) {
+    std::uint32_t live = 0;
+    if (!r.u32(q.seg.offset) || !r.u32(q.seg.capacity) || !r.u32(q.seg.length) || !r.u32(q.generation) ||
+        !r.u32(live) || live > 1) {
+      return Status::kCorrupt;
+    }
+    q.live = live != 0;
+  }
+  if (!r.u32s(t->free_seqs_, n_seqs) || !t->arena_.restore(r) || r.remaining() != 0) return Status::kCorrupt;
+  t->in_use_ = in_use;
+  t->committed_changes_ = committed;
+  // A fresh table already lists every descriptor as pending; the arena's restore did the
+  // same for every entry.
+  if (!t->validate().ok()) return Status::kCorrupt;
+  out = std::move(t);
+  return Status::kOk;
 }
 
 ValidationReport HeteroBlockTable::validate() const {

@@ -6,6 +6,7 @@
 // relocation copies entries in order and marks each one dirty, and collect()
 // reports dirty offsets in marking order.
 #include "hl_allocator/id_arena.hpp"
+#include "hl_allocator/snapshot_io.hpp"
 
 #include <algorithm>
 #include <bit>
@@ -125,6 +126,41 @@ std::uint64_t IdArena::free_entries() const noexcept {
     sum += std::uint64_t{parked_[c].size()} * class_capacity(c);
   }
   return sum;
+}
+
+void IdArena::snapshot(detail::SnapshotWriter& w) const {
+  w.u32s(ids_);
+  for (std::uint32_t c = 0; c < kNumClasses; ++c) w.u32s(parked_[c]);
+  for (std::uint32_t c = 0; c < kNumClasses; ++c) w.u32(carved_[c]);
+}
+
+bool IdArena::restore(detail::SnapshotReader& r) {
+  std::vector<std::uint32_t> ids;
+  if (!r.u32s(ids, kMaxEntries)) return false;
+  std::array<std::vector<std::uint32_t>, kNumClasses> parked;
+  for (std::uint32_t c = 0; c < kNumClasses; ++c) {
+    if (!r.u32s(parked[c], ids.size())) return false;
+  }
+  std::array<std::uint32_t, kNumClasses> carved{};
+  std::uint64_t carved_entries = 0;
+  for (std::uint32_t c = 0; c < kNumClasses; ++c) {
+    if (!r.u32(carved[c])) return false;
+    carved_entries += std::uint64_t{carved[c]} * class_capacity(c);
+  }
+  // The segments must tile the arena before anything is sized from the counts.
+  if (carved_entries != ids.size()) return false;
+  const std::size_t n = ids.size();
+  ids_ = std::move(ids);
+  is_dirty_.assign(n, 1);
+  dirty_order_.clear();
+  dirty_order_.reserve(n);
+  for (std::size_t k = 0; k < n; ++k) dirty_order_.push_back(static_cast<std::uint32_t>(k));
+  for (std::uint32_t c = 0; c < kNumClasses; ++c) {
+    parked_[c] = std::move(parked[c]);
+    ensure_capacity(parked_[c], std::max<std::size_t>(carved[c], parked_[c].size()));
+  }
+  carved_ = carved;
+  return true;
 }
 
 std::string IdArena::validate(std::span<const Segment> live) const {

@@ -2,6 +2,7 @@
 // hl::quant::cuda entry points over the C kernels' launchers.
 #include <cstddef>
 #include <cstring>
+#include <memory>
 #include <new>
 #include <span>
 #include <vector>
@@ -17,6 +18,7 @@ struct hlkv_table {
   HeteroBlockTable t;
   ExecDelta scratch_delta;  // reused by hlkv_table_collect_delta
   explicit hlkv_table(const TableConfig& c) : t(c) {}
+  explicit hlkv_table(HeteroBlockTable&& restored) : t(std::move(restored)) {}
 };
 
 struct hlkv_device_tables {
@@ -96,6 +98,35 @@ int hlkv_table_create(const HlkvTableConfig* config, hlkv_table** out) {
 }
 
 void hlkv_table_destroy(hlkv_table* table) { delete table; }
+
+int hlkv_table_snapshot(const hlkv_table* t, void* buf, size_t cap, size_t* size) {
+  if (t == nullptr || size == nullptr) return HLKV_STATUS_INVALID_ARGUMENT;
+  std::vector<std::byte> image;
+  try {
+    image = t->t.snapshot();
+  } catch (const std::bad_alloc&) {
+    return HLKV_STATUS_CAPACITY_EXCEEDED;
+  }
+  *size = image.size();
+  if (buf == nullptr || cap < image.size()) return buf == nullptr ? HLKV_STATUS_OK : HLKV_STATUS_INVALID_ARGUMENT;
+  std::memcpy(buf, image.data(), image.size());
+  return HLKV_STATUS_OK;
+}
+
+int hlkv_table_restore(const void* buf, size_t size, hlkv_table** out) {
+  if (out == nullptr || (buf == nullptr && size > 0)) return HLKV_STATUS_INVALID_ARGUMENT;
+  *out = nullptr;
+  try {
+    std::unique_ptr<HeteroBlockTable> table;
+    const Status s = HeteroBlockTable::restore(
+        std::span<const std::byte>(static_cast<const std::byte*>(buf), size), table);
+    if (s != Status::kOk) return st(s);
+    *out = new hlkv_table(std::move(*table));
+  } catch (const std::bad_alloc&) {
+    return HLKV_STATUS_CAPACITY_EXCEEDED;
+  }
+  return HLKV_STATUS_OK;
+}
 
 int hlkv_table_allocate(hlkv_table* t, const HlkvAllocRequest* req, HlkvHandle* out) {
   if (t == nullptr || req == nullptr || out == nullptr) return HLKV_STATUS_INVALID_ARGUMENT;

@@ -147,6 +147,8 @@ SIGNATURES: list[tuple[str, object, list]] = [
     ("hlkv_table_validate_config", _int, [_P(TableConfig)]),
     ("hlkv_table_create", _int, [_P(TableConfig), _P(_vp)]),
     ("hlkv_table_destroy", None, [_vp]),
+    ("hlkv_table_snapshot", _int, [_vp, _vp, _sz, _P(_sz)]),
+    ("hlkv_table_restore", _int, [_vp, _sz, _P(_vp)]),
     ("hlkv_table_allocate", _int, [_vp, _P(AllocRequest), _P(Handle)]),
     ("hlkv_table_retain", _int, [_vp, Handle]),
     ("hlkv_table_release", _int, [_vp, Handle]),
@@ -217,6 +219,12 @@ class HlkvError(RuntimeError):
     pass
 
 
+def check_table(status: int, what: str) -> None:
+    """Raises on a non-OK table status."""
+    if status != Status.OK:
+        raise HlkvError(f"{what}: table status {status}")
+
+
 def check(status: int, what: str) -> None:
     """Raises on a non-OK device status (with the CUDA error for CUDA_ERROR)."""
     if status != OK:
@@ -275,6 +283,26 @@ class Table:
         arr = (PoolConfig * max(len(pools), 1))(*[PoolConfig(f, sb, ns) for f, sb, ns in pools])
         cfg = TableConfig(max_blocks, block_tokens, len(pools), C.cast(arr, _P(PoolConfig)))
         return lib().hlkv_table_validate_config(C.byref(cfg))
+
+    def snapshot(self) -> bytes:
+        """The table's versioned binary image (hlkv_table_snapshot)."""
+        n = _sz()
+        check_table(lib().hlkv_table_snapshot(self.h, None, 0, C.byref(n)), "hlkv_table_snapshot")
+        buf = (C.c_char * max(n.value, 1))()
+        check_table(lib().hlkv_table_snapshot(self.h, buf, n.value, C.byref(n)), "hlkv_table_snapshot")
+        return bytes(buf[:n.value])
+
+    @classmethod
+    def restore(cls, image: bytes) -> tuple[int, "Table | None"]:
+        """(status, table rebuilt from a snapshot image, or None) -- hlkv_table_restore."""
+        h = _vp()
+        st = lib().hlkv_table_restore(image, len(image), C.byref(h))
+        if st != Status.OK:
+            return st, None
+        t = cls.__new__(cls)
+        t._keep = None
+        t.h = h
+        return st, t
 
     def close(self) -> None:
         if getattr(self, "h", None):

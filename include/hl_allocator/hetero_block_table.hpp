@@ -24,7 +24,9 @@
 // immediately, so a caller must not free a slot that queued GPU work still
 // reads (wait for the step's stream event first).
 #include <array>
+#include <cstddef>
 #include <cstdint>
+#include <memory>
 #include <span>
 #include <string>
 #include <vector>
@@ -196,6 +198,20 @@ class HeteroBlockTable {
   [[nodiscard]] std::uint32_t slot_bytes(FormatId format) const noexcept;
 
   [[nodiscard]] TableStats stats() const;
+
+  // -- snapshot (no counterpart in the reference, whose ABI v1 lists the missing
+  //    snapshot API among its limitations, hl_allocator_abi.md section 9) ------------
+  /// A versioned binary image of the whole table: configuration, block records, free
+  /// lists, pool stacks, sequences and id arena, with a checksum trailer.
+  [[nodiscard]] std::vector<std::byte> snapshot() const;
+  /// Rebuilds the table that `image` describes into `out`.  kCorrupt, with `out`
+  /// untouched, for an image that is short, damaged (checksum), of another version, ABI
+  /// or byte order, or inconsistent (validate()).  The restored table behaves as the
+  /// original from then on (same handles, free lists and arena layout), except that
+  /// every descriptor and arena entry is pending: its first collect_delta() carries the
+  /// whole device image, for a fresh device mirror.
+  [[nodiscard]] static Status restore(std::span<const std::byte> image,
+                                      std::unique_ptr<HeteroBlockTable>& out);
   [[nodiscard]] ValidationReport validate() const;
 
  private:

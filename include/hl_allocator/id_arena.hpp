@@ -38,6 +38,11 @@ struct SequenceSegment {
   friend constexpr bool operator==(SequenceSegment, SequenceSegment) noexcept = default;
 };
 
+namespace detail {
+class SnapshotWriter;
+class SnapshotReader;
+}  // namespace detail
+
 class IdArena {
  public:
   static constexpr std::uint32_t kMinSegment = 8;
@@ -76,6 +81,13 @@ class IdArena {
   [[nodiscard]] std::size_t pending_patches() const noexcept { return dirty_order_.size(); }
   /// Total capacity parked on the free lists.
   [[nodiscard]] std::uint64_t free_entries() const noexcept;
+
+  /// Appends the arena (entries, free lists, carved segment counts) to a table snapshot.
+  void snapshot(detail::SnapshotWriter& w) const;
+  /// Replaces the arena with one that snapshot() wrote; every entry is then pending, so
+  /// the next collect() reports all of them.  False, with nothing changed, on a malformed
+  /// image.
+  [[nodiscard]] bool restore(detail::SnapshotReader& r);
 
   /// Checks that `live` plus the free lists tile the array exactly and that the
   /// dirty bookkeeping is consistent; "" when it holds, else the first problem.

@@ -349,6 +349,22 @@ typedef struct {
 int hlkv_table_validate_config(const HlkvTableConfig* config);
 int hlkv_table_create(const HlkvTableConfig* config, hlkv_table** out);
 void hlkv_table_destroy(hlkv_table* table);
+/*
+ * Versioned binary image of the whole table (HeteroBlockTable::snapshot: configuration,
+ * records, free lists, pool stacks, sequences, id arena, checksum).  *size receives its
+ * length; the image is written when buf holds cap >= *size bytes (buf NULL: size only;
+ * cap too small: HLKV_STATUS_INVALID_ARGUMENT, nothing written).  No counterpart in the
+ * reference: its ABI v1 lists the missing snapshot API among its limitations
+ * (hl_allocator_abi.md, section 9).
+ */
+int hlkv_table_snapshot(const hlkv_table* t, void* buf, size_t cap, size_t* size);
+/*
+ * A new table rebuilt from a snapshot image (HeteroBlockTable::restore); destroy it with
+ * hlkv_table_destroy.  HLKV_STATUS_CORRUPT for a short, damaged, foreign or inconsistent
+ * image.  Every descriptor and arena entry of the restored table is pending, so the first
+ * sync of a fresh hlkv_device_tables uploads the whole device image.
+ */
+int hlkv_table_restore(const void* buf, size_t size, hlkv_table** out);
 
 int hlkv_table_allocate(hlkv_table* t, const HlkvAllocRequest* req, HlkvHandle* out);
 int hlkv_table_retain(hlkv_table* t, HlkvHandle block);

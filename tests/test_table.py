@@ -158,3 +158,134 @@ def test_append_tokens_decode_driver(hlkv_lib):
     assert a.release_sequence(seqs_a[1]) == 0
     st, targets, done = a.append_tokens(seqs_a, np.ones(3, np.uint32), 1)
     assert st == h.Status.STALE_HANDLE and done == 1
+
+
+def _random_ops(t, rng, steps, seqs, transcoding, formats=(0, 1, 3)):
+    """A reproducible random workload over the public table API (the mix of the reference's
+    randomized test, test_hetero_block_table.cpp:675-784); returns what each step returned."""
+    log = []
+
+    def random_block():
+        if not seqs:
+            return None
+        st, ids = t.sequence_block_ids(seqs[int(rng.integers(len(seqs)))])
+        return t.handle_of(ids[int(rng.integers(len(ids)))]) if ids else None
+
+    for _ in range(steps):
+        op = int(rng.integers(12))
+        if op == 0:
+            st, s = t.create_sequence()
+            log.append((op, st, (s.id, s.generation)))
+            if st == 0:
+                seqs.append(s)
+        elif op in (1, 2) and seqs:
+            st, b = t.append_block(seqs[int(rng.integers(len(seqs)))], formats[int(rng.integers(3))],
+                                   int(rng.integers(0, 17)))
+            log.append((op, st, (b.id, b.generation)))
+        elif op == 3 and (b := random_block()) is not None:
+            log.append((op, t.seal(b), t.append_shared_block(seqs[int(rng.integers(len(seqs)))], b)))
+        elif op == 4 and (b := random_block()) is not None:
+            t.seal(b)
+            st, fc = t.begin_format_change(b, formats[int(rng.integers(3))])
+            log.append((op, st, tuple(fc) if st == 0 else None))
+            if st == 0:
+                transcoding.append(b)
+        elif op == 5 and transcoding:
+            b = transcoding.pop(int(rng.integers(len(transcoding))))
+            log.append((op, t.commit_format_change(b, 1, 0x3F800000) if rng.integers(2) else t.abort_format_change(b)))
+        elif op == 6 and (b := random_block()) is not None:
+            log.append((op, t.set_residency(b, int(rng.integers(3)))))
+        elif op == 7 and (b := random_block()) is not None:
+            log.append((op, t.set_valid_tokens(b, int(rng.integers(17)))))
+        elif op == 8 and (b := random_block()) is not None:
+            log.append((op, t.set_scale(b, int(rng.integers(3)), int(rng.integers(1 << 32)))))
+        elif op >= 9 and seqs:
+            i = int(rng.integers(len(seqs)))
+            st = t.release_sequence(seqs[i])
+            log.append((op, st))
+            if st == 0:
+                seqs.pop(i)
+    return log
+
+
+def _mirror_apply(mirror_table, mirror_arena, d):
+    """The reference's ExecMirror::apply (tests/project1/exec_mirror.hpp:23-49) on arrays."""
+    if d.arena_size > mirror_arena.size:
+        grown = np.zeros(d.arena_size, np.uint32)
+        grown[:mirror_arena.size] = mirror_arena
+        mirror_arena = grown
+    for p in d.descriptor_patches:
+        mirror_table[p[3]] = p
+    for off, bid in d.id_patches:
+        mirror_arena[off] = bid
+    return mirror_table, mirror_arena
+
+
+def test_snapshot_restore_round_trip(hlkv_lib):
+    """A restored table re-snapshots to the same bytes, its first delta rebuilds the same
+    device mirror the original's deltas built, and from then on both tables answer the same
+    random operations with the same statuses, handles and deltas."""
+    h = hlkv_lib
+    pools = [(0, 4096, 40), (1, 2048, 40), (3, 1088, 60)]
+    a = h.Table(120, pools, block_tokens=16)
+    rng = np.random.default_rng(77)
+    seqs, transcoding = [], []
+    mt = np.zeros((120, 4), np.uint32)
+    ma = np.zeros(0, np.uint32)
+    for _ in range(6):
+        _random_ops(a, rng, 400, seqs, transcoding)
+        mt, ma = _mirror_apply(mt, ma, a.collect_delta())
+    image = a.snapshot()
+    st, b = h.Table.restore(image)
+    assert st == 0 and b is not None
+    assert b.snapshot() == image
+    # the restored table's first delta is the whole device image
+    db = b.collect_delta()
+    assert db.descriptor_patches.shape[0] == 120 and db.id_patches.shape[0] == db.arena_size
+    mt_b, ma_b = _mirror_apply(np.zeros((120, 4), np.uint32), np.zeros(0, np.uint32), db)
+    assert np.array_equal(mt_b, mt)
+    for s in seqs:
+        st, ids = a.sequence_block_ids(s)
+        assert b.sequence_block_ids(s) == (st, ids)
+    st, seg_a = a.batch_segments(seqs)
+    st_b, seg_b = b.batch_segments(seqs)
+    assert st == st_b == 0 and np.array_equal(seg_a, seg_b)
+    for off, ln in seg_a:
+        assert np.array_equal(ma_b[off:off + ln], ma[off:off + ln])
+    # the same operations from here on: same answers, same deltas
+    seqs_b, tr_b = list(seqs), list(transcoding)
+    for k in range(4):
+        la = _random_ops(a, np.random.default_rng(1000 + k), 300, seqs, transcoding)
+        lb = _random_ops(b, np.random.default_rng(1000 + k), 300, seqs_b, tr_b)
+        assert la == lb, k
+        da, dbk = a.collect_delta(), b.collect_delta()
+        assert np.array_equal(da.descriptor_patches, dbk.descriptor_patches), k
+        assert np.array_equal(da.id_patches, dbk.id_patches), k
+        assert (da.descriptor_table_size, da.arena_size) == (dbk.descriptor_table_size, dbk.arena_size)
+    assert b.validate()[0] == 0
+
+
+def test_snapshot_rejects_damaged_images(hlkv_lib):
+    import ctypes as C
+    h = hlkv_lib
+    t = h.Table(16, [(1, 2048, 8), (3, 1088, 8)], block_tokens=4)
+    st, s = t.create_sequence()
+    for f in (1, 3, 1):
+        assert t.append_block(s, f, 2)[0] == 0
+    image = t.snapshot()
+    corrupt = 10  # HLKV_STATUS_CORRUPT
+    for bad in (b"", image[:-1], image[:40], image + b"\0",
+                image[:100] + bytes([image[100] ^ 1]) + image[101:]):
+        assert h.Table.restore(bad)[0] == corrupt
+    # a foreign version with a valid checksum is still rejected
+    body = bytearray(image[:-8])
+    body[8] = 2
+    fnv = 0xCBF29CE484222325
+    for byte in body:
+        fnv = ((fnv ^ byte) * 0x100000001B3) & 0xFFFFFFFFFFFFFFFF
+    assert h.Table.restore(bytes(body) + fnv.to_bytes(8, "little"))[0] == corrupt
+    # snapshot into a buffer that is too small: nothing written
+    n = C.c_size_t()
+    small = (C.c_char * 8)()
+    assert h.lib().hlkv_table_snapshot(t.h, small, 8, C.byref(n)) == 6  # INVALID_ARGUMENT
+    assert n.value == len(image) and bytes(small) == b"\0" * 8
