@@ -90,6 +90,13 @@ WORKLOADS = {
                       attn=True, q_heads=64,
                       name="decode attention fused with dequant, long context: 16 seq x 131072 tok "
                            "(one layer), 8 KV heads x 128, 64 query heads, INT4 .85 / E4M3 .10 / FP16 .05"),
+    # Decode attention over a serving-like batch of mixed lengths: 8 sequences of 16,384
+    # tokens among 56 of 512 (mixed formats as 'mixed'), where one CTA per (sequence, KV head)
+    # leaves most SMs idle while the long sequences finish.
+    "attn_varied": dict(nseq=64, blocks=[1024] * 8 + [32] * 56, probs=(0.25, 0.5, 0.0, 0.25), scaling="weak",
+                        attn=True, q_heads=32,
+                        name="decode attention fused with dequant, mixed lengths: 8 seq x 16384 tok + 56 seq x "
+                             "512 tok, 8 KV heads x 128, 32 query heads, FP16 .25 / E4M3 .5 / INT4 .25"),
     # Config 1's data as one contiguous E4M3 array (8,388,608 values, 128-value groups):
     # the drop-in hlkv_dequantize_fp8_to_fp16 against the reference's own GPU kernel.
     "flat_e4m3": dict(n=8_388_608, group=128, fmt=1, scaling="weak", flat=True,
@@ -718,7 +725,8 @@ def cpu_encode_sample(tokens, tail_fmt, H: int, D: int, n: int, min_wall_s: floa
 
 
 def run_attention(args) -> None:
-    """hlkv_decode_attention over a whole cache per step (one launch)."""
+    """Decode attention over a whole cache per step: one launch, or with a split the kernel
+    and a merge, or in balanced mode a prefix pass, the kernel and a merge."""
     import numpy as np
     import torch
     import torch.distributed as dist
@@ -746,19 +754,34 @@ def run_attention(args) -> None:
     # With at least two (sequence, KV head) units per SM the grid already fills the GPU and a
     # split only adds the merge; with fewer, each unit is split so that about 32 CTAs per SM
     # are launched (long sequences, few of them).
+    # Uneven lengths (the longest sequence at least 1.5x the mean): the balanced mode over one
+    # CTA per resident slot (4 per SM), since per-unit CTAs would leave SMs idle while the
+    # long sequences finish (measured 0.195 ms against 0.696 ms unsplit, 0.226 ms at 16 splits).
     sms = torch.cuda.get_device_properties(torch.cuda.current_device()).multi_processor_count
     units = nseq * wl.H
     auto = 1 if units >= 2 * sms else max(1, -(-32 * sms // units))
     splits = args.splits if args.splits else auto
+    lens = wl.segs_host[:, 1].astype(np.float64)
+    uneven = lens.size > 0 and lens.max() >= 1.5 * lens.mean()
+    ctas = args.ctas if args.ctas else (4 * sms if uneven and not args.splits else 0)
     ws = None
-    if splits > 1:
+    if ctas:
+        # balanced: the units' blocks cut into `ctas` equal ranges
+        ws = torch.empty(hlkv.decode_attention_balanced_workspace_bytes(nseq, wl.H, D, ctas), dtype=torch.uint8,
+                         device="cuda")
+    elif splits > 1:
         ws = torch.empty(hlkv.decode_attention_workspace_bytes(nseq, wl.H, D, splits), dtype=torch.uint8,
                          device="cuda")
 
     def step():
-        hlkv.decode_attention_split(pools, wl.layout, wl.dt.table_ptr, wl.dt.table_size, wl.dt.arena_ptr,
-                                    wl.dt.arena_size, wl.segs, q, qh, scale, splits, ws, out, err,
-                                    stream=stream)
+        if ctas:
+            hlkv.decode_attention_balanced(pools, wl.layout, wl.dt.table_ptr, wl.dt.table_size, wl.dt.arena_ptr,
+                                           wl.dt.arena_size, wl.segs, q, qh, scale, ctas, ws, out, err,
+                                           stream=stream)
+        else:
+            hlkv.decode_attention_split(pools, wl.layout, wl.dt.table_ptr, wl.dt.table_size, wl.dt.arena_ptr,
+                                        wl.dt.arena_size, wl.segs, q, qh, scale, splits, ws, out, err,
+                                        stream=stream)
 
     # Algorithmic bytes: codes + row parameters of the K and V rows read, 20 B of descriptor
     # and arena entry per block, the queries read and the outputs written.
@@ -800,7 +823,8 @@ def run_attention(args) -> None:
             "data": "synthetic (seeded N(0,1) + outlier channels; N(0,1) queries)",
             "config": {"workload": spec["name"], "bytes_per_step_per_gpu": nbytes,
                        "kv_tokens_per_step_per_gpu": tokens, "query_heads": qh,
-                       "splits_per_sequence_head": splits,
+                       "splits_per_sequence_head": None if ctas else splits,
+                       "balanced_ctas": ctas or None,
                        "l2": "L2 flushed between launches" if flush is not None else "no flush needed",
                        "parallelism": f"sequence-sharded x{world}, no collective on the data path"},
             "kv_tokens_per_s": round(world * tokens * args.steps / (total_ms / 1e3), 1),
@@ -811,7 +835,7 @@ def run_attention(args) -> None:
                          "launch_ms": round(mean_ms, 5)},
             "e2e": {"value": None, "unit": "GB/s", "h2d_bytes_per_step": None, "d2h_bytes_per_step": None,
                     "reason": "the cache is resident in HBM; end to end is measured on 'mixed'"},
-            "gpu_launches": args.steps,
+            "gpu_launches": args.steps * (3 if ctas else (2 if splits > 1 else 1)),  # prefix, kernel, merge
             "clocks": clocks.summary(c0, c1),
             "cpu_baseline": None,
         }), flush=True)
@@ -1211,6 +1235,9 @@ def main() -> None:
     ap.add_argument("--workload", choices=sorted(WORKLOADS), default="mixed")
     ap.add_argument("--e2e-steps", type=int, default=10)
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--ctas", type=int, default=0,
+                    help="attention workloads: balanced mode over this many CTAs (0 = balanced over 4 per SM "
+                         "when sequence lengths are uneven, else split mode)")
     ap.add_argument("--splits", type=int, default=0,
                     help="attention workloads: CTAs per (sequence, KV head); 0 = none with >= 2 units per SM, else about 32 CTAs per SM")
     args = ap.parse_args()

@@ -52,8 +52,19 @@ struct AttnParams {
   uint32_t T, H, layout_id, q_heads;
   float qscale;     // softmax_scale * log2(e)
   uint32_t splits;  // CTAs per (sequence, KV head), each over a contiguous share of the blocks
-  float* ws;        // splits > 1: per CTA, kPart floats of partial results
+  float* ws;        // splits > 1 or balanced: kPart floats of partial results per slot
+  // Balanced mode: CTA c takes blocks [c W / G, (c + 1) W / G) of all units laid end to end
+  // (unit u = seq * H + h holds segs[seq].y blocks; W = prefix[nseq]), one piece per unit
+  // that range meets, and writes piece (c, u) to slot c + u.
+  uint32_t balanced;
+  const uint64_t* prefix;  // [nseq + 1]: H * (blocks of the sequences before)
 };
+
+// The CTA of a balanced launch over W blocks and G CTAs that holds block x: CTA c takes
+// [floor(c W / G), floor((c + 1) W / G)), so it is the largest c with floor(c W / G) <= x.
+__device__ __forceinline__ uint32_t balanced_cta(uint64_t x, uint64_t W, uint64_t G) {
+  return static_cast<uint32_t>(((x + 1) * G - 1) / W);
+}
 
 // Partial result of one CTA for its (sequence, KV head) and share of the blocks: the max
 // (exp2 domain) and the sum per query column, then the unnormalised outputs.
@@ -243,11 +254,48 @@ __global__ void __launch_bounds__(kAttnThreads, 4) decode_attention_kernel(const
   __shared__ const uint8_t* s_payload[kAttnThreads];
   __shared__ uint32_t s_fv[kAttnThreads];  // format | valid_tokens << 8 | scale mode << 30 (format 4: skip)
   __shared__ uint32_t s_sref[kAttnThreads];  // scale_ref of blocks with block-wide parameters
-  const uint32_t unit = blockIdx.x / p.splits, split = blockIdx.x % p.splits;
-  const uint32_t seq = unit / p.H, h = unit % p.H;
   const uint32_t lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
   const uint32_t grp = lane >> 2, quad = lane & 3;
   WarpTiles<kD>& w = reinterpret_cast<WarpTiles<kD>*>(s_raw)[warp];
+  const uint32_t T = p.T, H = p.H;
+
+  // The CTA's pieces: (seq, h, blocks [b0, b1)), each written to the output directly or
+  // to a partial slot.  Split mode: one piece.  Balanced mode: the units its range meets.
+  uint64_t x = 0, x_end = 0, W = 0;
+  if (p.balanced) {
+    W = p.prefix[p.nseq];
+    x = uint64_t{blockIdx.x} * W / gridDim.x;
+    x_end = (uint64_t{blockIdx.x} + 1) * W / gridDim.x;
+  }
+  for (bool first = true;; first = false) {
+  uint32_t seq, h, b0, b1, slot;
+  bool direct = false;
+  if (!p.balanced) {
+    if (!first) break;
+    const uint32_t unit = blockIdx.x / p.splits, split = blockIdx.x % p.splits;
+    seq = unit / H;
+    h = unit % H;
+    const uint32_t n = p.segs[seq].y;
+    b0 = static_cast<uint32_t>(uint64_t{n} * split / p.splits);
+    b1 = static_cast<uint32_t>(uint64_t{n} * (split + 1) / p.splits);
+    slot = blockIdx.x;
+    direct = p.splits == 1;
+  } else {
+    if (x >= x_end) break;
+    uint32_t lo = 0, hi = p.nseq;  // the sequence s with prefix[s] <= x < prefix[s + 1]
+    while (hi - lo > 1) {
+      const uint32_t mid = (lo + hi) >> 1;
+      if (p.prefix[mid] <= x) lo = mid; else hi = mid;
+    }
+    seq = lo;
+    const uint32_t n = p.segs[seq].y;  // > 0: x lies inside the sequence's range
+    const uint64_t local = x - p.prefix[seq];
+    h = static_cast<uint32_t>(local / n);
+    b0 = static_cast<uint32_t>(local - uint64_t{h} * n);
+    b1 = static_cast<uint32_t>(min(uint64_t{n}, b0 + (x_end - x)));
+    x += b1 - b0;
+    slot = blockIdx.x + seq * H + h;
+  }
 
   // B fragments of Q^T (k = head_dim, n = query head of the group; columns >= kG are 0).
   uint32_t qb[kSteps][2];
@@ -269,9 +317,6 @@ __global__ void __launch_bounds__(kAttnThreads, 4) decode_attention_kernel(const
   float m[2] = {-INFINITY, -INFINITY}, l[2] = {0.0f, 0.0f};
 
   const uint2 seg = p.segs[seq];
-  const uint32_t T = p.T, H = p.H;
-  const uint32_t b0 = static_cast<uint32_t>(uint64_t{seg.y} * split / p.splits);
-  const uint32_t b1 = static_cast<uint32_t>(uint64_t{seg.y} * (split + 1) / p.splits);
   // Blocks are resolved (arena -> descriptor -> checks) a batch at a time, one block per
   // thread, so the dependent lookups of a batch overlap instead of preceding each block's
   // payload reads.  Warp w then takes blocks w, w + 4, ... of the batch.
@@ -392,17 +437,19 @@ __global__ void __launch_bounds__(kAttnThreads, 4) decode_attention_kernel(const
         O = fmaf(s_o[(wi * 8 + g) * kD + e], a, O);
       }
     }
-    if (p.splits == 1) {
+    if (direct) {
       const float r = L > 0.0f ? O / L : 0.0f;
       p.out[(uint64_t{seq} * p.q_heads + h * kG + g) * kD + e] = __half_as_ushort(__float2half_rn(r));
     } else {
-      float* w = p.ws + uint64_t{blockIdx.x} * kPart<kD>;
-      w[16 + g * kD + e] = O;
+      float* wp = p.ws + uint64_t{slot} * kPart<kD>;
+      wp[16 + g * kD + e] = O;
       if (e == 0) {
-        w[g] = M;
-        w[8 + g] = L;
+        wp[g] = M;
+        wp[8 + g] = L;
       }
     }
+  }
+  __syncthreads();  // the merge buffers are read before the next piece stages tiles
   }
 }
 
@@ -429,6 +476,69 @@ __global__ void __launch_bounds__(kD) decode_attention_merge(const float* __rest
   out[(uint64_t{seq} * q_heads + qh) * kD + e] = __half_as_ushort(__float2half_rn(r));
 }
 
+// prefix[0] = 0, prefix[i + 1] = prefix[i] + H * segs[i].y: one CTA, a chunked block scan.
+__global__ void __launch_bounds__(kAttnThreads) attention_prefix(const uint2* __restrict__ segs, uint32_t nseq,
+                                                                 uint32_t H, uint64_t* __restrict__ prefix) {
+  __shared__ uint64_t s_tot[kAttnWarps];
+  const uint32_t lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+  if (threadIdx.x == 0) prefix[0] = 0;
+  uint64_t carry = 0;
+  for (uint32_t base = 0; base < nseq; base += kAttnThreads) {
+    const uint32_t i = base + threadIdx.x;
+    uint64_t v = i < nseq ? uint64_t{segs[i].y} * H : 0;
+#pragma unroll
+    for (int o = 1; o < 32; o <<= 1) {
+      const uint64_t n = __shfl_up_sync(0xFFFFFFFFu, v, o);
+      if (lane >= static_cast<uint32_t>(o)) v += n;
+    }
+    if (lane == 31) s_tot[warp] = v;
+    __syncthreads();
+    uint64_t before = 0, total = 0;
+#pragma unroll
+    for (int wi = 0; wi < kAttnWarps; ++wi) {
+      before += wi < static_cast<int>(warp) ? s_tot[wi] : 0;
+      total += s_tot[wi];
+    }
+    if (i < nseq) prefix[i + 1] = carry + before + v;
+    carry += total;
+    __syncthreads();  // s_tot is rewritten by the next chunk
+  }
+}
+
+// Merges a balanced launch's partials of one (sequence, query head) per CTA, kD threads:
+// the slots c + u of the CTAs c whose ranges meet unit u.
+template <int kD>
+__global__ void __launch_bounds__(kD)
+    decode_attention_merge_balanced(const float* __restrict__ ws, const uint64_t* __restrict__ prefix,
+                                    const uint2* __restrict__ segs, uint32_t nseq, uint32_t H, uint32_t group,
+                                    uint32_t q_heads, uint32_t ctas, uint16_t* __restrict__ out) {
+  const uint32_t seq = blockIdx.x / q_heads, qh = blockIdx.x % q_heads;
+  const uint32_t h = qh / group, g = qh % group, e = threadIdx.x;
+  const uint32_t n = segs[seq].y;
+  float M = -INFINITY, L = 0.0f, O = 0.0f;
+  if (n > 0) {
+    const uint64_t W = prefix[nseq], u = uint64_t{seq} * H + h;
+    const uint64_t start = prefix[seq] + uint64_t{h} * n;
+    const uint32_t c0 = balanced_cta(start, W, ctas), c1 = balanced_cta(start + n - 1, W, ctas);
+    // With more CTAs than blocks some ranges are empty: those CTAs wrote no slot.
+    auto empty = [&](uint32_t c) { return uint64_t{c} * W / ctas == (uint64_t{c} + 1) * W / ctas; };
+    for (uint32_t c = c0; c <= c1; ++c) {
+      if (!empty(c)) M = fmaxf(M, ws[(c + u) * kPart<kD> + g]);
+    }
+    if (M != -INFINITY) {
+      for (uint32_t c = c0; c <= c1; ++c) {
+        if (empty(c)) continue;
+        const float* ps = ws + (c + u) * kPart<kD>;
+        const float a = ps[g] == -INFINITY ? 0.0f : exp2f(ps[g] - M);
+        L = fmaf(ps[8 + g], a, L);
+        O = fmaf(ps[16 + g * kD + e], a, O);
+      }
+    }
+  }
+  const float r = L > 0.0f ? O / L : 0.0f;
+  out[(uint64_t{seq} * q_heads + qh) * kD + e] = __half_as_ushort(__float2half_rn(r));
+}
+
 template <int kD>
 cudaError_t launch_for_group(uint32_t group, const AttnParams& p, unsigned grid, cudaStream_t s) {
   switch (group) {
@@ -446,7 +556,7 @@ int launch_attention(const HlkvPools* pools, const HlkvLayout* layout, const Hlk
                      uint32_t table_size, const uint32_t* d_arena, uint32_t arena_size,
                      const HlkvSegment* d_segs, uint32_t nseq, const uint16_t* d_q, uint32_t q_heads,
                      float softmax_scale, uint32_t splits, void* d_ws, size_t ws_bytes, uint16_t* d_out,
-                     uint32_t* d_err, hlkv_stream_t stream) {
+                     uint32_t* d_err, hlkv_stream_t stream, bool balanced) {
   if (pools == nullptr || !layout_ok(layout) || d_err == nullptr) return HLKV_INVALID_ARGUMENT;
   if (layout->head_dim != 64 && layout->head_dim != 128) return HLKV_INVALID_ARGUMENT;
   const uint32_t H = layout->kv_heads;
@@ -460,14 +570,18 @@ int launch_attention(const HlkvPools* pools, const HlkvLayout* layout, const Hlk
       (table_size > 0 && d_table == nullptr) || (arena_size > 0 && d_arena == nullptr)) {
     return HLKV_INVALID_ARGUMENT;
   }
-  if (uint64_t{nseq} * H * splits > 0x7FFFFFFFull || uint64_t{nseq} * q_heads > 0x7FFFFFFFull) {
+  // Balanced mode: `splits` is the CTA count (at most 2^20, so slot and range arithmetic
+  // stays in 64 bits).
+  if (balanced ? splits > (1u << 20) || uint64_t{nseq} * H > 0x7FFFFFFFull
+               : uint64_t{nseq} * H * splits > 0x7FFFFFFFull) {
     return HLKV_INVALID_ARGUMENT;
   }
-  if (splits > 1) {
+  if (uint64_t{nseq} * q_heads > 0x7FFFFFFFull) return HLKV_INVALID_ARGUMENT;
+  if (balanced || splits > 1) {
     if (d_ws == nullptr || (reinterpret_cast<uintptr_t>(d_ws) & 15u) != 0) return HLKV_INVALID_ARGUMENT;
-    if (ws_bytes < hlkv_decode_attention_workspace_bytes(nseq, H, layout->head_dim, splits)) {
-      return HLKV_BUFFER_TOO_SMALL;
-    }
+    const size_t need = balanced ? hlkv_decode_attention_balanced_workspace_bytes(nseq, H, layout->head_dim, splits)
+                                 : hlkv_decode_attention_workspace_bytes(nseq, H, layout->head_dim, splits);
+    if (ws_bytes < need) return HLKV_BUFFER_TOO_SMALL;
   }
   AttnParams p{};
   const uint64_t elems = uint64_t{2} * layout->block_tokens * H * layout->head_dim;
@@ -495,9 +609,34 @@ int launch_attention(const HlkvPools* pools, const HlkvLayout* layout, const Hlk
   p.layout_id = layout->layout_id;
   p.q_heads = q_heads;
   p.qscale = softmax_scale * kLog2e;
+  const cudaStream_t s = reinterpret_cast<cudaStream_t>(stream);
+  if (balanced) {
+    // workspace: prefix[nseq + 1] (16-byte aligned), then the partial slots
+    const size_t prefix_bytes = (size_t{nseq} + 1) * sizeof(uint64_t);
+    uint64_t* prefix = static_cast<uint64_t*>(d_ws);
+    p.splits = 1;
+    p.balanced = 1;
+    p.prefix = prefix;
+    p.ws = reinterpret_cast<float*>(static_cast<unsigned char*>(d_ws) + (prefix_bytes + 15) / 16 * 16);
+    attention_prefix<<<1, kAttnThreads, 0, s>>>(p.segs, nseq, H, prefix);
+    cudaError_t e = cudaGetLastError();
+    if (e == cudaSuccess) {
+      e = layout->head_dim == 64 ? launch_for_group<64>(group, p, splits, s) : launch_for_group<128>(group, p, splits, s);
+    }
+    if (e == cudaSuccess) {
+      if (layout->head_dim == 64) {
+        decode_attention_merge_balanced<64><<<nseq * q_heads, 64, 0, s>>>(p.ws, prefix, p.segs, nseq, H, group,
+                                                                           q_heads, splits, d_out);
+      } else {
+        decode_attention_merge_balanced<128><<<nseq * q_heads, 128, 0, s>>>(p.ws, prefix, p.segs, nseq, H, group,
+                                                                             q_heads, splits, d_out);
+      }
+      e = cudaGetLastError();
+    }
+    return cuda_status(e);
+  }
   p.splits = splits;
   p.ws = splits > 1 ? static_cast<float*>(d_ws) : nullptr;
-  const cudaStream_t s = reinterpret_cast<cudaStream_t>(stream);
   const unsigned grid = nseq * H * splits;
   cudaError_t e = layout->head_dim == 64 ? launch_for_group<64>(group, p, grid, s)
                                          : launch_for_group<128>(group, p, grid, s);
@@ -528,7 +667,27 @@ extern "C" int hlkv_decode_attention(const HlkvPools* pools, const HlkvLayout* l
                                      uint32_t q_heads, float softmax_scale, uint16_t* d_out,
                                      uint32_t* d_err, hlkv_stream_t stream) {
   return hlkv::launch_attention(pools, layout, d_table, table_size, d_arena, arena_size, d_segs, nseq, d_q,
-                                q_heads, softmax_scale, 1, nullptr, 0, d_out, d_err, stream);
+                                q_heads, softmax_scale, 1, nullptr, 0, d_out, d_err, stream, false);
+}
+
+extern "C" size_t hlkv_decode_attention_balanced_workspace_bytes(uint32_t nseq, uint32_t kv_heads,
+                                                                 uint32_t head_dim, uint32_t ctas) {
+  if (head_dim != 64 && head_dim != 128) return 0;
+  const uint64_t part = head_dim == 64 ? hlkv::kPart<64> : hlkv::kPart<128>;
+  const uint64_t prefix = ((uint64_t{nseq} + 1) * sizeof(uint64_t) + 15) / 16 * 16;
+  return static_cast<size_t>(prefix + (uint64_t{ctas} + uint64_t{nseq} * kv_heads) * part * sizeof(float));
+}
+
+extern "C" int hlkv_decode_attention_balanced(const HlkvPools* pools, const HlkvLayout* layout,
+                                              const HlkvExecDescriptor* d_table, uint32_t table_size,
+                                              const uint32_t* d_arena, uint32_t arena_size,
+                                              const HlkvSegment* d_segs, uint32_t nseq, const uint16_t* d_q,
+                                              uint32_t q_heads, float softmax_scale, uint32_t ctas,
+                                              void* d_workspace, size_t workspace_bytes, uint16_t* d_out,
+                                              uint32_t* d_err, hlkv_stream_t stream) {
+  return hlkv::launch_attention(pools, layout, d_table, table_size, d_arena, arena_size, d_segs, nseq, d_q,
+                                q_heads, softmax_scale, ctas, d_workspace, workspace_bytes, d_out, d_err,
+                                stream, true);
 }
 
 extern "C" int hlkv_decode_attention_split(const HlkvPools* pools, const HlkvLayout* layout,
@@ -540,7 +699,7 @@ extern "C" int hlkv_decode_attention_split(const HlkvPools* pools, const HlkvLay
                                            uint32_t* d_err, hlkv_stream_t stream) {
   return hlkv::launch_attention(pools, layout, d_table, table_size, d_arena, arena_size, d_segs, nseq, d_q,
                                 q_heads, softmax_scale, splits, d_workspace, workspace_bytes, d_out, d_err,
-                                stream);
+                                stream, false);
 }
 
 // ---- split attention without a caller workspace -------------------------------------------
@@ -612,5 +771,5 @@ extern "C" int hlkv_decode_attention_split_noalloc(const HlkvPools* pools, const
   if (st != HLKV_OK) return st;
   return hlkv::launch_attention(pools, layout, d_table, table_size, d_arena, arena_size, d_segs, nseq, d_q,
                                 q_heads, softmax_scale, splits, scratch, HLKV_NOALLOC_SCRATCH_BYTES, d_out,
-                                d_err, stream);
+                                d_err, stream, false);
 }

@@ -136,6 +136,9 @@ SIGNATURES: list[tuple[str, object, list]] = [
     ("hlkv_decode_attention_workspace_bytes", _sz, [_u32, _u32, _u32, _u32]),
     ("hlkv_decode_attention_split", _int, [_P(Pools), _P(Layout), _vp, _u32, _vp, _u32, _vp, _u32, _vp,
                                            _u32, C.c_float, _u32, _vp, _sz, _vp, _vp, _vp]),
+    ("hlkv_decode_attention_balanced_workspace_bytes", _sz, [_u32, _u32, _u32, _u32]),
+    ("hlkv_decode_attention_balanced", _int, [_P(Pools), _P(Layout), _vp, _u32, _vp, _u32, _vp, _u32, _vp,
+                                              _u32, C.c_float, _u32, _vp, _sz, _vp, _vp, _vp]),
     ("hlkv_decode_attention_split_noalloc", _int, [_P(Pools), _P(Layout), _vp, _u32, _vp, _u32, _vp,
                                                    _u32, _vp, _u32, C.c_float, _u32, _vp, _vp, _vp]),
     ("hlkv_transcode", _int, [_P(Pools), _P(Layout), _vp, _u32, _vp, _vp]),
@@ -576,6 +579,25 @@ def decode_attention_split(pools: Pools, layout: Layout, table_ptr: int, table_s
                                            softmax_scale, splits, _ptr(workspace), ws_bytes, _ptr(out),
                                            _ptr(err), _stream_handle(stream))
     check(st, "hlkv_decode_attention_split")
+    return st
+
+
+def decode_attention_balanced_workspace_bytes(nseq: int, kv_heads: int, head_dim: int, ctas: int) -> int:
+    return lib().hlkv_decode_attention_balanced_workspace_bytes(nseq, kv_heads, head_dim, ctas)
+
+
+def decode_attention_balanced(pools: Pools, layout: Layout, table_ptr: int, table_size: int, arena_ptr: int,
+                              arena_size: int, segs, q, q_heads: int, softmax_scale: float, ctas: int,
+                              workspace, out, err, stream=None) -> int:
+    """Decode attention with the blocks of all (sequence, KV head) units balanced over
+    `ctas` CTAs; workspace: a device tensor of decode_attention_balanced_workspace_bytes."""
+    nseq = int(segs.shape[0])
+    ws_bytes = 0 if workspace is None else workspace.numel() * workspace.element_size()
+    st = lib().hlkv_decode_attention_balanced(C.byref(pools), C.byref(layout), table_ptr or None, table_size,
+                                              arena_ptr or None, arena_size, _ptr(segs), nseq, _ptr(q),
+                                              q_heads, softmax_scale, ctas, _ptr(workspace), ws_bytes,
+                                              _ptr(out), _ptr(err), _stream_handle(stream))
+    check(st, "hlkv_decode_attention_balanced")
     return st
 
 

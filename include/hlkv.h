@@ -235,6 +235,25 @@ int hlkv_decode_attention_split(const HlkvPools* pools, const HlkvLayout* layout
                                 uint16_t* d_out, uint32_t* d_err, hlkv_stream_t stream);
 
 /*
+ * The same attention with the work balanced over exactly `ctas` CTAs (1 .. 2^20): the
+ * (sequence, KV head) units' blocks, laid end to end, are cut into `ctas` equal ranges, so
+ * sequences of any mix of lengths keep every SM equally busy.  A range can end inside a unit
+ * and span several units; each part writes partial (max, sum, outputs) to the workspace
+ * (16-byte aligned, at least hlkv_decode_attention_balanced_workspace_bytes(nseq, kv_heads,
+ * head_dim, ctas) bytes), and a last launch merges them.  A first one-CTA launch writes the
+ * units' prefix sums there.  No counterpart in the reference.  Calls that overlap on the GPU
+ * must not share a workspace.
+ */
+size_t hlkv_decode_attention_balanced_workspace_bytes(uint32_t nseq, uint32_t kv_heads, uint32_t head_dim,
+                                                      uint32_t ctas);
+int hlkv_decode_attention_balanced(const HlkvPools* pools, const HlkvLayout* layout,
+                                   const HlkvExecDescriptor* d_table, uint32_t table_size,
+                                   const uint32_t* d_arena, uint32_t arena_size, const HlkvSegment* d_segs,
+                                   uint32_t nseq, const uint16_t* d_q, uint32_t q_heads, float softmax_scale,
+                                   uint32_t ctas, void* d_workspace, size_t workspace_bytes,
+                                   uint16_t* d_out, uint32_t* d_err, hlkv_stream_t stream);
+
+/*
  * hlkv_decode_attention_split with its partials in a fixed scratch array of this library
  * (HLKV_NOALLOC_SCRATCH_BYTES per device, part of its device image) instead of a caller
  * workspace: for callers that cannot allocate device memory when they call (a host binding

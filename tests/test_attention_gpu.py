@@ -165,3 +165,57 @@ def test_attention_block_wide_scales(hlkv_lib, oracle, cuda_device, T, H, D, gro
     want, oerr = oracle_attention(oracle, wl, q.astype(np.float64), scale)
     assert err == oerr == 0
     _close(got, want, vscale=40.0)
+
+
+@pytest.mark.parametrize("ctas", [1, 7, 64, 592, 5000])
+def test_balanced_attention_matches_oracle(hlkv_lib, oracle, cuda_device, ctas):
+    """The units' blocks cut into `ctas` equal ranges (ranges end inside units and span
+    several; 5000 CTAs exceed the block count, leaving empty ranges), over sequences of very
+    different lengths, empty ones included: the same oracle, and two calls in a row on one
+    workspace agree bit for bit."""
+    import torch
+    from hlkv.workload import build_workload, mixed_formats
+    T, H, D, group = 16, 4, 128, 2
+    lens = [3, 0, 61, 1, 17, 0, 9]
+    fm = mixed_formats(len(lens), lens, probs=(0.25, 0.35, 0.15, 0.25), seed=ctas)
+    rng = np.random.default_rng(ctas)
+    vt = [[T] * (len(r) - 1) + [int(rng.integers(1, T + 1))] if r else [] for r in fm]
+    wl = build_workload(fm, T=T, H=H, D=D, seed=ctas + 3, valid_tokens=vt)
+    qh = H * group
+    q = rng.standard_normal((len(lens), qh, D)).astype(np.float16)
+    ws = torch.empty(hlkv_lib.decode_attention_balanced_workspace_bytes(len(lens), H, D, ctas),
+                     dtype=torch.uint8, device="cuda")
+    outs = []
+    for call in range(2):
+        out = torch.full((len(lens), qh, D), 0x7777, dtype=torch.int32, device="cuda").to(torch.int16)
+        err = torch.zeros(1, dtype=torch.int32, device="cuda")
+        hlkv_lib.decode_attention_balanced(wl.hlkv_pools(), wl.layout, wl.dt.table_ptr, wl.dt.table_size,
+                                           wl.dt.arena_ptr, wl.dt.arena_size, wl.segs,
+                                           torch.from_numpy(q.view(np.int16)).cuda(), qh, 0.1, ctas, ws,
+                                           out, err)
+        torch.cuda.synchronize()
+        assert int(err.item()) == 0
+        outs.append(out.cpu().numpy().view(np.float16).astype(np.float64))
+    assert np.array_equal(outs[0], outs[1])
+    want, oerr = oracle_attention(oracle, wl, q.astype(np.float64), 0.1)
+    assert oerr == 0
+    _close(outs[0], want, vscale=20.0)
+    assert (outs[0][[1, 5]] == 0).all()  # empty sequences give zeros
+
+
+def test_balanced_attention_workspace_checks(hlkv_lib, cuda_device):
+    import ctypes as C
+    import hlkv
+    lay = hlkv.Layout(16, 8, 128, 1)
+    pools = hlkv.Pools()
+    L = hlkv.lib()
+    need = hlkv_lib.decode_attention_balanced_workspace_bytes(2, 8, 128, 100)
+    assert need == 32 + (100 + 2 * 8) * (16 + 8 * 128) * 4
+    args = lambda ctas, ws, nbytes: (C.byref(pools), C.byref(lay), None, 0, None, 0, C.c_void_p(16), 2,
+                                     C.c_void_p(16), 32, 0.1, ctas, ws, nbytes, C.c_void_p(16),
+                                     C.c_void_p(16), None)
+    assert L.hlkv_decode_attention_balanced(*args(100, C.c_void_p(256), need - 1)) == hlkv.BUFFER_TOO_SMALL
+    assert L.hlkv_decode_attention_balanced(*args(100, None, need)) == hlkv.INVALID_ARGUMENT
+    assert L.hlkv_decode_attention_balanced(*args(100, C.c_void_p(264), need)) == hlkv.INVALID_ARGUMENT
+    assert L.hlkv_decode_attention_balanced(*args(0, C.c_void_p(256), need)) == hlkv.INVALID_ARGUMENT
+    assert L.hlkv_decode_attention_balanced(*args((1 << 20) + 1, C.c_void_p(256), 1 << 40)) == hlkv.INVALID_ARGUMENT
