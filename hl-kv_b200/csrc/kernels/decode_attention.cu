@@ -12,11 +12,16 @@
 // in binary32 arithmetic (exp2 with the scale folded in), the result rounded to binary16.
 // A sequence without valid tokens gives zeros.
 //
-// Structure: one CTA per (sequence, KV head), 8 warps taking the sequence's blocks
-// round-robin.  Per block and warp: 2 lanes per token compute the G scores of 16 tokens
-// at a time (each lane half of head_dim, queries from shared memory), an online-softmax
-// update, then the lanes split head_dim to accumulate p * v for the G queries.  The 8
-// warps' partial (max, sum, out) are merged in shared memory at the end.
+// Structure: a CTA of 4 warps works on one (sequence, KV head) unit, or on one share of
+// it (split mode: `splits` CTAs per unit), or on an equal range of all units' blocks laid
+// end to end (balanced mode), piece by piece.  Per piece, the CTA resolves up to 128 blocks
+// at a time (one thread per block: arena -> descriptor -> checks), and the warps take the
+// blocks round-robin, prefetching their next block into L2.  Per 16-token tile a warp
+// decodes the K and V rows of its head into shared memory (one out-of-line staging routine
+// per format), computes S^T = K . Q^T with mma.sync m16n8k16 (FP16 in, FP32 accumulate),
+// runs an online softmax in exp2, and adds V^T . P into its O^T accumulators.  The warps'
+// (max, sum, outputs) merge in shared memory; the result goes to the output, or to a
+// partial slot that a merge launch combines.
 #include <cuda_fp16.h>
 #include <cuda_runtime.h>
 
