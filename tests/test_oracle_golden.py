@@ -378,7 +378,21 @@ def _ref_transcode(ref, pools, T, H, D, jobs):
     binary32 values into the destination row (rows of later tokens from zeros)."""
     rows = 2 * T * H
     packed = lambda f, n: 2 * n if f == 0 else (n // 2 if f == 3 else n)
-    for ff, fs, tf, ts, vt in jobs[:, :5]:
+    for ff, fs, tf, ts, vt, fmode, fref in jobs[:, :7]:
+        # block-wide source parameters (scale modes 1 and 2), as the reference's decoder
+        # would be given them; a job whose parameters it rejects (or mode 3) moves nothing
+        wide = None
+        if ff != 0 and fmode != 0:
+            if fmode > 2:
+                continue
+            if fmode == 1:
+                wide = np.array([[np.uint32(fref).view(np.float32), 0]], np.float32)
+            else:
+                halves = np.array([fref & 0xFFFF, fref >> 16], np.uint16).view(np.float16).astype(np.float32)
+                wide = halves.reshape(1, 2)
+            probe = np.zeros(packed(int(ff), D), np.uint8)
+            if ref.dequantize_to_fp16(int(ff), probe, D, wide, D)[0] != 0:
+                continue
         src_buf, sb_s, _ = pools[int(ff)]
         dst_buf, sb_d, _ = pools[int(tf)]
         src = src_buf[int(fs) * sb_s:(int(fs) + 1) * sb_s]
@@ -389,6 +403,8 @@ def _ref_transcode(ref, pools, T, H, D, jobs):
                 codes = src[packed(int(ff), r * D):packed(int(ff), (r + 1) * D)]
                 if ff == 0:
                     p = np.zeros((0, 2), np.float32)
+                elif wide is not None:
+                    p = wide
                 elif ff == 3:
                     p = src[sc + 8 * r:sc + 8 * r + 8].view(np.float32).reshape(1, 2)
                 else:
@@ -450,3 +466,44 @@ def test_transcode_oracle_matches_reference_calls(oracle, ref):
     assert err == (1 << 9)
     for f in range(4):
         assert np.array_equal(a[f][0], b[f][0]), f
+
+
+def test_transcode_block_wide_sources_match_reference_calls(oracle, ref):
+    """Sources with block-wide parameters (the job's from_scale_mode / from_scale_ref): the
+    oracle equals the reference's own calls given those parameters; jobs whose parameters
+    the reference's decoder rejects (non-finite, FP8 bias) or with mode 3 move nothing and
+    report HLKV_ERR_SCALE_MODE."""
+    rng = np.random.default_rng(37)
+    T, H, D, n_slots = 4, 2, 64, 8
+    pools = {}
+    for f in (0, 1, 2, 3):
+        sb = (oracle.slot_bytes_needed(f, T, H, D) + 15) // 16 * 16
+        pools[f] = (rng.integers(0, 256, size=n_slots * sb, dtype=np.uint8), sb, n_slots)
+    f16 = lambda v: int(np.array([v], np.float16).view(np.uint16)[0])
+    f32 = lambda v: int(np.array([v], np.float32).view(np.uint32)[0])
+    jobs = np.array([
+        [1, 0, 3, 0, T, 1, f32(0.25), 0],                    # E4M3, binary32 scale
+        [2, 1, 1, 1, 3, 2, f16(0.5), 0],                     # E5M2, binary16 pair, bias 0
+        [3, 2, 1, 2, T, 2, f16(0.125) | f16(-1.5) << 16, 0],  # INT4, scale and bias
+        [3, 3, 2, 3, 2, 1, f32(0.01), 0],                    # INT4, binary32 scale, bias 0
+        [1, 4, 3, 4, T, 2, f16(1.0) | f16(2.0) << 16, 0],    # FP8 with a bias: rejected
+        [3, 5, 1, 5, T, 1, f32(np.inf), 0],                  # non-finite scale: rejected
+        [1, 6, 3, 6, T, 3, 9, 0],                            # mode 3: rejected
+        [1, 7, 3, 7, T, 0, 0, 0],                            # per-row parameters
+    ], np.uint32)
+    # per-row parameters of the last source: a finite scale per row
+    sb1 = pools[1][1]
+    code1 = oracle.slot_bytes_needed(1, T, H, D) - 4 * 2 * T * H
+    pools[1][0][7 * sb1 + code1:7 * sb1 + code1 + 4 * 2 * T * H] = \
+        np.full(2 * T * H, 0.02, np.float32).view(np.uint8)
+    a = {f: (b.copy(), sb, ns) for f, (b, sb, ns) in pools.items()}
+    b = {f: (b.copy(), sb, ns) for f, (b, sb, ns) in pools.items()}
+    err = oracle.transcode(a, T, H, D, jobs)
+    _ref_transcode(ref, b, T, H, D, jobs)
+    assert err & (1 << 7)
+    for f in range(4):
+        assert np.array_equal(a[f][0], b[f][0]), f
+    for k in (4, 5, 6):  # the rejected jobs' destination slots are untouched
+        tf, ts = int(jobs[k, 2]), int(jobs[k, 3])
+        sb = pools[tf][1]
+        assert np.array_equal(a[tf][0][ts * sb:(ts + 1) * sb], pools[tf][0][ts * sb:(ts + 1) * sb]), k
