@@ -467,9 +467,12 @@ __global__ void __launch_bounds__(kD) decode_attention_merge(const float* __rest
   const uint32_t h = qh / group, g = qh % group, e = threadIdx.x;
   const float* w = ws + uint64_t{seq * H + h} * splits * kPart<kD>;
   float M = -INFINITY;
+  // Unrolled, so that each thread keeps several partials' loads in flight.
+#pragma unroll 8
   for (uint32_t s = 0; s < splits; ++s) M = fmaxf(M, w[uint64_t{s} * kPart<kD> + g]);
   float L = 0.0f, O = 0.0f;
   if (M != -INFINITY) {
+#pragma unroll 8
     for (uint32_t s = 0; s < splits; ++s) {
       const float* ps = w + uint64_t{s} * kPart<kD>;
       const float a = ps[g] == -INFINITY ? 0.0f : exp2f(ps[g] - M);
@@ -525,12 +528,17 @@ __global__ void __launch_bounds__(kD)
     const uint64_t W = prefix[nseq], u = uint64_t{seq} * H + h;
     const uint64_t start = prefix[seq] + uint64_t{h} * n;
     const uint32_t c0 = balanced_cta(start, W, ctas), c1 = balanced_cta(start + n - 1, W, ctas);
-    // With more CTAs than blocks some ranges are empty: those CTAs wrote no slot.
-    auto empty = [&](uint32_t c) { return uint64_t{c} * W / ctas == (uint64_t{c} + 1) * W / ctas; };
+    // With more CTAs than blocks some ranges are empty: those CTAs wrote no slot.  With
+    // ctas <= W every range holds at least one block, and the test is skipped.
+    const bool sparse = ctas > W;
+    auto empty = [&](uint32_t c) { return sparse && uint64_t{c} * W / ctas == (uint64_t{c} + 1) * W / ctas; };
+    // Unrolled, so that each thread keeps several partials' loads in flight.
+#pragma unroll 8
     for (uint32_t c = c0; c <= c1; ++c) {
       if (!empty(c)) M = fmaxf(M, ws[(c + u) * kPart<kD> + g]);
     }
     if (M != -INFINITY) {
+#pragma unroll 8
       for (uint32_t c = c0; c <= c1; ++c) {
         if (empty(c)) continue;
         const float* ps = ws + (c + u) * kPart<kD>;
