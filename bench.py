@@ -102,6 +102,11 @@ WORKLOADS = {
     "flat_e4m3": dict(n=8_388_608, group=128, fmt=1, scaling="weak", flat=True,
                       name="contiguous E4M3 -> FP16: 8,388,608 values (1 seq x 4096 tok x K+V x 8 "
                            "heads x 128), scale per 128 values; drop-in vs the reference's kernel"),
+    # The same conversion at 2^28 values (805 MB moved, over 6x L2): the drop-in against the
+    # reference's own kernel where bandwidth rather than launch latency sets the time.
+    "flat_e4m3_large": dict(n=268_435_456, group=128, fmt=1, scaling="weak", flat=True,
+                            name="contiguous E4M3 -> FP16: 268,435,456 values, scale per 128 values; "
+                                 "drop-in vs the reference's kernel at a bandwidth-bound size"),
     # Decode step: every (sequence, layer) stream appends one token, encoded into its tail
     # block (kernel 2), and the allocator's descriptor delta is applied on the device
     # (kernel 3).  Sequences sharded over the ranks.

@@ -45,7 +45,7 @@ __device__ __forceinline__ bool params_ok(uint32_t f, float2 sb) {
 // kVecUnroll chunks per thread per pass: every load of a pass is issued before the
 // first conversion, so each thread keeps kVecUnroll code loads (and their scale loads)
 // in flight; a short array then occupies the whole GPU in a single pass.
-constexpr uint32_t kVecUnroll = 4;
+constexpr uint32_t kVecUnroll = 8;  // at 2^28 values: 0.889 of the copy peak, 4 chunks: 0.849
 
 template <uint32_t kF, typename Index, bool kCheck>
 __global__ void __launch_bounds__(kThreads)
