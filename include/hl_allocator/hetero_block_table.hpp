@@ -17,7 +17,7 @@
 // the GPU by hlkv_apply_delta), batch_segments() gives the per-step
 // {offset, length} per sequence, and a kernel reads block j of sequence i as
 // descriptor_table[arena[segment_i.offset + j]].  build_exec_table() is the
-// O(total blocks) materialized path, kept as a checker.
+// O(total blocks) materialized path, kept for cross-checking the incremental one.
 //
 // Not thread-safe: one owner thread mutates; const calls may run concurrently
 // only while nothing mutates.  release() and commit_format_change() free slots

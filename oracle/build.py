@@ -1,4 +1,4 @@
-"""Build recipe for the checker libraries (TEST INFRASTRUCTURE ONLY).
+"""Build recipe for the oracle libraries (TEST INFRASTRUCTURE ONLY).
 
     python oracle/build.py            # both, when the reference tree is present
 

@@ -2,7 +2,7 @@
  * hlkv_oracle.c -- TEST INFRASTRUCTURE ONLY.
  *
  * CPU restatement of the reference HL-KV algorithms for the quantized KV-block
- * path.  It is the checker that the CUDA kernels are compared against, and the
+ * path.  It is the oracle that the CUDA kernels are compared against, and the
  * "port" CPU baseline of bench.py.  Nothing in the product library links,
  * loads or calls this file; only tests/, __graft_entry__.smoke() and the
  * cpu_baseline leg of bench.py do.

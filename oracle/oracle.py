@@ -1,4 +1,4 @@
-"""ctypes bindings to the checker libraries (TEST INFRASTRUCTURE ONLY).
+"""ctypes bindings to the oracle libraries (TEST INFRASTRUCTURE ONLY).
 
 ``Oracle`` binds ``oracle/_build/liboracle.so`` (the C restatement in
 hlkv_oracle.c); ``Ref`` binds ``oracle/_ref/libhlkv_ref.so`` (the reference's

@@ -77,7 +77,7 @@ def test_kernel_entry_points_reject_bad_arguments(hlkv_lib):
 
 
 def test_product_does_not_load_the_oracle(hlkv_lib):
-    """The product library links no checker code."""
+    """The product library links no oracle code."""
     import subprocess
     out = subprocess.run(["nm", "-D", "--defined-only", hlkv_lib.LIB_PATH], capture_output=True,
                          text=True).stdout
