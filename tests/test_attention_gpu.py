@@ -32,7 +32,8 @@ def _run(hlkv, wl, q_heads, scale, seed, segs=None):
     return q, out.cpu().numpy().view(np.float16).astype(np.float64), int(err.item())
 
 
-@pytest.mark.parametrize("T,H,D,group", [(16, 8, 128, 4), (16, 2, 64, 1), (4, 2, 128, 8), (32, 1, 64, 2)])
+@pytest.mark.parametrize("T,H,D,group", [(16, 8, 128, 4), (16, 2, 64, 1), (4, 2, 128, 8), (32, 1, 64, 2),
+                                         (128, 2, 128, 4), (512, 1, 64, 2)])
 def test_attention_matches_oracle(hlkv_lib, oracle, cuda_device, T, H, D, group):
     from hlkv.workload import build_workload, mixed_formats
     fm = mixed_formats(5, [3, 17, 1, 40, 9], probs=(0.25, 0.35, 0.15, 0.25), seed=T + D)

@@ -51,7 +51,7 @@ def _all_ids(wl):
     return ids
 
 
-@pytest.mark.parametrize("T,H,D", [(16, 8, 128), (4, 2, 64), (2, 2, 256), (5, 3, 64)])
+@pytest.mark.parametrize("T,H,D", [(16, 8, 128), (4, 2, 64), (2, 2, 256), (5, 3, 64), (512, 2, 128)])
 def test_append_encode_bit_exact(hlkv_lib, oracle, cuda_device, T, H, D):
     from hlkv.workload import build_workload
     fm = [[0, 1, 2, 3, 1, 3, 0], [3, 1, 2]]

@@ -54,7 +54,8 @@ def test_device_tables_match_host(hlkv_lib, small_mixed):
         assert np.array_equal(arena[off:off + ln], host_arena(wl)[off:off + ln])
 
 
-@pytest.mark.parametrize("T,H,D", [(4, 2, 64), (16, 8, 128), (2, 3, 256), (1, 1, 64), (32, 1, 128)])
+@pytest.mark.parametrize("T,H,D", [(4, 2, 64), (16, 8, 128), (2, 3, 256), (1, 1, 64), (32, 1, 128),
+                                   (128, 4, 128), (512, 1, 64)])  # 512: the largest block_tokens
 def test_geometries(hlkv_lib, oracle, cuda_device, T, H, D):
     from hlkv.workload import build_workload, mixed_formats
     rng = np.random.default_rng(T * 100 + H * 10 + D)

@@ -22,7 +22,7 @@ def _jobs_for(wl, picks):
     return np.array(jobs, np.uint32)
 
 
-@pytest.mark.parametrize("T,H,D", [(16, 8, 128), (4, 2, 64), (2, 2, 256), (5, 3, 64)])
+@pytest.mark.parametrize("T,H,D", [(16, 8, 128), (4, 2, 64), (2, 2, 256), (5, 3, 64), (512, 1, 128)])
 def test_transcode_bit_exact_then_gather(hlkv_lib, oracle, cuda_device, T, H, D):
     import torch
     from hlkv.workload import build_workload
