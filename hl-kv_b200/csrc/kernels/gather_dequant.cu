@@ -164,12 +164,12 @@ __device__ __forceinline__ void stream_block(const Params& p, const Item& it, ui
       if (v < nchunks && r < it.valid_rows) {
         live |= 1u << u;
         if (f == dev::kFp16) {
-          raw[u] = dev::ld_stream(reinterpret_cast<const uint4*>(payload) + v);
+          raw[u] = dev::ld_stream256(reinterpret_cast<const uint4*>(payload) + v);
         } else if (f == dev::kInt4) {
-          raw[u].x = dev::ld_stream(reinterpret_cast<const uint32_t*>(payload) + v);
+          raw[u].x = dev::ld_stream256(reinterpret_cast<const uint32_t*>(payload) + v);
           prm[u] = wide ? it.prm : __ldg(reinterpret_cast<const float2*>(params) + row);
         } else {
-          const uint2 c = dev::ld_stream(reinterpret_cast<const uint2*>(payload) + v);
+          const uint2 c = dev::ld_stream256(reinterpret_cast<const uint2*>(payload) + v);
           raw[u].x = c.x;
           raw[u].y = c.y;
           prm[u].x = wide ? it.prm.x : __ldg(reinterpret_cast<const float*>(params) + row);
