@@ -76,6 +76,57 @@ def test_kernel_entry_points_reject_bad_arguments(hlkv_lib):
     assert L.hlkv_append_encode(C.byref(pools), C.byref(lay), None, 0, None, 0, None, 64, 0) == 0
 
 
+def test_attention_and_transcode_reject_bad_arguments(hlkv_lib):
+    """Argument checks of the attention entry points and the transcode, which return before
+    any CUDA call (the pointers below are never dereferenced)."""
+    import ctypes as C
+    L = hlkv_lib.lib()
+    pools = hlkv_lib.Pools()
+    lay = hlkv_lib.Layout(16, 8, 128, 1)
+    p8, err = C.c_void_p(256), C.c_void_p(512)
+    INV, OK, SMALL = hlkv_lib.INVALID_ARGUMENT, hlkv_lib.OK, hlkv_lib.BUFFER_TOO_SMALL
+
+    def attn(layout=lay, nseq=1, qh=32, scale=0.1, e=err):
+        return L.hlkv_decode_attention(C.byref(pools), C.byref(layout), None, 0, None, 0, p8, nseq, p8,
+                                       qh, scale, p8, e, None)
+
+    assert attn(e=None) == INV
+    assert attn(qh=12) == INV                    # not a multiple of the 8 KV heads
+    assert attn(qh=8 * 16) == INV                # group 16: groups are 1, 2, 4, 8
+    assert attn(scale=0.0) == INV and attn(scale=float("inf")) == INV and attn(scale=float("nan")) == INV
+    assert attn(layout=hlkv_lib.Layout(16, 8, 256, 1)) == INV  # head_dim 64 or 128 only
+    assert attn(layout=hlkv_lib.Layout(1024, 8, 128, 1)) == INV  # more than 512 block tokens
+    assert attn(nseq=0) == OK                    # empty batch: nothing to do
+
+    def split(splits, ws, ws_bytes):
+        return L.hlkv_decode_attention_split(C.byref(pools), C.byref(lay), None, 0, None, 0, p8, 4, p8,
+                                             32, 0.1, splits, ws, ws_bytes, p8, err, None)
+
+    need = hlkv_lib.decode_attention_workspace_bytes(4, 8, 128, 3)
+    assert split(0, p8, need) == INV                       # no splits
+    assert split(3, None, need) == INV                     # no workspace
+    assert split(3, C.c_void_p(264), need) == INV          # workspace not 16-byte aligned
+    assert split(3, p8, need - 1) == SMALL
+
+    def balanced(ctas, ws_bytes):
+        return L.hlkv_decode_attention_balanced(C.byref(pools), C.byref(lay), None, 0, None, 0, p8, 4, p8,
+                                                32, 0.1, ctas, p8, ws_bytes, p8, err, None)
+
+    bneed = hlkv_lib.decode_attention_balanced_workspace_bytes(4, 8, 128, 64)
+    assert balanced((1 << 20) + 1, 1 << 40) == INV         # at most 2^20 CTAs
+    assert balanced(64, bneed - 1) == SMALL
+
+    def transcode(n, jobs, e=err, layout=lay):
+        return L.hlkv_transcode(C.byref(pools), C.byref(layout), jobs, n, e, None)
+
+    assert transcode(1, p8, e=None) == INV
+    assert transcode(1, None) == INV
+    assert transcode(1, C.c_void_p(264)) == INV            # jobs not 16-byte aligned
+    assert transcode(1, p8, layout=hlkv_lib.Layout(16, 8, 100, 1)) == INV
+    assert transcode(0, None) == OK
+    assert L.hlkv_last_cuda_error() == 0
+
+
 def test_product_does_not_load_the_oracle(hlkv_lib):
     """The product library links no oracle code."""
     import subprocess
