@@ -337,6 +337,9 @@ int hlkv_quantize(int format, const float* d_in, size_t n, size_t group_size, fl
                   hlkv_stream_t stream);
 
 /* ---- host table (hl::alloc::HeteroBlockTable, hetero_block_table.hpp:141-245) ----------- */
+/* The table (and device-table) calls take a handle from hlkv_table_create / _restore
+ * (hlkv_device_tables_create); like the C++ object references they stand for, a NULL or
+ * destroyed handle is not checked. */
 typedef struct hlkv_table hlkv_table;
 
 typedef struct {
