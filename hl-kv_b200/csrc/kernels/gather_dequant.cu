@@ -27,7 +27,6 @@
 #include <cuda_runtime.h>
 
 #include <cstdint>
-#include <cstdlib>
 
 #include "codec.cuh"
 #include "common.cuh"
@@ -37,15 +36,8 @@ namespace hlkv {
 namespace {
 
 constexpr int kThreads = 256;
-#ifndef HLKV_GATHER_MIN_CTAS
-#define HLKV_GATHER_MIN_CTAS 4
-#endif
-#ifndef HLKV_GATHER_UNROLL
-#define HLKV_GATHER_UNROLL 4
-#endif
-constexpr int kMinCtasPerSm = HLKV_GATHER_MIN_CTAS;  // 4: 64 registers per thread
-constexpr int kUnroll = HLKV_GATHER_UNROLL;          // chunks per lane per tile: 2 KB tiles
-constexpr int kDefaultWaves = 1;
+constexpr int kMinCtasPerSm = 4;  // 64 registers per thread
+constexpr int kUnroll = 4;        // chunks per lane per tile: 2 KB tiles
 constexpr uint32_t kTileChunks = 32 * kUnroll;  // 8-element chunks per warp tile
 
 struct DevPool {
@@ -287,19 +279,7 @@ __global__ void __launch_bounds__(kThreads, kMinCtasPerSm) gather_dequant_kernel
   if ((threadIdx.x & 31) == 0) dev::bulk_wait_all();
 }
 
-// Grid = waves x (SMs x resident CTAs).  With more than one wave the hardware
-// block scheduler hands freed SM slots to the next CTA, which evens out the
-// per-CTA work (blocks of different formats carry different byte counts).
-// HLKV_GATHER_WAVES overrides the default for tuning.
-int gather_waves() {
-  static const int waves = [] {
-    const char* e = std::getenv("HLKV_GATHER_WAVES");
-    const int v = e != nullptr ? std::atoi(e) : 0;
-    return v >= 1 && v <= 64 ? v : kDefaultWaves;
-  }();
-  return waves;
-}
-
+// Grid = one wave of SMs x resident CTAs (more waves measured no faster).
 template <int kD>
 int grid_for() {
   static thread_local int cached_device = -1;
@@ -312,7 +292,7 @@ int grid_for() {
                                                       0) != cudaSuccess) {
       return 0;
     }
-    cached_grid = sm_count() * (per_sm > 0 ? per_sm : 1) * gather_waves();
+    cached_grid = sm_count() * (per_sm > 0 ? per_sm : 1);
     cached_device = device;
   }
   return cached_grid;

@@ -24,7 +24,11 @@ import subprocess
 import sys
 
 HERE = os.path.dirname(os.path.abspath(__file__))
-REF_ROOT = os.environ.get("HLKV_REFERENCE_ROOT", "/root/reference")
+# The reference tree: HLKV_REFERENCE_ROOT, else a checkout named "reference" beside
+# this repository.  Where neither exists (a machine that only runs the prebuilt
+# libraries), nothing of the reference is built.
+REF_ROOT = os.environ.get("HLKV_REFERENCE_ROOT") or os.path.normpath(
+    os.path.join(HERE, os.pardir, os.pardir, "reference"))
 BUILD_DIR = os.path.join(HERE, "_build")
 REF_DIR = os.path.join(HERE, "_ref")
 ORACLE_SO = os.path.join(BUILD_DIR, "liboracle.so")
