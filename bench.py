@@ -1,29 +1,37 @@
 """Benchmark of the heterogeneous KV gather-dequant path on B200.
 
     python bench.py [--gpus N] [--steps K] [--warmup W] [--impl hlkv|reference]
-                    [--workload mixed|mixed_updates|homogeneous|fp16|e4m3|int4|llama8b|llama70b|decode|decode_small]
+                    [--workload llama8b|mixed|mixed_updates|homogeneous|fp16|e4m3|int4|llama70b|decode|...]
 
-Default workload ("mixed", the headline configuration): one step = one
-hlkv_gather_dequant launch over a single-layer cache of 64 sequences x 2048
-tokens, 16-token blocks, 8 KV heads x 128, K and V; per-block format FP16 0.25
-/ E4M3 0.5 / INT4 0.25; N(0,1) values with 4 outlier channels per head x20;
-block ids and slots scattered by a seeded scramble.  Inputs and outputs (about
-850 MB) exceed the 126 MB L2, so no flush is needed between steps.  With N GPUs
-(torchrun), each rank holds its own cache of that size (weak scaling, no
-inter-GPU traffic); ranks meet only at barriers and at the max-over-ranks
-reduction of the timings.
+Default workload ("llama8b", the Llama-3-8B-shaped cache): 32 layers of 64
+sequences x 8192 tokens, 16-token blocks, 8 KV heads x 128, K and V, age tiers
+(newest 512 tokens FP16, the 2048 before them E4M3, the rest INT4), N(0,1)
+values with 4 outlier channels per head x20, block ids and slots scattered by a
+seeded scramble.  The sequences are sharded over the N GPUs (one process each,
+torchrun for N > 1; strong scaling, no inter-GPU traffic): one step is one
+hlkv_gather_dequant launch per layer into an FP16 scratch buffer of a layer's
+size.  A step moves 95 GB at N=1, far more than the 126 MB L2, so no flush is
+needed.  Ranks meet only at barriers and at the max-over-ranks reduction of the
+timings.
 
-Other workloads: "homogeneous" (1 sequence x 4096 tokens of E4M3, L2-resident:
-flushed between steps), single-format caches "fp16" / "e4m3" / "int4", and the
-multi-layer caches "llama8b" (32 layers, 64 x 8192 tokens, age tiers) and
-"llama70b" (8 resident layers of 16 x 131072 tokens), whose sequences are
-sharded over the ranks (strong scaling); one step there is one launch per
-layer into a single FP16 scratch buffer.
+Other workloads: "mixed" (one layer of 64 x 2048 tokens, per-block formats FP16
+.25 / E4M3 .5 / INT4 .25, a cache per GPU: weak scaling), "homogeneous" (1
+sequence x 4096 tokens of E4M3, L2-resident: flushed between steps),
+single-format caches "fp16" / "e4m3" / "int4", "llama70b" (8 resident layers of
+16 x 131072 tokens with 1000 descriptor updates per step), the decode-step
+append ("decode"), decode attention ("attn_*") and the flat FP8 drop-in
+("flat_*").
 
 value = algorithmic bytes of all ranks / max-over-ranks device time, GB/s.
 Algorithmic bytes per block = codes + row parameters read + 2*T*H*D*2 bytes
 written + 20 bytes of descriptor and arena entry (131 092 / 99 348 / 83 988
 bytes for FP16 / E4M3 / INT4 blocks).
+
+Beside it the line carries: `e2e` (the same metric through the C ABI with host
+buffers: segments up, every layer's FP16 output down), `parity` (the last
+launch's output for a sample of sequences against the reference's CPU gather,
+bit for bit), `roofline` and `cpu_baseline` (the reference's CPU gather of the
+same sample on all host threads).
 
 --impl reference times the reference's CPU path instead (its
 dequantize_reference_to_fp16 per parameter group walked through its own
@@ -55,7 +63,9 @@ WORKLOADS = {
                           updates=1000,
                           name="mixed-format single layer (as 'mixed') + 1000 random descriptor "
                                "updates per step (valid tokens; format changes transcoded on the device)"),
-    "homogeneous": dict(nseq=1, blocks=256, probs=(0.0, 1.0, 0.0, 0.0), scaling="weak",
+    "homogeneous": dict(nseq=1, blocks=256, probs=(0.0, 1.0, 0.0, 0.0), scaling="weak", flush=True,
+                        l2="25 MB per step fits the L2: a 2x-L2 buffer is overwritten between steps, "
+                           "value from the per-step events",
                         name="homogeneous E4M3: 1 seq x 4096 tok, 16-tok blocks, 8 KV heads x 128, K+V"),
     # Single-format caches of the mixed workload's size: per-format throughput.
     "fp16": dict(nseq=64, blocks=128, probs=(1.0, 0.0, 0.0, 0.0), scaling="weak",
@@ -66,13 +76,13 @@ WORKLOADS = {
                  name="INT4 only: 64 seq x 2048 tok, 16-tok blocks, 8 KV heads x 128, K+V"),
     # Llama-3-8B-shaped cache sharded by sequence; a step dequantizes all 32 layers, one
     # launch per layer into one FP16 scratch buffer.
-    "llama8b": dict(nseq=64, tokens=8192, tiers=(512, 2048), layers=32, scaling="strong",
+    "llama8b": dict(nseq=64, tokens=8192, tiers=(512, 2048), layers=32, scaling="strong", cpu_sample_seqs=2,
                     name="Llama-3-8B cache: 32 layers, 64 seq x 8192 tok sharded by sequence, "
                          "8 KV heads x 128, K+V; newest 512 tok FP16, previous 2048 E4M3, rest INT4"),
     # Llama-3-70B-shaped long context sharded by sequence; 8 resident layers per GPU (the
     # 80-layer payload of 234 GB does not fit one GPU), one launch per layer per step.
     "llama70b": dict(nseq=16, blocks=8192, probs=(0.05, 0.10, 0.0, 0.85), layers=8,
-                     scaling="strong", updates=1000,
+                     scaling="strong", updates=1000, cpu_sample_seqs=1,
                      name="Llama-3-70B long context: 16 seq x 131072 tok sharded by sequence, "
                           "8 resident layers, 8 KV heads x 128, K+V; INT4 .85 / E4M3 .10 / FP16 .05; "
                           "1000 random descriptor updates (valid_tokens changes and format "
@@ -80,7 +90,7 @@ WORKLOADS = {
     # Decode attention straight from the quantized blocks of the mixed cache: 32 query
     # heads over the 8 KV heads (Llama-3-8B's GQA group of 4), one query per sequence.
     "attn_mixed": dict(nseq=64, blocks=128, probs=(0.25, 0.5, 0.0, 0.25), scaling="weak",
-                       attn=True, q_heads=32,
+                       attn=True, q_heads=32, l2="L2 flushed between launches (313 MB read per step)",
                        name="decode attention fused with dequant over the mixed cache: 64 seq x 2048 "
                             "tok, 8 KV heads x 128, 32 query heads, FP16 .25 / E4M3 .5 / INT4 .25"),
     # Decode attention over one layer of the long-context cache (config 5's shape: 16 seq x
@@ -94,17 +104,19 @@ WORKLOADS = {
     # tokens among 56 of 512 (mixed formats as 'mixed'), where one CTA per (sequence, KV head)
     # leaves most SMs idle while the long sequences finish.
     "attn_varied": dict(nseq=64, blocks=[1024] * 8 + [32] * 56, probs=(0.25, 0.5, 0.0, 0.25), scaling="weak",
-                        attn=True, q_heads=32,
+                        attn=True, q_heads=32, l2="L2 flushed between launches",
                         name="decode attention fused with dequant, mixed lengths: 8 seq x 16384 tok + 56 seq x "
                              "512 tok, 8 KV heads x 128, 32 query heads, FP16 .25 / E4M3 .5 / INT4 .25"),
     # Config 1's data as one contiguous E4M3 array (8,388,608 values, 128-value groups):
     # the drop-in hlkv_dequantize_fp8_to_fp16 against the reference's own GPU kernel.
     "flat_e4m3": dict(n=8_388_608, group=128, fmt=1, scaling="weak", flat=True,
+                      l2="L2 flushed between launches",
                       name="contiguous E4M3 -> FP16: 8,388,608 values (1 seq x 4096 tok x K+V x 8 "
                            "heads x 128), scale per 128 values; drop-in vs the reference's kernel"),
     # The same conversion at 2^28 values (805 MB moved, over 6x L2): the drop-in against the
     # reference's own kernel where bandwidth rather than launch latency sets the time.
     "flat_e4m3_large": dict(n=268_435_456, group=128, fmt=1, scaling="weak", flat=True,
+                            l2="L2 flushed between launches",
                             name="contiguous E4M3 -> FP16: 268,435,456 values, scale per 128 values; "
                                  "drop-in vs the reference's kernel at a bandwidth-bound size"),
     # Decode step: every (sequence, layer) stream appends one token, encoded into its tail
@@ -160,12 +172,13 @@ import pynvml
 pynvml.nvmlInit()
 h = pynvml.nvmlDeviceGetHandleByIndex(int(sys.argv[1]))
 period = float(sys.argv[2])
-print("max", pynvml.nvmlDeviceGetMaxClockInfo(h, pynvml.NVML_CLOCK_SM), flush=True)
+out = open(sys.argv[3], "w", buffering=1)
+print("max", pynvml.nvmlDeviceGetMaxClockInfo(h, pynvml.NVML_CLOCK_SM), file=out)
 while True:
     try:
         mhz = pynvml.nvmlDeviceGetClockInfo(h, pynvml.NVML_CLOCK_SM)
         reasons = pynvml.nvmlDeviceGetCurrentClocksEventReasons(h)
-        print(time.time(), mhz, reasons, flush=True)
+        print(time.time(), mhz, reasons, file=out)
     except pynvml.NVMLError:
         pass
     time.sleep(period)
@@ -174,10 +187,12 @@ while True:
 
 class ClockSampler:
     """Samples SM clock and throttle reasons of one GPU through NVML in a child process
-    (NVML calls made from the benchmarked process contend with its CUDA calls).
-    Sample times are time.time(); summary() takes the same clock."""
+    (NVML calls made from the benchmarked process contend with its CUDA calls).  The
+    child appends to a temporary file, so a long run never blocks it on a full pipe;
+    __enter__ returns once the first sample is in.  Sample times are time.time();
+    summary() takes the same clock."""
 
-    def __init__(self, index: int, period_s: float = 0.002):
+    def __init__(self, index: int, period_s: float = 0.02):
         # NVML enumerates all GPUs; map the CUDA index through CUDA_VISIBLE_DEVICES.
         vis = os.environ.get("CUDA_VISIBLE_DEVICES")
         self.index = int(vis.split(",")[index]) if vis and vis.split(",")[0].isdigit() else index
@@ -185,14 +200,28 @@ class ClockSampler:
         self.samples: list[tuple[float, int, int]] = []
         self.max_mhz = None
         self._p = None
+        self._path = None
+
+    def _read(self) -> list[list[str]]:
+        try:
+            with open(self._path) as f:
+                return [line.split() for line in f.read().splitlines()]
+        except OSError:
+            return []
 
     def __enter__(self):
         import subprocess
+        import tempfile
         try:
-            self._p = subprocess.Popen([sys.executable, "-c", _SAMPLER, str(self.index), str(self.period)],
-                                       stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
-            first = self._p.stdout.readline().split()
-            self.max_mhz = int(first[1]) if len(first) == 2 and first[0] == "max" else None
+            fd, self._path = tempfile.mkstemp(prefix="hlkv_clocks_", suffix=".txt")
+            os.close(fd)
+            self._p = subprocess.Popen([sys.executable, "-c", _SAMPLER, str(self.index), str(self.period),
+                                        self._path], stdout=subprocess.DEVNULL, stderr=subprocess.DEVNULL)
+            deadline = time.time() + 20.0
+            while time.time() < deadline and self._p.poll() is None:
+                if any(len(f) == 3 for f in self._read()):
+                    break
+                time.sleep(0.02)
         except Exception:
             self._p = None
         return self
@@ -200,23 +229,33 @@ class ClockSampler:
     def __exit__(self, *exc):
         if self._p is None:
             return
-        time.sleep(2 * self.period)
+        time.sleep(max(0.1, 3 * self.period))
         self._p.terminate()  # this child only, by its own handle
-        out, _ = self._p.communicate(timeout=30)
-        for line in out.splitlines():
-            f = line.split()
-            if len(f) == 3:
+        try:
+            self._p.wait(timeout=30)
+        except Exception:
+            pass
+        for f in self._read():
+            if len(f) == 2 and f[0] == "max":
+                self.max_mhz = int(f[1])
+            elif len(f) == 3:
                 self.samples.append((float(f[0]), int(f[1]), int(f[2])))
+        try:
+            os.unlink(self._path)
+        except OSError:
+            pass
 
     def summary(self, t0: float, t1: float) -> dict:
+        """Samples inside [t0, t1] (the timed region); a region shorter than three sample
+        periods is widened to the whole sampled window (warm-up included)."""
         names = {0x2: "applications_clocks_setting", 0x4: "sw_power_cap", 0x8: "hw_slowdown",
                  0x20: "sw_thermal_slowdown", 0x40: "hw_thermal_slowdown",
                  0x80: "hw_power_brake_slowdown", 0x100: "display_clock_setting"}
         inside = [s for s in self.samples if t0 <= s[0] <= t1]
-        window = "timed"
-        if len(inside) < 3:  # very short timed regions: widen to the neighbouring samples
-            inside = [s for s in self.samples if t0 - 0.25 <= s[0] <= t1 + 0.25]
-            window = "timed +-0.25 s"
+        window = "timed region"
+        if len(inside) < 3:
+            inside = list(self.samples)
+            window = "whole bench window (timed region shorter than 3 samples)"
         if not inside:
             return {"sm_mhz": None, "sm_max_mhz": self.max_mhz, "reasons": [], "samples": 0}
         reasons = sorted({n for _, _, r in inside for b, n in names.items() if r & b})
@@ -236,26 +275,77 @@ def traffic_from_profile(workload: str) -> int | None:
         return None
 
 
-def cpu_gather_sample(wl, nseq_sample: int, min_wall_s: float = 2.0, max_reps: int = 20):
-    """Times the reference's CPU path (oracle/_ref) -- or the C restatement when the reference
-    library is absent -- on host copies of the first nseq_sample sequences."""
+def static_config(workload: str, world: int) -> dict:
+    """The `config` object of the JSON line: a description of the workload that both arms
+    print identically (no measured or device-dependent values)."""
+    spec = WORKLOADS[workload]
+    cfg = {"workload": spec["name"], "key": workload, "scaling": spec["scaling"]}
+    for k in ("layers", "nseq", "tokens", "updates", "q_heads"):
+        if k in spec:
+            cfg[{"nseq": "sequences", "tokens": "tokens_per_sequence"}.get(k, k)] = spec[k]
+    cfg["l2"] = spec.get("l2", "a step's inputs and outputs exceed 4x the 126 MB L2: no flush needed")
+    cfg["parallelism"] = (f"sequences sharded over {world} GPU(s), one process each, no collective "
+                          "on the data path" if spec["scaling"] == "strong" else
+                          f"one cache per GPU x{world}, no collective on the data path")
+    return cfg
+
+
+def sample_inputs(wl, rows):
+    """Host copies of what the gather reads for the table sequences `rows` (indices into
+    wl.seqs): the device descriptor table and arena as the kernel sees them, the rows'
+    segments, and compact pools holding only the slots those blocks reference (their
+    descriptors' slots renumbered into the compact pools; the decode does not depend on the
+    slot number).  Keeps host memory to the sample's size on caches of tens of GB."""
+    import numpy as np
+    import torch
+    sys.path.insert(0, os.path.join(ROOT, "tests"))
+    from helpers import device_arena, device_table_words
+    table = device_table_words(wl).copy()
+    arena = device_arena(wl)
+    segs = np.ascontiguousarray(wl.segs_host[rows], dtype=np.uint32).reshape(-1, 2)
+    ids = np.concatenate([arena[o:o + n] for o, n in segs]) if len(segs) else np.zeros(0, np.uint32)
+    pools = {}
+    for f, (buf, sb, _) in wl.pools.items():
+        sel = ids[(table[ids, 1] & 0xF) == f]
+        if sel.size == 0:
+            continue
+        uniq, inv = np.unique(table[sel, 0], return_inverse=True)
+        host = buf[torch.from_numpy(uniq.astype(np.int64)).to(buf.device)].cpu().numpy().reshape(-1)
+        table[sel, 0] = inv.astype(np.uint32)
+        pools[f] = (host, sb, int(uniq.size))
+    return pools, table, arena, segs
+
+
+def cpu_gather_sample(wl, rows, out_dev, out_first_elem: int, timed: bool, min_wall_s: float = 10.0,
+                      max_reps: int = 200):
+    """The reference's CPU path (oracle/_ref: its dequantize_reference_to_fp16 per parameter
+    group, walked through the same descriptor table) -- or the C restatement when the
+    reference library is absent -- on the table sequences `rows`.  Its output is compared
+    bit for bit with the GPU's output for the same sequences (out_dev from element
+    out_first_elem on: `parity`); with `timed`, the gather is repeated on all host threads for
+    about min_wall_s seconds (`cpu_baseline`)."""
     import numpy as np
     from oracle.oracle import Oracle, Ref, ref_available
-    sys.path.insert(0, os.path.join(ROOT, "tests"))
-    from helpers import device_arena, device_table_words, host_pools
+    from hlkv.workload import block_bytes
     kind = "reference" if ref_available() else "port"
     impl = Ref() if kind == "reference" else Oracle()
-    segs = wl.segs_host[:nseq_sample]
+    pools, table, arena, segs = sample_inputs(wl, rows)
     nblocks = int(segs[:, 1].sum())
-    out = np.empty(nblocks * wl.block_elems, dtype=np.uint16)
-    pools, table, arena = host_pools(wl), device_table_words(wl), device_arena(wl)
+    out = np.empty(max(1, nblocks * wl.block_elems), dtype=np.uint16)
     threads = os.cpu_count() or 1
-    from hlkv.workload import block_bytes
-    ids = [arena[o:o + n] for o, n in segs]
+    ids = np.concatenate([arena[o:o + n] for o, n in segs])
     nbytes = sum(block_bytes(int(table[i][1] & 0xF), wl.T, wl.H, wl.D, int((table[i][1] >> 10) & 0x3FF))
-                 for row in ids for i in row)
-    impl.gather_dequant(pools, wl.T, wl.H, wl.D, wl.layout.layout_id, table, arena, segs, out,
-                        threads=threads)  # warm-up
+                 for i in ids)
+    err = impl.gather_dequant(pools, wl.T, wl.H, wl.D, wl.layout.layout_id, table, arena, segs, out,
+                              threads=threads)
+    got = out_dev[out_first_elem:out_first_elem + nblocks * wl.block_elems].cpu().numpy().view(np.uint16)
+    parity = {"ok": bool(err == 0 and np.array_equal(got, out[:nblocks * wl.block_elems])),
+              "checked": f"{len(rows)} sequences ({nblocks} blocks, {nblocks * wl.block_elems} fp16 values) "
+                         f"of the last launch's output against the reference's CPU gather ({kind}), "
+                         "bit for bit",
+              "differing_values": int(np.count_nonzero(got != out[:nblocks * wl.block_elems]))}
+    if not timed:
+        return parity, None
     reps, t0 = 0, time.perf_counter()
     while True:
         err = impl.gather_dequant(pools, wl.T, wl.H, wl.D, wl.layout.layout_id, table, arena, segs,
@@ -266,9 +356,9 @@ def cpu_gather_sample(wl, nseq_sample: int, min_wall_s: float = 2.0, max_reps: i
             break
     assert err == 0
     gbs = nbytes * reps / wall / 1e9
-    return {"value": round(gbs, 3), "unit": "GB/s", "cores": threads, "kind": kind,
-            "sample": f"{nseq_sample} of {len(wl.segs_host)} sequences ({nblocks} blocks, "
-                      f"{nbytes / 1e6:.1f} MB algorithmic) x {reps} passes, {wall:.2f} s wall"}
+    return parity, {"value": round(gbs, 3), "unit": "GB/s", "cores": threads, "kind": kind,
+                    "sample": f"{len(rows)} sequences of one layer ({nblocks} blocks, {nbytes / 1e6:.1f} MB "
+                              f"algorithmic) x {reps} passes, {wall:.2f} s wall"}
 
 
 def build_bench_workload(spec: dict, rank: int, world: int, spare_slots: int = 0):
@@ -288,104 +378,12 @@ def build_bench_workload(spec: dict, rank: int, world: int, spare_slots: int = 0
     return build_workload(rows, seed=1000 + rank, spare_slots=spare_slots), n
 
 
-class RandomUpdates:
-    """Seeded stream of descriptor updates applied before each sweep of a multi-layer
-    cache: half set_valid_tokens on a random unsealed block, half format changes to the
-    next tier (seal, begin_format_change, device transcode, commit), then one delta flush,
-    all queued on the stream ahead of the sweep's launches.  Keeps the sweep's algorithmic
-    bytes current (valid tokens and formats change them)."""
-
-    _NEXT = {0: 1, 1: 3, 3: 1}  # FP16 -> E4M3 -> INT4 -> E4M3
-
-    def __init__(self, wl, n: int, seed: int):
-        import numpy as np
-        import torch
-        from hlkv.workload import block_bytes
-        self.wl, self.n, self.block_bytes = wl, n, block_bytes
-        self.rng = np.random.default_rng(seed)
-        self.ids = np.concatenate([np.array(wl.table.sequence_block_ids(s)[1], np.uint32)
-                                   for s in wl.seqs])
-        m = wl.table.max_blocks()
-        self.sealed = np.zeros(m, bool)
-        self.fmt = np.zeros(m, np.uint8)
-        self.vt = np.zeros(m, np.uint32)
-        for bid in self.ids:
-            info = wl.table.device_descriptor(int(bid))[1]
-            self.fmt[bid], self.vt[bid] = info & 0xF, (info >> 10) & 0x3FF
-        self.sweep_bytes = wl.algorithmic_bytes
-        self.jobs_host = torch.empty((n, 8), dtype=torch.int32).pin_memory()
-        self.jobs_dev = torch.empty((n, 8), dtype=torch.int32, device="cuda")
-        self.jobs_np = self.jobs_host.numpy().view(np.uint32)
-        self.uploaded = torch.cuda.Event()
-        self.first = True
-        self.counts = {"valid_tokens": 0, "format_changes": 0}
-
-    def _bytes(self, f: int, vt: int) -> int:
-        w = self.wl
-        return self.block_bytes(f, w.T, w.H, w.D, vt)
-
-    def prepare(self) -> int:
-        """Host half: one batch of table updates (commits included) collected into the
-        device tables' staging; returns the bytes the batch moves on the device."""
-        import hlkv
-        w, t, rng = self.wl, self.wl.table, self.rng
-        if not self.first:
-            self.uploaded.synchronize()  # the previous upload has read jobs_host
-        self.first = False
-        picks = rng.choice(self.ids.size, size=self.n, replace=False)
-        kinds = rng.integers(0, 2, size=self.n)
-        out_bytes = 2 * 2 * w.T * w.H * w.D + 20  # FP16 written + descriptor per block
-        nj, moved, changed = 0, 0, []
-        for i, kind in zip(picks, kinds):
-            bid = int(self.ids[i])
-            h = t.handle_of(bid)
-            f, vt = int(self.fmt[bid]), int(self.vt[bid])
-            if kind == 0 and not self.sealed[bid]:
-                nvt = int(rng.integers(1, w.T + 1))
-                assert t.set_valid_tokens(h, nvt) == 0
-                self.sweep_bytes += self._bytes(f, nvt) - self._bytes(f, vt)
-                self.vt[bid] = nvt
-                self.counts["valid_tokens"] += 1
-                moved += 32  # one descriptor patch read and written
-                continue
-            target = self._NEXT[f]
-            if not self.sealed[bid]:
-                assert t.seal(h) == 0
-                self.sealed[bid] = True
-            st, fc = t.begin_format_change(h, target)
-            assert st == 0, st
-            self.jobs_np[nj] = (fc[0], fc[1], fc[2], fc[3], vt, 0, 0, 0)
-            nj += 1
-            changed.append(h)
-            # source codes + params of the valid rows read, all destination rows written
-            moved += (self._bytes(f, vt) - out_bytes) + (self._bytes(target, w.T) - out_bytes) + 64
-            self.sweep_bytes += self._bytes(target, vt) - self._bytes(f, vt)
-            self.fmt[bid] = target
-        # The commits only change host state; the device sees them through the delta,
-        # which launch() queues after the transcode.
-        for h in changed:
-            assert t.commit_format_change(h, 0, 0) == 0
-        self.counts["format_changes"] += nj
-        self.n_jobs = nj
-        w.dt.collect(t)
-        return moved
-
-    def launch(self, stream, err) -> None:
-        """Device half: job upload, transcode, delta upload and kernel (3), in stream order."""
-        import hlkv
-        w, nj = self.wl, self.n_jobs
-        if nj:
-            self.jobs_dev[:nj].copy_(self.jobs_host[:nj], non_blocking=True)
-            self.uploaded.record(stream)
-            hlkv.transcode(w.hlkv_pools(), w.layout, self.jobs_dev[:nj], err, stream=stream)
-        w.dt.flush(stream)
-
-
 def run_hlkv(args) -> None:
     import numpy as np
     import torch
     import torch.distributed as dist
     import hlkv
+    from hlkv.workload import UpdateStream
 
     rank, world, local = dist_env()
     torch.cuda.set_device(local)
@@ -395,21 +393,25 @@ def run_hlkv(args) -> None:
                                 device_id=torch.device("cuda", local))
     spec = WORKLOADS[args.workload]
     layers = spec.get("layers", 1)
+    e2e_steps = max(1, min(args.steps, args.e2e_steps if layers == 1 else min(args.e2e_steps, 4)))
     # Format changes take a slot in the target pool before the commit frees the old one.
-    spare = spec.get("updates", 0) * (args.steps + args.warmup + 1)
+    spare = spec.get("updates", 0) * (args.steps + args.warmup + e2e_steps + 3)
+    t_build = time.perf_counter()
     wl, nseq_rank = build_bench_workload(spec, rank, world, spare)
+    build_s = time.perf_counter() - t_build
     pools = wl.hlkv_pools()
     # One launch per layer per step, all into one FP16 scratch buffer of a layer's size.
     layer_segs = [wl.segs[l * nseq_rank:(l + 1) * nseq_rank] for l in range(layers)]
     layer_blocks = [int(wl.segs_host[l * nseq_rank:(l + 1) * nseq_rank, 1].sum()) for l in range(layers)]
-    n_out = max(layer_blocks) * wl.block_elems
+    n_out = max(1, max(layer_blocks)) * wl.block_elems
     out = torch.empty(n_out, dtype=torch.int16, device="cuda")
     err = torch.zeros(1, dtype=torch.int32, device="cuda")
     stream = torch.cuda.current_stream()
 
-    updates = RandomUpdates(wl, spec["updates"], 5000 + rank) if spec.get("updates") else None
+    updates = UpdateStream(wl, spec["updates"], 5000 + rank) if spec.get("updates") else None
     moved = [0]  # algorithmic bytes of the steps run so far (updates change the sweep's bytes)
     host_update_s = [0.0]
+    launches = [0]
 
     def prepare():
         """Host work of a step (table updates), outside the device-timed window."""
@@ -420,38 +422,39 @@ def run_hlkv(args) -> None:
 
     def step():
         if updates is not None:
-            updates.launch(stream, err)
+            launches[0] += updates.launch(stream, err)
         moved[0] += updates.sweep_bytes if updates is not None else wl.algorithmic_bytes
         for segs in layer_segs:
             hlkv.gather_dequant(pools, wl.layout, wl.dt.table_ptr, wl.dt.table_size,
                                 wl.dt.arena_ptr, wl.dt.arena_size, segs, out, err, stream=stream)
+        launches[0] += len(layer_segs)
 
     def barrier():
         if world > 1:
             dist.barrier()
-
-    for _ in range(args.warmup):
-        prepare()
-        step()
-    torch.cuda.synchronize()
-    assert int(err.item()) == 0, f"error bits {int(err.item()):#x}"
 
     # Inputs + outputs smaller than a few L2 capacities would be served from L2 on the
     # next step: then a buffer of twice the L2 size is overwritten between steps and the
     # value is taken from the per-step events (the flush is not timed).
     l2_bytes = torch.cuda.get_device_properties(torch.cuda.current_device()).L2_cache_size
     flush = None
-    if wl.algorithmic_bytes < 4 * l2_bytes:
+    if spec.get("flush"):
         flush = torch.empty(2 * l2_bytes, dtype=torch.uint8, device="cuda")
     ev = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True))
           for _ in range(args.steps)]
     t_start = torch.cuda.Event(enable_timing=True)
     t_end = torch.cuda.Event(enable_timing=True)
     with ClockSampler(torch.cuda.current_device()) as clocks:
+        for _ in range(args.warmup):
+            prepare()
+            step()
+        torch.cuda.synchronize()
+        assert int(err.item()) == 0, f"error bits {int(err.item()):#x}"
         barrier()
         torch.cuda.synchronize()
         moved[0] = 0
         host_update_s[0] = 0.0
+        launches[0] = 0
         h0 = time.time()
         t_start.record(stream)
         for k in range(args.steps):
@@ -468,6 +471,7 @@ def run_hlkv(args) -> None:
     total_ms = t_start.elapsed_time(t_end)
     step_ms = [a.elapsed_time(b) for a, b in ev]
     bytes_per_step = moved[0] / args.steps
+    timed_launches = launches[0]
     assert int(err.item()) == 0
     if flush is not None or updates is not None:
         # the timed work is the launches, not the flushes or the host table updates between them
@@ -484,17 +488,17 @@ def run_hlkv(args) -> None:
     achieved = bytes_per_step / (mean_step_ms / 1e3) / 1e9
     mean_launch_ms = mean_step_ms / layers
 
-    e2e = None
-    if layers == 1:
-        e2e = measure_e2e(args, wl, out, err, stream, world, bytes_per_step, barrier)
-    else:
-        e2e = {"value": None, "unit": "GB/s", "h2d_bytes_per_step": None, "d2h_bytes_per_step": None,
-               "reason": "multi-layer cache is resident in HBM; end to end is measured on the "
-                         "single-layer workloads"}
+    # Parity and the CPU baseline, outside every timed region: the reference's CPU gather
+    # of the first sequences of the last layer (the last launch, whose output is still in
+    # `out`), compared bit for bit with the GPU output; timed on all host threads at N=1.
+    parity, cpu = None, None
+    if rank == 0:
+        k = min(spec.get("cpu_sample_seqs", 16), nseq_rank)
+        rows = list(range((layers - 1) * nseq_rank, (layers - 1) * nseq_rank + k))
+        parity, cpu = cpu_gather_sample(wl, rows, out, 0, timed=world == 1 and not args.no_cpu_baseline)
 
-    cpu = None
-    if world == 1 and not args.no_cpu_baseline and layers == 1:
-        cpu = cpu_gather_sample(wl, nseq_sample=min(16, len(wl.segs_host)))
+    e2e = measure_e2e(args, wl, layer_segs, nseq_rank, out, err, stream, world, e2e_steps, updates,
+                      barrier)
 
     if rank == 0:
         line = {
@@ -503,32 +507,33 @@ def run_hlkv(args) -> None:
             "ms_per_step": round(total_ms / args.steps, 5), "higher_is_better": True,
             "scaling": spec["scaling"], "vs_baseline": None, "dtype": "fp16 out; fp16/e4m3/int4 in",
             "data": "synthetic (seeded N(0,1) + outlier channels, quantized on the GPU)",
-            "config": {"workload": spec["name"], "layers": layers,
-                       "sequences_per_gpu": nseq_rank,
-                       "blocks_per_gpu": wl.total_blocks,
-                       "blocks_per_format": {"fp16": wl.blocks_per_format[0],
-                                             "e4m3": wl.blocks_per_format[1],
-                                             "int4": wl.blocks_per_format[3]},
-                       "bytes_per_step_per_gpu": round(bytes_per_step),
-                       "updates_per_step": spec.get("updates", 0),
-                       "updates_applied": updates.counts if updates is not None else None,
-                       "host_update_ms_per_step": round(1e3 * host_update_s[0] / args.steps, 3)
-                       if updates is not None else None,
-                       "l2": ("inputs+outputs (%.0f MB) exceed 4x the %.0f MB L2; no flush" % (
-                           bytes_per_step / 1e6, l2_bytes / 1e6)) if flush is None else
-                             ("L2 flushed between steps (%.0f MB overwritten); value from the "
-                              "per-step events" % (2 * l2_bytes / 1e6)),
-                       "parallelism": f"sequence-sharded x{world}, no collective on the data path"},
+            "config": static_config(args.workload, world),
+            "work": {"layers": layers, "sequences_per_gpu": nseq_rank,
+                     "blocks_per_gpu": wl.total_blocks,
+                     "blocks_per_format": {"fp16": wl.blocks_per_format[0],
+                                           "e4m3": wl.blocks_per_format[1],
+                                           "int4": wl.blocks_per_format[3]},
+                     "bytes_per_step_per_gpu": round(bytes_per_step),
+                     "updates_applied": updates.counts if updates is not None else None,
+                     "host_update_ms_per_step": round(1e3 * host_update_s[0] / args.steps, 3)
+                     if updates is not None else None,
+                     "l2": ("L2 flushed between steps (%.0f MB overwritten); value from the per-step "
+                            "events" % (2 * l2_bytes / 1e6)) if flush is not None else
+                           ("no flush: %.0f MB of inputs+outputs per step against a %.0f MB L2" % (
+                               bytes_per_step / 1e6, l2_bytes / 1e6)),
+                     "build_s": round(build_s, 1)},
             "per_gpu_gbs": round(per_gpu, 2),
             "pct_hbm_peak": round(100 * per_gpu / peak, 2),
             "roofline": {"bound": "hbm", "achieved": round(achieved, 2), "peak": peak,
                          "unit": "GB/s", "frac": round(achieved / peak, 4),
-                         "peak_source": f"{peak_kind} (MEASURED_PEAKS.json hbm_gbs)",
+                         "peak_source": f"{peak_kind} (MEASURED_PEAKS.json hbm_gbs, copy bandwidth)",
                          "traffic": traffic_from_profile(args.workload),
                          "kernel": "gather_dequant_kernel<128>",
                          "launch_ms": round(mean_launch_ms, 5)},
+            "parity": parity["ok"] if parity is not None else None,
+            "parity_detail": parity,
             "e2e": e2e,
-            "gpu_launches": args.steps * layers,  # gather launches in the timed region
+            "gpu_launches": timed_launches,  # gathers (+ transcode and delta with updates)
             "clocks": clocks.summary(h0, h1),
             "cpu_baseline": cpu,
         }
@@ -672,10 +677,10 @@ def run_decode(args) -> None:
             "ms_per_step": round(dev_total / args.steps, 5), "higher_is_better": True,
             "scaling": "strong", "vs_baseline": None, "dtype": "fp16 in; e4m3/int4 out",
             "data": "synthetic (seeded lengths, formats and N(0,1) tokens)",
-            "config": {"workload": spec["name"], "streams_per_gpu": n, "sequences_per_gpu": len(lengths),
-                       "blocks_at_start": int(nb.sum()), "bytes_per_step_per_gpu": round(step_bytes),
-                       "build_s": round(build_s, 1),
-                       "parallelism": f"sequence-sharded x{world}, no collective on the data path"},
+            "config": static_config(args.workload, world),
+            "work": {"streams_per_gpu": n, "sequences_per_gpu": len(lengths),
+                     "blocks_at_start": int(nb.sum()), "bytes_per_step_per_gpu": round(step_bytes),
+                     "build_s": round(build_s, 1)},
             "us_per_step": {"device": round(1e3 * dev_total / args.steps, 2),
                             "encode_kernel": round(1e3 * enc_mean, 2),
                             "delta_upload_and_apply": round(1e3 * delta_mean, 2),
@@ -826,12 +831,12 @@ def run_attention(args) -> None:
             "higher_is_better": True, "scaling": "weak", "vs_baseline": None,
             "dtype": "fp16/e4m3/int4 KV in; fp32 math; fp16 out",
             "data": "synthetic (seeded N(0,1) + outlier channels; N(0,1) queries)",
-            "config": {"workload": spec["name"], "bytes_per_step_per_gpu": nbytes,
-                       "kv_tokens_per_step_per_gpu": tokens, "query_heads": qh,
-                       "splits_per_sequence_head": None if ctas else splits,
-                       "balanced_ctas": ctas or None,
-                       "l2": "L2 flushed between launches" if flush is not None else "no flush needed",
-                       "parallelism": f"sequence-sharded x{world}, no collective on the data path"},
+            "config": static_config(args.workload, world),
+            "work": {"bytes_per_step_per_gpu": nbytes,
+                     "kv_tokens_per_step_per_gpu": tokens, "query_heads": qh,
+                     "splits_per_sequence_head": None if ctas else splits,
+                     "balanced_ctas": ctas or None,
+                     "l2": "L2 flushed between launches" if flush is not None else "no flush needed"},
             "kv_tokens_per_s": round(world * tokens * args.steps / (total_ms / 1e3), 1),
             "roofline": {"bound": "hbm", "achieved": round(nbytes / (mean_ms / 1e3) / 1e9, 2), "peak": peak,
                          "unit": "GB/s", "frac": round(nbytes / (mean_ms / 1e3) / 1e9 / peak, 4),
@@ -963,10 +968,10 @@ def run_flat(args) -> None:
             "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(total_ms / args.steps, 5),
             "higher_is_better": True, "scaling": "weak", "vs_baseline": None,
             "dtype": "e4m3 in; fp16 out", "data": "synthetic (seeded N(0,1), quantized on the GPU)",
-            "config": {"workload": spec["name"], "bytes_per_step_per_gpu": nbytes,
-                       "l2": "L2 flushed between launches (%.0f MB overwritten); value from the "
-                             "per-launch events" % (2 * l2_bytes / 1e6),
-                       "parallelism": f"one array per GPU x{world}"},
+            "config": static_config(args.workload, world),
+            "work": {"bytes_per_step_per_gpu": nbytes,
+                     "l2": "L2 flushed between launches (%.0f MB overwritten); value from the "
+                           "per-launch events" % (2 * l2_bytes / 1e6)},
             "roofline": {"bound": "hbm", "achieved": round(achieved, 2), "peak": peak, "unit": "GB/s",
                          "frac": round(achieved / peak, 4),
                          "peak_source": f"{peak_kind} (MEASURED_PEAKS.json hbm_gbs)", "traffic": None,
@@ -1016,90 +1021,112 @@ def _sum_over_ranks(values, world: int):
     return t.tolist()
 
 
-def measure_e2e(args, wl, out, err, stream, world, bytes_per_step, barrier) -> dict:
-    """End to end through the C ABI with host buffers: every step uploads the pools and
-    segments from pinned host memory, syncs the (unchanged) device tables, runs the
-    gather and reads the FP16 output back into pinned host memory.  Steps alternate
-    between two sets of device buffers on an upload stream and a readback stream, so
-    that one step's upload overlaps the previous step's readback (PCIe is full duplex);
-    every step still moves all of its bytes in both directions."""
+def measure_e2e(args, wl, layer_segs, nseq_rank, out, err, stream, world, e2e_steps, updates,
+                barrier) -> dict:
+    """End to end through the C ABI with host buffers.  The pools are the resident KV cache
+    (they stay in HBM, as in a serving engine); every step
+      * (with updates) runs the host table updates and their collect into pinned staging,
+        which kernel (3) reads in place, plus the transcode jobs' upload,
+      * uploads the step's segments of every layer from pinned host memory,
+      * runs one gather per layer into one of two FP16 scratch buffers, and
+      * reads each layer's FP16 output back into pinned host memory on a second stream,
+        overlapping the next layer's gather (a layer's scratch is reused two layers later,
+        after its readback).
+    Timed with CUDA events from before the first upload to after the last readback."""
     import numpy as np
     import torch
     import hlkv
-    e2e_steps = max(1, min(args.steps, args.e2e_steps))
-    n_out = out.numel()
-    host_pools = {f: buf.cpu().pin_memory() for f, (buf, _, _) in wl.pools.items()}
+    layers = len(layer_segs)
     host_segs = wl.segs.cpu().pin_memory()
-    host_out = [torch.empty(n_out, dtype=torch.int16).pin_memory() for _ in range(2)]
-    h2d = sum(p.numel() for p in host_pools.values()) + host_segs.numel() * 4
-    d2h = n_out * 2
-    dev_pools = [wl.pools, {f: (torch.empty_like(buf), sb, ns) for f, (buf, sb, ns) in wl.pools.items()}]
-    dev_segs = [wl.segs, torch.empty_like(wl.segs)]
+    dev_segs = torch.empty_like(wl.segs)
     dev_out = [out, torch.empty_like(out)]
-    hl_pools = [hlkv.make_pools(dp) for dp in dev_pools]
-    s_in, s_out = torch.cuda.Stream(), torch.cuda.Stream()
-    uploaded = [torch.cuda.Event() for _ in range(2)]
+    host_out = [torch.empty(out.numel(), dtype=torch.int16).pin_memory() for _ in range(2)]
+    layer_elems = [int(s[:, 1].sum().item()) * wl.block_elems for s in layer_segs]
+    s_out = torch.cuda.Stream()
     gathered = [torch.cuda.Event() for _ in range(2)]
     read_back = [torch.cuda.Event() for _ in range(2)]
     used = [False, False]
+    pools = wl.hlkv_pools()
+    staged = [0]
+    moved = [0]
 
-    def e2e_step(k: int) -> None:
-        b = k & 1
-        with torch.cuda.stream(s_in):
+    def e2e_step() -> None:
+        if updates is not None:
+            nd, ni = wl.table.pending()
+            moved[0] += updates.prepare()
+            staged[0] += 16 * nd + 8 * ni + 32 * updates.n_jobs
+        dev_segs.copy_(host_segs, non_blocking=True)
+        if updates is not None:
+            updates.launch(stream, err)
+        moved[0] += updates.sweep_bytes if updates is not None else wl.algorithmic_bytes
+        for l in range(layers):
+            b = l & 1
             if used[b]:
-                s_in.wait_event(gathered[b])  # the gather two steps back has read pools[b]
-            for f, (buf, _, _) in dev_pools[b].items():
-                buf.copy_(host_pools[f], non_blocking=True)
-            dev_segs[b].copy_(host_segs, non_blocking=True)
-            uploaded[b].record(s_in)
-        stream.wait_event(uploaded[b])
-        if used[b]:
-            stream.wait_event(read_back[b])  # out[b] of two steps back has been read back
-        wl.dt.sync(wl.table, stream)
-        hlkv.gather_dequant(hl_pools[b], wl.layout, wl.dt.table_ptr, wl.dt.table_size,
-                            wl.dt.arena_ptr, wl.dt.arena_size, dev_segs[b], dev_out[b], err,
-                            stream=stream)
-        gathered[b].record(stream)
-        with torch.cuda.stream(s_out):
-            s_out.wait_event(gathered[b])
-            host_out[b].copy_(dev_out[b], non_blocking=True)
-            read_back[b].record(s_out)
-        used[b] = True
+                stream.wait_event(read_back[b])  # the readback of this scratch is done
+            hlkv.gather_dequant(pools, wl.layout, wl.dt.table_ptr, wl.dt.table_size, wl.dt.arena_ptr,
+                                wl.dt.arena_size, dev_segs[l * nseq_rank:(l + 1) * nseq_rank], dev_out[b],
+                                err, stream=stream)
+            gathered[b].record(stream)
+            with torch.cuda.stream(s_out):
+                s_out.wait_event(gathered[b])
+                host_out[b][:layer_elems[l]].copy_(dev_out[b][:layer_elems[l]], non_blocking=True)
+                read_back[b].record(s_out)
+            used[b] = True
 
-    e2e_step(0)
-    e2e_step(1)
+    e2e_step()
     torch.cuda.synchronize()
     barrier()
+    staged[0] = 0
+    moved[0] = 0
     e0 = torch.cuda.Event(enable_timing=True)
     e1 = torch.cuda.Event(enable_timing=True)
+    w0 = time.perf_counter()
     e0.record(stream)
-    s_in.wait_event(e0)
-    s_out.wait_event(e0)
-    for k in range(e2e_steps):
-        e2e_step(k)
+    for _ in range(e2e_steps):
+        e2e_step()
+    s_out.wait_stream(stream)
     e1.record(s_out)  # after the last readback, which follows every other operation
     torch.cuda.synchronize()
-    (e2e_ms,) = max_over_ranks([e0.elapsed_time(e1)], world, "cuda")
-    e2e_value = world * bytes_per_step * e2e_steps / (e2e_ms / 1e3) / 1e9
-    last = (e2e_steps - 1) & 1
-    ok_bits = np.array_equal(host_out[last].numpy().view(np.uint16),
-                             dev_out[last].cpu().numpy().view(np.uint16))
+    wall_s = time.perf_counter() - w0
+    e2e_ms, wall_ms = max_over_ranks([e0.elapsed_time(e1), 1e3 * wall_s], world, "cuda")
+    bytes_per_step = moved[0] / e2e_steps
+    if world > 1 and WORKLOADS[args.workload]["scaling"] == "strong":
+        (job_bytes,) = _sum_over_ranks([bytes_per_step], world)
+    else:
+        job_bytes = world * bytes_per_step
+    e2e_value = job_bytes * e2e_steps / (max(e2e_ms, wall_ms) / 1e3) / 1e9
+    last = (layers - 1) & 1
+    ok_bits = np.array_equal(host_out[last][:layer_elems[-1]].numpy().view(np.uint16),
+                             dev_out[last][:layer_elems[-1]].cpu().numpy().view(np.uint16))
     assert int(err.item()) == 0
+    h2d = host_segs.numel() * 4 + staged[0] // e2e_steps
+    d2h = 2 * sum(layer_elems)
     return {"value": round(e2e_value, 2), "unit": "GB/s", "steps": e2e_steps,
+            "per_gpu": round(e2e_value / world, 2),
             "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h,
-            "path": "pinned host pools+segments -> H2D -> device-table sync -> "
-                    "hlkv_gather_dequant -> D2H of the FP16 output; two buffer sets, "
-                    "upload of step k overlaps readback of step k-1", "readback_ok": ok_bits}
+            "ms_per_step": round(max(e2e_ms, wall_ms) / e2e_steps, 3),
+            "d2h_gbs_per_gpu": round(d2h / (max(e2e_ms, wall_ms) / e2e_steps / 1e3) / 1e9, 2),
+            "path": ("host table updates + collect_delta (pinned staging read in place by kernel 3) -> "
+                     if updates is not None else "") +
+                    "pinned host segments -> H2D -> hlkv_gather_dequant per layer (pools resident "
+                    "in HBM) -> D2H of every layer's FP16 output into pinned host memory, "
+                    "overlapped with the next layer's gather",
+            "readback_ok": bool(ok_bits)}
 
 
-def _blocks_and_probs(spec: dict):
-    """Blocks per sequence-layer and the format mix; age tiers become their proportions
-    (the CPU cost of a block depends only on its format)."""
-    if "tiers" not in spec:
-        return spec["blocks"], spec["probs"]
-    nb = spec["tokens"] // 16
-    n16, n8 = spec["tiers"][0] // 16, spec["tiers"][1] // 16
-    return nb, (n16 / nb, n8 / nb, 0.0, (nb - n16 - n8) / nb)
+def _cpu_formats(spec: dict, nseq: int, seed: int) -> list:
+    """Per-block formats of nseq sequences of one layer of the workload: the age tiers
+    (oldest blocks INT4, then E4M3, the newest FP16) or a seeded draw from the mix."""
+    import numpy as np
+    if "tiers" in spec:
+        nb = spec["tokens"] // 16
+        n16, n8 = spec["tiers"][0] // 16, spec["tiers"][1] // 16
+        row = np.array([3] * (nb - n16 - n8) + [1] * n8 + [0] * n16, dtype=np.uint8)
+        return [row.copy() for _ in range(nseq)]
+    blocks = spec["blocks"] if np.isscalar(spec["blocks"]) else int(np.mean(spec["blocks"]))
+    rng = np.random.default_rng(seed + 1)
+    p = np.asarray(spec["probs"], dtype=np.float64)
+    return [rng.choice(np.arange(4, dtype=np.uint8), size=blocks, p=p / p.sum()) for _ in range(nseq)]
 
 
 def run_reference(args) -> None:
@@ -1120,25 +1147,24 @@ def run_reference(args) -> None:
         return
     # Size the per-step sample so that warm-up + steps stay within about two minutes.
     budget_s = 120.0 / max(1, args.steps + args.warmup)
-    blocks, probs = _blocks_and_probs(spec)
-    wl = build_cpu_workload(kind, nseq=1, blocks=blocks, probs=probs, seed=1000)
+    wl = build_cpu_workload(kind, formats=_cpu_formats(spec, 1, 1000), seed=1000)
     per_seq_s = time_cpu_gather(wl, threads)[0]
     nseq = int(max(1, min(spec["nseq"], budget_s / max(per_seq_s, 1e-6))))
-    wl = build_cpu_workload(kind, nseq=nseq, blocks=blocks, probs=probs, seed=1000)
+    wl = build_cpu_workload(kind, formats=_cpu_formats(spec, nseq, 1000), seed=1000)
     for _ in range(args.warmup):
         time_cpu_gather(wl, threads)
     times = [time_cpu_gather(wl, threads)[0] for _ in range(args.steps)]
     total = sum(times)
     value = wl["bytes"] * args.steps / total / 1e9
-    sample = (f"{nseq} of {spec['nseq']} sequences ({wl['blocks']} blocks, "
+    sample = (f"{nseq} of {spec['nseq']} sequences of one layer ({wl['blocks']} blocks, "
               f"{wl['bytes'] / 1e6:.1f} MB algorithmic) per step")
     print(json.dumps({
         "impl": "reference", "metric": METRIC, "value": round(value, 3), "unit": "GB/s",
         "n_gpus": world, "steps": args.steps, "warmup": args.warmup,
         "ms_per_step": round(1e3 * total / args.steps, 3), "higher_is_better": True,
-        "scaling": "weak", "vs_baseline": None, "dtype": "fp16 out; fp16/e4m3/int4 in",
+        "scaling": spec["scaling"], "vs_baseline": None, "dtype": "fp16 out; fp16/e4m3/int4 in",
         "data": "synthetic (seeded N(0,1) + outlier channels, quantize_reference)",
-        "config": {"workload": spec["name"], "parallelism": f"{threads} host threads"},
+        "config": static_config(args.workload, world),
         "cpu_baseline": {"value": round(value, 3), "unit": "GB/s", "cores": threads, "kind": kind,
                          "sample": sample},
         "e2e": {"value": round(value, 3), "unit": "GB/s", "h2d_bytes_per_step": 0,
@@ -1184,7 +1210,7 @@ def run_reference_flat(args, spec: dict, kind: str, threads: int) -> None:
         "ms_per_step": round(1e3 * total / args.steps, 3), "higher_is_better": True,
         "scaling": "weak", "vs_baseline": None, "dtype": "e4m3 in; fp16 out",
         "data": "synthetic (seeded N(0,1), quantize_reference)",
-        "config": {"workload": spec["name"], "parallelism": f"{threads} host threads"},
+        "config": static_config(args.workload, world),
         "cpu_baseline": {"value": round(value, 3), "unit": "GB/s", "cores": threads, "kind": kind,
                          "sample": f"the whole array ({n} values) per step"},
         "e2e": {"value": round(value, 3), "unit": "GB/s", "h2d_bytes_per_step": 0,
@@ -1223,7 +1249,7 @@ def run_reference_decode(args, spec: dict, kind: str, threads: int) -> None:
         "ms_per_step": round(1e3 * total / args.steps, 3), "higher_is_better": True,
         "scaling": "strong", "vs_baseline": None, "dtype": "fp16 in; e4m3/int4 out",
         "data": "synthetic (seeded N(0,1) tokens, formats .5/.5)",
-        "config": {"workload": spec["name"], "parallelism": f"{threads} host threads"},
+        "config": static_config(args.workload, world),
         "cpu_baseline": {"value": round(value, 3), "unit": "GB/s", "cores": threads, "kind": kind,
                          "sample": f"one full step: {n} appended tokens ({x.shape[0]} rows of {D})"},
         "e2e": {"value": round(value, 3), "unit": "GB/s", "h2d_bytes_per_step": 0,
@@ -1237,7 +1263,7 @@ def main() -> None:
     ap.add_argument("--steps", type=int, default=200)
     ap.add_argument("--warmup", type=int, default=5)
     ap.add_argument("--impl", choices=["hlkv", "reference"], default="hlkv")
-    ap.add_argument("--workload", choices=sorted(WORKLOADS), default="mixed")
+    ap.add_argument("--workload", choices=sorted(WORKLOADS), default="llama8b")
     ap.add_argument("--e2e-steps", type=int, default=10)
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--ctas", type=int, default=0,

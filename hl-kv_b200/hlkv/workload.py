@@ -207,3 +207,113 @@ def host_table(wl: KVWorkload) -> np.ndarray:
     """device_descriptor(id) for every id, uint32 [max_blocks, 4]."""
     n = wl.table.max_blocks()
     return np.array([wl.table.device_descriptor(i) for i in range(n)], dtype=np.uint32).reshape(n, 4)
+
+
+class UpdateStream:
+    """Seeded stream of descriptor updates for a resident cache, as a serving engine makes
+    them between sweeps: each batch takes `n` distinct blocks of the workload's sequences;
+    half get set_valid_tokens (1..T) while unsealed, the rest a format change to the next
+    age tier (seal, begin_format_change, a transcode job, commit).  prepare() is the host
+    half (table calls, then collect() into the device tables' pinned staging); launch()
+    queues the device half (job upload, hlkv_transcode, then the delta flush = kernel 3).
+
+    `sweep_bytes` tracks the algorithmic bytes of one gather over all the workload's
+    sequences as valid tokens and formats change.  The pools need `n` spare slots per
+    batch in every target format (a format change takes its new slot before the commit
+    frees the old one)."""
+
+    NEXT = {FP16: FP8_E4M3, FP8_E4M3: INT4, INT4: FP8_E4M3}  # FP16 -> E4M3 -> INT4 -> E4M3
+
+    def __init__(self, wl: KVWorkload, n: int, seed: int):
+        import torch
+        self.wl, self.n = wl, n
+        self.rng = np.random.default_rng(seed)
+        ids = []
+        for s in wl.seqs:
+            st, row = wl.table.sequence_block_ids(s)
+            if st != Status.OK:
+                raise RuntimeError("sequence_block_ids")
+            ids.extend(row)
+        self.ids = np.array(ids, dtype=np.uint32)
+        m = wl.table.max_blocks()
+        self.sealed = np.zeros(m, bool)
+        self.fmt = np.zeros(m, np.uint8)
+        self.vt = np.zeros(m, np.uint32)
+        for bid in self.ids:
+            info = wl.table.device_descriptor(int(bid))[1]
+            self.fmt[bid], self.vt[bid] = info & 0xF, (info >> 10) & 0x3FF
+        self.sweep_bytes = wl.algorithmic_bytes
+        self.jobs_host = torch.empty((n, 8), dtype=torch.int32).pin_memory()
+        self.jobs_dev = torch.empty((n, 8), dtype=torch.int32, device="cuda")
+        self.jobs_np = self.jobs_host.numpy().view(np.uint32)
+        self.uploaded = torch.cuda.Event()
+        self.first = True
+        self.n_jobs = 0
+        self.counts = {"valid_tokens": 0, "format_changes": 0}
+
+    def _bytes(self, f: int, vt: int) -> int:
+        w = self.wl
+        return block_bytes(f, w.T, w.H, w.D, vt)
+
+    def prepare(self) -> int:
+        """Host half of one batch; returns the bytes the batch moves on the device
+        (descriptor patches, transcode reads and writes)."""
+        w, t, rng = self.wl, self.wl.table, self.rng
+        if not self.first:
+            self.uploaded.synchronize()  # the previous upload has read jobs_host
+        self.first = False
+        picks = rng.choice(self.ids.size, size=self.n, replace=False)
+        kinds = rng.integers(0, 2, size=self.n)
+        out_bytes = 2 * 2 * w.T * w.H * w.D + 20  # FP16 written + descriptor per block
+        nj, moved, changed = 0, 0, []
+        for i, kind in zip(picks, kinds):
+            bid = int(self.ids[i])
+            h = t.handle_of(bid)
+            f, vt = int(self.fmt[bid]), int(self.vt[bid])
+            if kind == 0 and not self.sealed[bid]:
+                nvt = int(rng.integers(1, w.T + 1))
+                if t.set_valid_tokens(h, nvt) != Status.OK:
+                    raise RuntimeError("set_valid_tokens")
+                self.sweep_bytes += self._bytes(f, nvt) - self._bytes(f, vt)
+                self.vt[bid] = nvt
+                self.counts["valid_tokens"] += 1
+                moved += 32  # one descriptor patch read and written
+                continue
+            target = self.NEXT[f]
+            if not self.sealed[bid]:
+                if t.seal(h) != Status.OK:
+                    raise RuntimeError("seal")
+                self.sealed[bid] = True
+            st, fc = t.begin_format_change(h, target)
+            if st != Status.OK:
+                raise RuntimeError(f"begin_format_change: {st}")
+            self.jobs_np[nj] = (fc[0], fc[1], fc[2], fc[3], vt, 0, 0, 0)
+            nj += 1
+            changed.append(h)
+            # source codes + params of the valid rows read, all destination rows written
+            moved += (self._bytes(f, vt) - out_bytes) + (self._bytes(target, w.T) - out_bytes) + 64
+            self.sweep_bytes += self._bytes(target, vt) - self._bytes(f, vt)
+            self.fmt[bid] = target
+        # The commits only change host state; the device sees them through the delta,
+        # which launch() queues after the transcode.
+        for h in changed:
+            if t.commit_format_change(h, 0, 0) != Status.OK:
+                raise RuntimeError("commit_format_change")
+        self.counts["format_changes"] += nj
+        self.n_jobs = nj
+        w.dt.collect(t)
+        return moved
+
+    def launch(self, stream, err) -> int:
+        """Device half, in stream order: job upload, transcode, delta flush (kernel 3).
+        Returns the number of kernels queued."""
+        from . import transcode
+        w, nj = self.wl, self.n_jobs
+        launches = 0
+        if nj:
+            self.jobs_dev[:nj].copy_(self.jobs_host[:nj], non_blocking=True)
+            self.uploaded.record(stream)
+            check(transcode(w.hlkv_pools(), w.layout, self.jobs_dev[:nj], err, stream=stream), "transcode")
+            launches += 1
+        w.dt.flush(stream)
+        return launches + 1

@@ -33,9 +33,14 @@ def _block_bytes(f: int, T: int, H: int, D: int) -> int:
     return packed_bytes(f, elems) + params + 2 * elems + 20
 
 
-def build_cpu_workload(kind: str, nseq: int, blocks: int, probs, seed: int, T: int = 16,
-                       H: int = 8, D: int = 128, outliers: int = 4, scale: float = 20.0) -> dict:
-    fm = _formats(nseq, blocks, probs, seed)
+def build_cpu_workload(kind: str, nseq: int = 0, blocks: int = 0, probs=None, seed: int = 0,
+                       T: int = 16, H: int = 8, D: int = 128, outliers: int = 4, scale: float = 20.0,
+                       formats: list | None = None) -> dict:
+    """`formats` (one uint8 array of block formats per sequence) replaces the seeded draw of
+    nseq x blocks formats from `probs`."""
+    fm = [np.asarray(r, dtype=np.uint8) for r in formats] if formats is not None else \
+        _formats(nseq, blocks, probs, seed)
+    nseq = len(fm)
     nbytes = sum(_block_bytes(int(f), T, H, D) for row in fm for f in row)
     threads = os.cpu_count() or 1
     if kind == "reference":
