@@ -1,14 +1,19 @@
 // HeteroBlockTable (see include/hl_allocator/hetero_block_table.hpp).
 //
-// The observable contract follows the reference's
-// project1_allocator/src/hetero_block_table.cpp: LIFO free lists primed so the
-// first pops return 0, 1, 2, ...; the check order of every call (hence which
-// Status wins when several apply); the first delta carrying every record; the
-// descriptor dirty list reported in marking order; and device_descriptor()'s
-// non-executable form (format 15, slot 0xFFFFFFFF, block_id kept, the other
-// info bits and scale_ref of the host record kept).  oracle/table_trace.cpp
-// replays the same seeded call stream on both implementations and compares
-// every word.
+// What is observable follows the reference (project1_allocator/src/hetero_block_table.cpp)
+// and is pinned word for word by oracle/table_trace.cpp against the reference library:
+// block ids, slots and sequence ids are reused last-freed-first and are first handed out
+// as 0, 1, 2, ...; each call rejects with the same status when several problems apply;
+// the first delta carries every descriptor in id order, later ones the changed
+// descriptors in first-change order; device_descriptor() of a free or non-resident block
+// is the record with format 15 and slot 0xFFFFFFFF.
+//
+// Storage is this library's own.  Every free list is a stack threaded through the free
+// objects themselves (a free block record's `reserved` word, a slot's entry of its pool's
+// `below` array, a released sequence's segment offset), sized once at construction, so no
+// release path allocates.  Descriptor changes go through an epoch-stamped ChangeQueue,
+// like the arena's.  Each block operation is one check-then-edit on its record
+// (edit_block below), with the checks in the order the reference applies them.
 #include "hl_allocator/hetero_block_table.hpp"
 #include "hl_allocator/snapshot_io.hpp"
 
@@ -16,98 +21,134 @@
 #include <cstring>
 #include <limits>
 #include <stdexcept>
+#include <utility>
 
 namespace hl::alloc {
 namespace {
 
 constexpr std::uint32_t kIdLimit = 0xFFFF'FFFEu;  // 0xFFFFFFFF is the invalid id
 
-constexpr std::uint32_t raw(FormatId f) noexcept { return static_cast<std::uint32_t>(f); }
-constexpr bool scale_mode_ok(ScaleMode m) noexcept { return static_cast<std::uint32_t>(m) <= 3u; }
-constexpr bool residency_ok(Residency r) noexcept { return static_cast<std::uint32_t>(r) <= 2u; }
-
-// A LIFO stack whose pops yield 0, 1, ..., count-1 first.
-void prime_lifo(std::vector<std::uint32_t>& stack, std::uint32_t count) {
-  stack.clear();
-  stack.reserve(count);
-  for (std::uint32_t v = count; v-- > 0;) stack.push_back(v);
-}
+constexpr std::uint32_t fmt_index(FormatId f) noexcept { return static_cast<std::uint32_t>(f); }
+constexpr bool valid_scale_mode(ScaleMode m) noexcept { return static_cast<std::uint32_t>(m) <= 3u; }
+constexpr bool valid_residency(Residency r) noexcept { return static_cast<std::uint32_t>(r) <= 2u; }
 
 ValidationReport corrupt(std::string what) { return {Status::kCorrupt, std::move(what)}; }
+
+// Runs `edit` on the record of a live block, or returns the status that rejected its handle.
+template <typename Edit>
+Status edit_block(Status found, BlockDescriptor* d, Edit&& edit) {
+  return found == Status::kOk ? edit(*d) : found;
+}
 
 }  // namespace
 
 Status HeteroBlockTable::validate_config(const TableConfig& config) noexcept {
   if (config.max_blocks == 0 || config.max_blocks > kIdLimit) return Status::kInvalidArgument;
-  if (config.block_tokens == 0 || config.block_tokens > kMaxBlockTokens) {
-    return Status::kInvalidArgument;
-  }
+  if (config.block_tokens == 0 || config.block_tokens > kMaxBlockTokens) return Status::kInvalidArgument;
   if (config.pools.empty()) return Status::kInvalidArgument;
-  std::array<bool, kMaxFormats> used{};
-  for (const PoolConfig& p : config.pools) {
-    if (raw(p.format) >= kMaxFormats) return Status::kUnknownFormat;
-    if (used[raw(p.format)]) return Status::kInvalidArgument;
-    used[raw(p.format)] = true;
-    if (p.slot_bytes == 0 || p.num_slots == 0 || p.num_slots > kIdLimit) {
-      return Status::kInvalidArgument;
-    }
+  std::uint32_t seen = 0;  // one bit per format (kMaxFormats <= 32)
+  static_assert(kMaxFormats <= 32);
+  for (const PoolConfig& pc : config.pools) {
+    const std::uint32_t f = fmt_index(pc.format);
+    if (f >= kMaxFormats) return Status::kUnknownFormat;
+    if ((seen >> f) & 1u) return Status::kInvalidArgument;
+    seen |= 1u << f;
+    if (pc.slot_bytes == 0 || pc.num_slots == 0 || pc.num_slots > kIdLimit) return Status::kInvalidArgument;
   }
   return Status::kOk;
 }
 
 HeteroBlockTable::HeteroBlockTable(const TableConfig& config) : block_tokens_(config.block_tokens) {
   if (const Status s = validate_config(config); s != Status::kOk) {
-    throw std::invalid_argument(std::string("HeteroBlockTable: invalid TableConfig: ") +
-                                to_string(s));
+    throw std::invalid_argument(std::string("HeteroBlockTable: invalid TableConfig: ") + to_string(s));
   }
-  records_.resize(config.max_blocks);
-  for (std::uint32_t id = 0; id < config.max_blocks; ++id) reset_record(id, 0);
-  prime_lifo(free_ids_, config.max_blocks);
-  // The device table starts as garbage: the first delta must carry every record.
-  is_dirty_.assign(config.max_blocks, 1);
-  dirty_ids_.reserve(config.max_blocks);
-  for (std::uint32_t id = 0; id < config.max_blocks; ++id) dirty_ids_.push_back(id);
+  const std::uint32_t n = config.max_blocks;
+  blocks_.resize(n);
+  // Every id free, chained 0 -> 1 -> ... so that allocation hands them out in id order.
+  for (std::uint32_t id = n; id-- > 0;) {
+    init_free_record(id, 0);
+    blocks_[id].reserved = free_block_top_;
+    free_block_top_ = id;
+  }
   for (const PoolConfig& pc : config.pools) {
-    SlotPool& p = pools_[raw(pc.format)];
-    p.present = true;
-    p.slot_bytes = pc.slot_bytes;
-    p.capacity = pc.num_slots;
-    prime_lifo(p.lifo, pc.num_slots);
+    SlotStack& st = slots_[fmt_index(pc.format)];
+    st.present = true;
+    st.slot_bytes = pc.slot_bytes;
+    st.capacity = pc.num_slots;
+    st.below.resize(pc.num_slots);
+    for (std::uint32_t s = pc.num_slots; s-- > 0;) push(st, s);
   }
+  // The device copy starts undefined: the first delta carries every descriptor.
+  changed_blocks_.grow(n);
+  for (std::uint32_t id = 0; id < n; ++id) changed_blocks_.mark(id);
 }
 
 // ---- helpers ---------------------------------------------------------------------------
 
-HeteroBlockTable::SlotPool* HeteroBlockTable::pool(FormatId f) noexcept {
-  return raw(f) < kMaxFormats && pools_[raw(f)].present ? &pools_[raw(f)] : nullptr;
+HeteroBlockTable::SlotStack* HeteroBlockTable::stack(FormatId f) noexcept {
+  const std::uint32_t i = fmt_index(f);
+  return i < kMaxFormats && slots_[i].present ? &slots_[i] : nullptr;
 }
-const HeteroBlockTable::SlotPool* HeteroBlockTable::pool(FormatId f) const noexcept {
-  return raw(f) < kMaxFormats && pools_[raw(f)].present ? &pools_[raw(f)] : nullptr;
-}
-
-Status HeteroBlockTable::verify(BlockHandle h) const noexcept {
-  if (h.id >= records_.size()) return Status::kInvalidHandle;
-  const BlockDescriptor& d = records_[h.id];
-  return d.generation == h.generation && d.state() != BlockState::kFree ? Status::kOk
-                                                                         : Status::kStaleHandle;
+const HeteroBlockTable::SlotStack* HeteroBlockTable::stack(FormatId f) const noexcept {
+  const std::uint32_t i = fmt_index(f);
+  return i < kMaxFormats && slots_[i].present ? &slots_[i] : nullptr;
 }
 
-Status HeteroBlockTable::verify(SequenceHandle s) const noexcept {
-  if (s.id >= seqs_.size()) return Status::kInvalidHandle;
-  const Seq& q = seqs_[s.id];
-  return q.live && q.generation == s.generation ? Status::kOk : Status::kStaleHandle;
+bool HeteroBlockTable::pop(SlotStack& st, std::uint32_t& slot) noexcept {
+  if (st.top == kEnd) return false;
+  slot = st.top;
+  st.top = st.below[slot];
+  st.depth -= 1;
+  return true;
 }
 
-Status HeteroBlockTable::verify(const AllocRequest& r) const noexcept {
-  if (pool(r.format) == nullptr) return Status::kUnknownFormat;
-  if (r.valid_tokens > block_tokens_ || r.layout > kMaxLayoutId || !scale_mode_ok(r.scale_mode)) {
-    return Status::kInvalidArgument;
-  }
+void HeteroBlockTable::push(SlotStack& st, std::uint32_t slot) noexcept {
+  st.below[slot] = st.top;
+  st.top = slot;
+  st.depth += 1;
+}
+
+Status HeteroBlockTable::find(BlockHandle h, BlockDescriptor*& out) noexcept {
+  const BlockDescriptor* c = nullptr;
+  const Status s = std::as_const(*this).find(h, c);
+  out = const_cast<BlockDescriptor*>(c);
+  return s;
+}
+
+Status HeteroBlockTable::find(BlockHandle h, const BlockDescriptor*& out) const noexcept {
+  if (h.id >= blocks_.size()) return Status::kInvalidHandle;
+  const BlockDescriptor& d = blocks_[h.id];
+  if (d.state() == BlockState::kFree || d.generation != h.generation) return Status::kStaleHandle;
+  out = &d;
   return Status::kOk;
 }
 
-void HeteroBlockTable::reset_record(std::uint32_t id, std::uint32_t generation) noexcept {
-  BlockDescriptor d{};
+Status HeteroBlockTable::find(SequenceHandle h, SeqRecord*& out) noexcept {
+  const SeqRecord* c = nullptr;
+  const Status s = std::as_const(*this).find(h, c);
+  out = const_cast<SeqRecord*>(c);
+  return s;
+}
+
+Status HeteroBlockTable::find(SequenceHandle h, const SeqRecord*& out) const noexcept {
+  if (h.id >= seq_records_.size()) return Status::kInvalidHandle;
+  const SeqRecord& q = seq_records_[h.id];
+  if (!q.live || q.generation != h.generation) return Status::kStaleHandle;
+  out = &q;
+  return Status::kOk;
+}
+
+Status HeteroBlockTable::admissible(const AllocRequest& r) const noexcept {
+  if (stack(r.format) == nullptr) return Status::kUnknownFormat;
+  const bool ok = r.valid_tokens <= block_tokens_ && r.layout <= kMaxLayoutId && valid_scale_mode(r.scale_mode);
+  return ok ? Status::kOk : Status::kInvalidArgument;
+}
+
+// A free record: not executable (format 15, no slot), its id kept, everything else zero.
+// The `reserved` word is set by whoever chains the record into the free ids.
+void HeteroBlockTable::init_free_record(std::uint32_t id, std::uint32_t generation) noexcept {
+  BlockDescriptor& d = blocks_[id];
+  d = BlockDescriptor{};
   d.exec.slot = kNoSlot;
   d.exec.block_id = id;
   d.exec.set_format(kInvalidFormat);
@@ -115,34 +156,34 @@ void HeteroBlockTable::reset_record(std::uint32_t id, std::uint32_t generation) 
   d.set_state(BlockState::kFree);
   d.set_pending_format(kInvalidFormat);
   d.pending_slot = kNoSlot;
-  records_[id] = d;
 }
 
-void HeteroBlockTable::touch(std::uint32_t id) noexcept {
-  if (is_dirty_[id]) return;
-  is_dirty_[id] = 1;
-  dirty_ids_.push_back(id);  // capacity == max_blocks, never reallocates
-}
-
-void HeteroBlockTable::retire(std::uint32_t id) noexcept {
-  const BlockDescriptor d = records_[id];
-  // The stacks were reserved to their pool size, so these pushes never allocate.
-  if (SlotPool* p = pool(d.exec.format()); p != nullptr && d.exec.slot != kNoSlot) {
-    p->lifo.push_back(d.exec.slot);
+// The last reference is gone: both slots (the current one and, if a change were in flight,
+// the pending one) go back to their pools, the record becomes free under the next
+// generation and its id goes on top of the free ids.
+void HeteroBlockTable::free_block(std::uint32_t id) noexcept {
+  const BlockDescriptor old = blocks_[id];
+  if (SlotStack* st = stack(old.exec.format()); st != nullptr && old.exec.slot != kNoSlot) {
+    push(*st, old.exec.slot);
   }
-  if (SlotPool* p = pool(d.pending_format()); p != nullptr && d.pending_slot != kNoSlot) {
-    p->lifo.push_back(d.pending_slot);
+  if (SlotStack* st = stack(old.pending_format()); st != nullptr && old.pending_slot != kNoSlot) {
+    push(*st, old.pending_slot);
   }
-  reset_record(id, d.generation + 1u);  // the generation wraps at 2^32 by design
-  free_ids_.push_back(id);
+  init_free_record(id, old.generation + 1u);  // generations wrap at 2^32 by design
+  blocks_[id].reserved = free_block_top_;
+  free_block_top_ = id;
   in_use_ -= 1;
-  touch(id);
+  changed_blocks_.mark(id);
 }
 
-void HeteroBlockTable::drop_reference(std::uint32_t id) noexcept {
-  BlockDescriptor& d = records_[id];
+// Drops one reference; the block is freed exactly when its count goes from 1 to 0.  (A
+// record that misuse has already freed -- release() of a block a sequence still lists --
+// only has its count field decremented when that sequence later lets go of it, as the
+// reference does; it is never freed twice.)
+void HeteroBlockTable::unreference(std::uint32_t id) noexcept {
+  BlockDescriptor& d = blocks_[id];
   if (d.refcount() == 1) {
-    retire(id);
+    free_block(id);
   } else {
     d.set_refcount(d.refcount() - 1);
   }
@@ -151,313 +192,315 @@ void HeteroBlockTable::drop_reference(std::uint32_t id) noexcept {
 // ---- blocks ------------------------------------------------------------------------------
 
 Result<BlockHandle> HeteroBlockTable::allocate(const AllocRequest& request) {
-  if (const Status s = verify(request); s != Status::kOk) return s;
-  if (free_ids_.empty()) return Status::kOutOfBlocks;
-  SlotPool& p = *pool(request.format);
-  if (p.lifo.empty()) return Status::kOutOfSlots;
+  if (const Status s = admissible(request); s != Status::kOk) return s;
+  if (free_block_top_ == kEnd) return Status::kOutOfBlocks;
+  SlotStack& st = *stack(request.format);
+  std::uint32_t slot = 0;
+  if (!pop(st, slot)) return Status::kOutOfSlots;
+  const std::uint32_t id = free_block_top_;
+  BlockDescriptor& d = blocks_[id];
+  free_block_top_ = d.reserved;
 
-  const std::uint32_t id = free_ids_.back();
-  free_ids_.pop_back();
-  const std::uint32_t slot = p.lifo.back();
-  p.lifo.pop_back();
-
-  BlockDescriptor& d = records_[id];
-  d.exec.slot = slot;
-  d.exec.info = BlockExecDescriptor::pack_info(request.format, request.scale_mode, request.layout,
-                                               request.valid_tokens);
-  d.exec.scale_ref = request.scale_ref;
-  d.control = 0;
+  const std::uint32_t generation = d.generation;
+  d = BlockDescriptor{};
+  d.generation = generation;
+  d.exec = BlockExecDescriptor{slot,
+                               BlockExecDescriptor::pack_info(request.format, request.scale_mode,
+                                                              request.layout, request.valid_tokens),
+                               request.scale_ref, id};
   d.set_state(BlockState::kOpen);
   d.set_residency(Residency::kDevice);
   d.set_pending_format(kInvalidFormat);
   d.set_refcount(1);
   d.pending_slot = kNoSlot;
-  d.reserved = 0;
   in_use_ += 1;
-  touch(id);
-  return BlockHandle{id, d.generation};
+  changed_blocks_.mark(id);
+  return BlockHandle{id, generation};
 }
 
 Status HeteroBlockTable::retain(BlockHandle handle) {
-  if (const Status s = verify(handle); s != Status::kOk) return s;
-  BlockDescriptor& d = records_[handle.id];
-  if (d.refcount() >= kMaxRefcount) return Status::kRefcountOverflow;
-  d.set_refcount(d.refcount() + 1);
-  return Status::kOk;
+  BlockDescriptor* d = nullptr;
+  const Status found = find(handle, d);
+  return edit_block(found, d, [&](BlockDescriptor& b) {
+    if (b.refcount() >= kMaxRefcount) return Status::kRefcountOverflow;
+    b.set_refcount(b.refcount() + 1);
+    return Status::kOk;
+  });
 }
 
 Status HeteroBlockTable::release(BlockHandle handle) {
-  if (const Status s = verify(handle); s != Status::kOk) return s;
-  const BlockDescriptor& d = records_[handle.id];
-  // The last reference of a block being transcoded must wait for commit/abort:
-  // a conversion kernel may still read the old slot.
-  if (d.refcount() == 1 && d.state() == BlockState::kTranscoding) return Status::kInvalidState;
-  drop_reference(handle.id);
-  return Status::kOk;
+  BlockDescriptor* d = nullptr;
+  const Status found = find(handle, d);
+  return edit_block(found, d, [&](BlockDescriptor& b) {
+    // A block in a format change keeps its last reference until the change commits or
+    // aborts: the transcoding kernel may still read the old slot.
+    if (b.refcount() == 1 && b.state() == BlockState::kTranscoding) return Status::kInvalidState;
+    unreference(handle.id);
+    return Status::kOk;
+  });
 }
 
 Status HeteroBlockTable::set_valid_tokens(BlockHandle handle, std::uint32_t valid_tokens) {
-  if (const Status s = verify(handle); s != Status::kOk) return s;
-  BlockDescriptor& d = records_[handle.id];
-  if (d.state() != BlockState::kOpen) return Status::kInvalidState;
-  if (valid_tokens > block_tokens_) return Status::kInvalidArgument;
-  d.exec.set_valid_tokens(valid_tokens);
-  touch(handle.id);
-  return Status::kOk;
+  BlockDescriptor* d = nullptr;
+  const Status found = find(handle, d);
+  return edit_block(found, d, [&](BlockDescriptor& b) {
+    if (b.state() != BlockState::kOpen) return Status::kInvalidState;
+    if (valid_tokens > block_tokens_) return Status::kInvalidArgument;
+    b.exec.set_valid_tokens(valid_tokens);
+    changed_blocks_.mark(handle.id);
+    return Status::kOk;
+  });
 }
 
 Status HeteroBlockTable::seal(BlockHandle handle) {
-  if (const Status s = verify(handle); s != Status::kOk) return s;
-  BlockDescriptor& d = records_[handle.id];
-  if (d.state() != BlockState::kOpen) return Status::kInvalidState;
-  d.set_state(BlockState::kSealed);  // host-only: no device change
-  return Status::kOk;
+  BlockDescriptor* d = nullptr;
+  const Status found = find(handle, d);
+  return edit_block(found, d, [&](BlockDescriptor& b) {
+    if (b.state() != BlockState::kOpen) return Status::kInvalidState;
+    b.set_state(BlockState::kSealed);  // host bookkeeping only: the device record is unchanged
+    return Status::kOk;
+  });
 }
 
 Status HeteroBlockTable::set_residency(BlockHandle handle, Residency residency) {
-  if (const Status s = verify(handle); s != Status::kOk) return s;
-  if (!residency_ok(residency)) return Status::kInvalidArgument;
-  BlockDescriptor& d = records_[handle.id];
-  if (d.state() == BlockState::kTranscoding) return Status::kInvalidState;
-  d.set_residency(residency);
-  touch(handle.id);  // the device record becomes executable or not
-  return Status::kOk;
+  BlockDescriptor* d = nullptr;
+  const Status found = find(handle, d);
+  return edit_block(found, d, [&](BlockDescriptor& b) {
+    if (!valid_residency(residency)) return Status::kInvalidArgument;
+    if (b.state() == BlockState::kTranscoding) return Status::kInvalidState;
+    b.set_residency(residency);
+    changed_blocks_.mark(handle.id);  // executable on the device or not
+    return Status::kOk;
+  });
 }
 
 Status HeteroBlockTable::set_scale(BlockHandle handle, ScaleMode mode, std::uint32_t scale_ref) {
-  if (const Status s = verify(handle); s != Status::kOk) return s;
-  if (!scale_mode_ok(mode)) return Status::kInvalidArgument;
-  BlockDescriptor& d = records_[handle.id];
-  if (d.state() == BlockState::kTranscoding) return Status::kInvalidState;
-  d.exec.set_scale_mode(mode);
-  d.exec.scale_ref = scale_ref;
-  touch(handle.id);
-  return Status::kOk;
+  BlockDescriptor* d = nullptr;
+  const Status found = find(handle, d);
+  return edit_block(found, d, [&](BlockDescriptor& b) {
+    if (!valid_scale_mode(mode)) return Status::kInvalidArgument;
+    if (b.state() == BlockState::kTranscoding) return Status::kInvalidState;
+    b.exec.set_scale_mode(mode);
+    b.exec.scale_ref = scale_ref;
+    changed_blocks_.mark(handle.id);
+    return Status::kOk;
+  });
 }
 
 Result<FormatChange> HeteroBlockTable::begin_format_change(BlockHandle handle, FormatId target) {
-  if (const Status s = verify(handle); s != Status::kOk) return s;
-  BlockDescriptor& d = records_[handle.id];
-  if (d.state() != BlockState::kSealed) return Status::kInvalidState;
-  if (d.residency() != Residency::kDevice) return Status::kNotDeviceResident;
-  SlotPool* to = pool(target);
+  BlockDescriptor* d = nullptr;
+  if (const Status s = find(handle, d); s != Status::kOk) return s;
+  if (d->state() != BlockState::kSealed) return Status::kInvalidState;
+  if (d->residency() != Residency::kDevice) return Status::kNotDeviceResident;
+  SlotStack* to = stack(target);
   if (to == nullptr) return Status::kUnknownFormat;
-  if (target == d.exec.format()) return Status::kInvalidArgument;
-  if (to->lifo.empty()) return Status::kOutOfSlots;
-  const std::uint32_t to_slot = to->lifo.back();
-  to->lifo.pop_back();
-  d.pending_slot = to_slot;
-  d.set_pending_format(target);
-  d.set_state(BlockState::kTranscoding);
-  return FormatChange{d.exec.format(), d.exec.slot, target, to_slot};
+  if (target == d->exec.format()) return Status::kInvalidArgument;
+  std::uint32_t to_slot = 0;
+  if (!pop(*to, to_slot)) return Status::kOutOfSlots;
+  // Readers still see the old format and slot (no descriptor change) until the commit.
+  d->pending_slot = to_slot;
+  d->set_pending_format(target);
+  d->set_state(BlockState::kTranscoding);
+  return FormatChange{d->exec.format(), d->exec.slot, target, to_slot};
 }
 
-Status HeteroBlockTable::commit_format_change(BlockHandle handle, ScaleMode mode,
-                                              std::uint32_t scale_ref) {
-  if (const Status s = verify(handle); s != Status::kOk) return s;
-  if (!scale_mode_ok(mode)) return Status::kInvalidArgument;
-  BlockDescriptor& d = records_[handle.id];
-  if (d.state() != BlockState::kTranscoding) return Status::kInvalidState;
-  pool(d.exec.format())->lifo.push_back(d.exec.slot);
-  d.exec.slot = d.pending_slot;
-  d.exec.set_format(d.pending_format());
-  d.exec.set_scale_mode(mode);
-  d.exec.scale_ref = scale_ref;
-  d.pending_slot = kNoSlot;
-  d.set_pending_format(kInvalidFormat);
-  d.set_state(BlockState::kSealed);
-  committed_changes_ += 1;
-  touch(handle.id);
-  return Status::kOk;
+Status HeteroBlockTable::commit_format_change(BlockHandle handle, ScaleMode mode, std::uint32_t scale_ref) {
+  BlockDescriptor* d = nullptr;
+  const Status found = find(handle, d);
+  return edit_block(found, d, [&](BlockDescriptor& b) {
+    if (!valid_scale_mode(mode)) return Status::kInvalidArgument;
+    if (b.state() != BlockState::kTranscoding) return Status::kInvalidState;
+    push(*stack(b.exec.format()), b.exec.slot);  // the old payload's slot
+    b.exec.slot = b.pending_slot;
+    b.exec.set_format(b.pending_format());
+    b.exec.set_scale_mode(mode);
+    b.exec.scale_ref = scale_ref;
+    b.pending_slot = kNoSlot;
+    b.set_pending_format(kInvalidFormat);
+    b.set_state(BlockState::kSealed);
+    committed_changes_ += 1;
+    changed_blocks_.mark(handle.id);
+    return Status::kOk;
+  });
 }
 
 Status HeteroBlockTable::abort_format_change(BlockHandle handle) {
-  if (const Status s = verify(handle); s != Status::kOk) return s;
-  BlockDescriptor& d = records_[handle.id];
-  if (d.state() != BlockState::kTranscoding) return Status::kInvalidState;
-  pool(d.pending_format())->lifo.push_back(d.pending_slot);
-  d.pending_slot = kNoSlot;
-  d.set_pending_format(kInvalidFormat);
-  d.set_state(BlockState::kSealed);
-  return Status::kOk;
+  BlockDescriptor* d = nullptr;
+  const Status found = find(handle, d);
+  return edit_block(found, d, [&](BlockDescriptor& b) {
+    if (b.state() != BlockState::kTranscoding) return Status::kInvalidState;
+    push(*stack(b.pending_format()), b.pending_slot);
+    b.pending_slot = kNoSlot;
+    b.set_pending_format(kInvalidFormat);
+    b.set_state(BlockState::kSealed);
+    return Status::kOk;
+  });
 }
 
 Result<BlockDescriptor> HeteroBlockTable::lookup(BlockHandle handle) const {
-  if (const Status s = verify(handle); s != Status::kOk) return s;
-  return records_[handle.id];
+  const BlockDescriptor* d = nullptr;
+  if (const Status s = find(handle, d); s != Status::kOk) return s;
+  return *d;
 }
 
 Status HeteroBlockTable::lookup_batch(std::span<const BlockHandle> handles,
                                       std::span<BlockExecDescriptor> out) const {
   if (out.size() < handles.size()) return Status::kInvalidArgument;
   for (std::size_t k = 0; k < handles.size(); ++k) {
-    if (const Status s = verify(handles[k]); s != Status::kOk) return s;
-    const BlockDescriptor& d = records_[handles[k].id];
-    if (d.residency() != Residency::kDevice) return Status::kNotDeviceResident;
-    out[k] = d.exec;
+    const BlockDescriptor* d = nullptr;
+    if (const Status s = find(handles[k], d); s != Status::kOk) return s;
+    if (d->residency() != Residency::kDevice) return Status::kNotDeviceResident;
+    out[k] = d->exec;
   }
   return Status::kOk;
 }
 
 BlockHandle HeteroBlockTable::handle_of(std::uint32_t block_id) const noexcept {
-  if (block_id >= records_.size() || records_[block_id].state() == BlockState::kFree) {
-    return kInvalidBlock;
-  }
-  return BlockHandle{block_id, records_[block_id].generation};
+  const bool live = block_id < blocks_.size() && blocks_[block_id].state() != BlockState::kFree;
+  return live ? BlockHandle{block_id, blocks_[block_id].generation} : kInvalidBlock;
 }
 
 // ---- sequences ---------------------------------------------------------------------------
 
 Result<SequenceHandle> HeteroBlockTable::create_sequence() {
-  std::uint32_t id;
-  if (!free_seqs_.empty()) {
-    id = free_seqs_.back();
-    free_seqs_.pop_back();
+  std::uint32_t id = free_seq_top_;
+  if (id != kEnd) {
+    free_seq_top_ = seq_records_[id].seg.offset;
   } else {
-    if (seqs_.size() >= kIdLimit) return Status::kCapacityExceeded;
-    // release_sequence() must never allocate: keep room to park every sequence.
-    if (free_seqs_.capacity() < seqs_.size() + 1) {
-      free_seqs_.reserve(std::max<std::size_t>(8, 2 * (seqs_.size() + 1)));
-    }
-    id = static_cast<std::uint32_t>(seqs_.size());
-    seqs_.emplace_back();
+    if (seq_records_.size() >= kIdLimit) return Status::kCapacityExceeded;
+    id = static_cast<std::uint32_t>(seq_records_.size());
+    seq_records_.emplace_back();  // may throw; nothing has changed yet
   }
-  Seq& q = seqs_[id];
+  SeqRecord& q = seq_records_[id];
+  q.seg = IdArena::Segment{};  // storage comes with the first block
   q.live = true;
-  q.seg = IdArena::Segment{};  // storage comes with the first append
   return SequenceHandle{id, q.generation};
 }
 
 Result<BlockHandle> HeteroBlockTable::append_block(SequenceHandle seq, const AllocRequest& request) {
-  if (const Status s = verify(seq); s != Status::kOk) return s;
-  IdArena::Segment& seg = seqs_[seq.id].seg;
-  // Room first (may move the segment or throw); nothing can fail after allocate().
-  if (const Status s = arena_.reserve(seg, seg.length + 1); s != Status::kOk) return s;
-  Result<BlockHandle> block = allocate(request);
-  if (!block.ok()) return block.status();
-  arena_.push_back(seg, block.value().id);
-  return block;
+  SeqRecord* q = nullptr;
+  if (const Status s = find(seq, q); s != Status::kOk) return s;
+  // The arena room comes first: it may move the segment (or throw) while nothing else has
+  // changed, and once the block is allocated nothing can fail.
+  if (const Status s = arena_.reserve(q->seg, q->seg.length + 1); s != Status::kOk) return s;
+  const Result<BlockHandle> b = allocate(request);
+  if (b.ok()) arena_.push_back(q->seg, b.value().id);
+  return b;
 }
 
 Status HeteroBlockTable::append_shared_block(SequenceHandle seq, BlockHandle block) {
-  if (const Status s = verify(seq); s != Status::kOk) return s;
-  if (const Status s = verify(block); s != Status::kOk) return s;
-  // Open blocks still receive appends; only immutable ones may be shared.
-  if (records_[block.id].state() == BlockState::kOpen) return Status::kInvalidState;
-  IdArena::Segment& seg = seqs_[seq.id].seg;
-  if (const Status s = arena_.reserve(seg, seg.length + 1); s != Status::kOk) return s;
+  SeqRecord* q = nullptr;
+  if (const Status s = find(seq, q); s != Status::kOk) return s;
+  BlockDescriptor* d = nullptr;
+  if (const Status s = find(block, d); s != Status::kOk) return s;
+  if (d->state() == BlockState::kOpen) return Status::kInvalidState;  // still being appended to
+  if (const Status s = arena_.reserve(q->seg, q->seg.length + 1); s != Status::kOk) return s;
   if (const Status s = retain(block); s != Status::kOk) return s;
-  arena_.push_back(seg, block.id);
+  arena_.push_back(q->seg, block.id);
   return Status::kOk;
 }
 
 Status HeteroBlockTable::release_sequence(SequenceHandle seq) {
-  if (const Status s = verify(seq); s != Status::kOk) return s;
-  Seq& q = seqs_[seq.id];
-  const std::span<const std::uint32_t> ids = arena_.view(q.seg);
-  // All-or-nothing: check before changing anything.
-  const bool busy = std::any_of(ids.begin(), ids.end(), [&](std::uint32_t id) {
-    return records_[id].state() == BlockState::kTranscoding;
-  });
-  if (busy) return Status::kInvalidState;
-  for (const std::uint32_t id : ids) drop_reference(id);
-  arena_.release(q.seg);
-  q.live = false;
-  q.generation += 1;
-  free_seqs_.push_back(seq.id);
+  SeqRecord* q = nullptr;
+  if (const Status s = find(seq, q); s != Status::kOk) return s;
+  const std::span<const std::uint32_t> members = arena_.view(q->seg);
+  // All or nothing: a member in a format change blocks the whole release.
+  for (const std::uint32_t id : members) {
+    if (blocks_[id].state() == BlockState::kTranscoding) return Status::kInvalidState;
+  }
+  for (const std::uint32_t id : members) unreference(id);
+  arena_.release(q->seg);
+  q->live = false;
+  q->generation += 1;
+  q->seg.offset = free_seq_top_;  // chain the id into the free sequence ids
+  free_seq_top_ = seq.id;
   return Status::kOk;
 }
 
-Status HeteroBlockTable::append_tokens(std::span<const SequenceHandle> seqs,
-                                       std::span<const FormatId> new_formats, std::uint32_t layout,
-                                       std::span<TokenTarget> out, std::size_t& n_done) {
+Status HeteroBlockTable::append_tokens(std::span<const SequenceHandle> seqs, std::span<const FormatId> new_formats,
+                                       std::uint32_t layout, std::span<TokenTarget> out, std::size_t& n_done) {
   n_done = 0;
   const std::size_t n = seqs.size();
   if (new_formats.size() < n || out.size() < n) return Status::kInvalidArgument;
-  // Each sequence is a chain of dependent random reads (its Seq record, the arena entry of
-  // its tail, the tail's record and dirty flag).  Prefetches for sequences further ahead, one
-  // link of the chain per distance, keep several chains' misses in flight at once.
-  constexpr std::size_t kAheadSeq = 24, kAheadTail = 16, kAheadRecord = 8;
-  auto seq_at = [&](std::size_t k) -> const Seq* {
-    const std::uint32_t id = seqs[k].id;
-    return id < seqs_.size() ? &seqs_[id] : nullptr;
-  };
-  auto tail_of = [&](const Seq* q) -> const std::uint32_t* {
-    return q != nullptr && q->seg.capacity > 0 && q->seg.length > 0
-               ? arena_.view(q->seg).data() + (q->seg.length - 1)
-               : nullptr;
+  // Sequence i's work is a chain of dependent random reads: its record, the arena entry of
+  // its last block, that block's record and change stamp.  Touching the links of the
+  // sequences a few places ahead (each link at its own distance) keeps several chains'
+  // cache misses in flight.
+  auto tail_entry = [&](std::size_t k) -> const std::uint32_t* {
+    const std::uint32_t sid = seqs[k].id;
+    if (sid >= seq_records_.size()) return nullptr;
+    const IdArena::Segment& g = seq_records_[sid].seg;
+    return g.capacity != 0 && g.length != 0 ? arena_.view(g).data() + (g.length - 1) : nullptr;
   };
   for (std::size_t i = 0; i < n; ++i) {
-    if (i + kAheadSeq < n) {
-      if (const Seq* q = seq_at(i + kAheadSeq)) __builtin_prefetch(q);
+    if (i + 24 < n && seqs[i + 24].id < seq_records_.size()) __builtin_prefetch(&seq_records_[seqs[i + 24].id]);
+    if (i + 16 < n) {
+      if (const std::uint32_t* t = tail_entry(i + 16)) __builtin_prefetch(t);
     }
-    if (i + kAheadTail < n) {
-      if (const std::uint32_t* t = tail_of(seq_at(i + kAheadTail))) __builtin_prefetch(t);
-    }
-    if (i + kAheadRecord < n) {
-      if (const std::uint32_t* t = tail_of(seq_at(i + kAheadRecord)); t != nullptr && *t < records_.size()) {
-        __builtin_prefetch(&records_[*t], 1);
-        __builtin_prefetch(&is_dirty_[*t], 1);
+    if (i + 8 < n) {
+      if (const std::uint32_t* t = tail_entry(i + 8); t != nullptr && *t < blocks_.size()) {
+        __builtin_prefetch(&blocks_[*t], 1);
       }
     }
 
-    const SequenceHandle sh = seqs[i];
-    if (const Status s = verify(sh); s != Status::kOk) return s;
-    if (const std::uint32_t* t = tail_of(&seqs_[sh.id]); t != nullptr) {
-      const std::uint32_t tail = *t;
-      // lookup(handle_of(tail)): a free (or out-of-range) tail is an invalid handle.
-      if (tail >= records_.size() || records_[tail].state() == BlockState::kFree) return Status::kInvalidHandle;
-      BlockDescriptor& d = records_[tail];
-      const std::uint32_t vt = d.exec.valid_tokens();
-      if (vt < block_tokens_) {
-        if (d.state() != BlockState::kOpen) return Status::kInvalidState;  // set_valid_tokens
-        d.exec.set_valid_tokens(vt + 1);
-        touch(tail);
-        out[i] = TokenTarget{tail, vt};
+    SeqRecord* q = nullptr;
+    if (const Status s = find(seqs[i], q); s != Status::kOk) return s;
+    const IdArena::Segment& g = q->seg;
+    if (g.capacity != 0 && g.length != 0) {
+      const std::uint32_t tail = arena_.view(g)[g.length - 1];
+      // As lookup(handle_of(tail)): a free tail reads as an invalid handle.
+      if (tail >= blocks_.size() || blocks_[tail].state() == BlockState::kFree) return Status::kInvalidHandle;
+      BlockDescriptor& b = blocks_[tail];
+      const std::uint32_t used = b.exec.valid_tokens();
+      if (used < block_tokens_) {  // room in the tail: set_valid_tokens(tail, used + 1)
+        if (b.state() != BlockState::kOpen) return Status::kInvalidState;
+        b.exec.set_valid_tokens(used + 1);
+        changed_blocks_.mark(tail);
+        out[i] = TokenTarget{tail, used};
         n_done = i + 1;
         continue;
       }
     }
-    AllocRequest req;
-    req.format = new_formats[i];
-    req.valid_tokens = 1;
-    req.layout = layout;
-    const Result<BlockHandle> r = append_block(sh, req);
-    if (!r.ok()) return r.status();
-    out[i] = TokenTarget{r.value().id, 0};
+    AllocRequest next;
+    next.format = new_formats[i];
+    next.valid_tokens = 1;
+    next.layout = layout;
+    const Result<BlockHandle> b = append_block(seqs[i], next);
+    if (!b.ok()) return b.status();
+    out[i] = TokenTarget{b.value().id, 0};
     n_done = i + 1;
   }
   return Status::kOk;
 }
 
-Result<std::span<const std::uint32_t>> HeteroBlockTable::sequence_block_ids(
-    SequenceHandle seq) const {
-  if (const Status s = verify(seq); s != Status::kOk) return s;
-  return arena_.view(seqs_[seq.id].seg);
+Result<std::span<const std::uint32_t>> HeteroBlockTable::sequence_block_ids(SequenceHandle seq) const {
+  const SeqRecord* q = nullptr;
+  if (const Status s = find(seq, q); s != Status::kOk) return s;
+  return arena_.view(q->seg);
 }
 
-Status HeteroBlockTable::build_exec_table(std::span<const SequenceHandle> seqs,
-                                          ExecTable& out) const {
+Status HeteroBlockTable::build_exec_table(std::span<const SequenceHandle> seqs, ExecTable& out) const {
   out.indptr.clear();
   out.blocks.clear();
+  // Every handle is checked before anything is built.
   std::uint64_t total = 0;
-  for (const SequenceHandle s : seqs) {
-    if (const Status st = verify(s); st != Status::kOk) return st;
-    total += seqs_[s.id].seg.length;
+  for (const SequenceHandle h : seqs) {
+    const SeqRecord* q = nullptr;
+    if (const Status s = find(h, q); s != Status::kOk) return s;
+    total += q->seg.length;
   }
   if (total > std::numeric_limits<std::uint32_t>::max()) return Status::kInvalidArgument;
   out.indptr.reserve(seqs.size() + 1);
   out.blocks.reserve(total);
   out.indptr.push_back(0);
-  for (const SequenceHandle s : seqs) {
-    for (const std::uint32_t id : arena_.view(seqs_[s.id].seg)) {
-      const BlockDescriptor& d = records_[id];
-      if (d.residency() != Residency::kDevice) {
+  for (const SequenceHandle h : seqs) {
+    for (const std::uint32_t id : arena_.view(seq_records_[h.id].seg)) {
+      if (blocks_[id].residency() != Residency::kDevice) {
         out.indptr.clear();
         out.blocks.clear();
         return Status::kNotDeviceResident;
       }
-      out.blocks.push_back(d.exec);
+      out.blocks.push_back(blocks_[id].exec);
     }
     out.indptr.push_back(static_cast<std::uint32_t>(out.blocks.size()));
   }
@@ -468,86 +511,89 @@ Status HeteroBlockTable::build_exec_table(std::span<const SequenceHandle> seqs,
 
 Status HeteroBlockTable::batch_segments(std::span<const SequenceHandle> seqs,
                                         std::vector<SequenceSegment>& out) const {
-  out.clear();
-  out.reserve(seqs.size());
-  for (const SequenceHandle s : seqs) {
-    if (const Status st = verify(s); st != Status::kOk) {
-      out.clear();
-      return st;
+  out.resize(seqs.size());
+  std::size_t k = 0;
+  for (const SequenceHandle h : seqs) {
+    const SeqRecord* q = nullptr;
+    const Status s = find(h, q);
+    if (s != Status::kOk) {
+      out.clear();  // all or nothing
+      return s;
     }
-    out.push_back(IdArena::kernel_view(seqs_[s.id].seg));
+    out[k++] = IdArena::kernel_view(q->seg);
   }
   return Status::kOk;
 }
 
 void HeteroBlockTable::collect_delta(ExecDelta& out) {
-  out.descriptor_patches.clear();
-  out.descriptor_patches.reserve(dirty_ids_.size());  // may throw; nothing changed yet
-  arena_.collect(out.id_patches);                      // strong guarantee
-  for (const std::uint32_t id : dirty_ids_) {
-    out.descriptor_patches.push_back(device_descriptor(id));
-    is_dirty_[id] = 0;
-  }
-  dirty_ids_.clear();
+  // Both outputs are sized before either queue is drained, so a throw changes nothing.
+  out.descriptor_patches.resize(changed_blocks_.size());
+  arena_.collect(out.id_patches);
+  std::size_t k = 0;
+  changed_blocks_.drain([&](std::uint32_t id) noexcept { out.descriptor_patches[k++] = device_descriptor(id); });
   out.descriptor_table_size = max_blocks();
   out.arena_size = arena_.size();
 }
 
 BlockExecDescriptor HeteroBlockTable::device_descriptor(std::uint32_t block_id) const noexcept {
   BlockExecDescriptor e{};
-  if (block_id < records_.size()) {
-    const BlockDescriptor& d = records_[block_id];
+  bool executable = false;
+  if (block_id < blocks_.size()) {
+    const BlockDescriptor& d = blocks_[block_id];
     e = d.exec;
-    if (d.state() != BlockState::kFree && d.residency() == Residency::kDevice) return e;
+    executable = d.state() != BlockState::kFree && d.residency() == Residency::kDevice;
   }
-  e.slot = kNoSlot;  // kernels must never dereference this record
-  e.set_format(kInvalidFormat);
-  e.block_id = block_id;
+  if (!executable) {  // a record no kernel may follow: no slot, format 15
+    e.slot = kNoSlot;
+    e.set_format(kInvalidFormat);
+    e.block_id = block_id;
+  }
   return e;
 }
 
 // ---- introspection -----------------------------------------------------------------------
 
-bool HeteroBlockTable::has_pool(FormatId format) const noexcept { return pool(format) != nullptr; }
+bool HeteroBlockTable::has_pool(FormatId format) const noexcept { return stack(format) != nullptr; }
 
 std::uint32_t HeteroBlockTable::free_slots(FormatId format) const noexcept {
-  const SlotPool* p = pool(format);
-  return p ? static_cast<std::uint32_t>(p->lifo.size()) : 0u;
+  const SlotStack* st = stack(format);
+  return st != nullptr ? st->depth : 0u;
 }
 
 std::uint32_t HeteroBlockTable::pool_slots(FormatId format) const noexcept {
-  const SlotPool* p = pool(format);
-  return p ? p->capacity : 0u;
+  const SlotStack* st = stack(format);
+  return st != nullptr ? st->capacity : 0u;
 }
 
 std::uint32_t HeteroBlockTable::slot_bytes(FormatId format) const noexcept {
-  const SlotPool* p = pool(format);
-  return p ? p->slot_bytes : 0u;
+  const SlotStack* st = stack(format);
+  return st != nullptr ? st->slot_bytes : 0u;
 }
 
 TableStats HeteroBlockTable::stats() const {
   TableStats st;
   st.blocks_capacity = max_blocks();
   st.format_changes_committed = committed_changes_;
-  for (const BlockDescriptor& d : records_) {
+  for (const BlockDescriptor& d : blocks_) {
     st.blocks_per_state[static_cast<std::size_t>(d.state())] += 1;
     if (d.state() == BlockState::kFree) continue;
     st.blocks_in_use += 1;
-    st.blocks_per_format[raw(d.exec.format())] += 1;
+    st.blocks_per_format[fmt_index(d.exec.format())] += 1;
     st.blocks_per_residency[static_cast<std::size_t>(d.residency())] += 1;
     st.valid_tokens += d.exec.valid_tokens();
     st.payload_bytes_in_use += slot_bytes(d.exec.format());
     if (d.state() == BlockState::kTranscoding) st.payload_bytes_in_use += slot_bytes(d.pending_format());
   }
   st.token_capacity_in_use = std::uint64_t{st.blocks_in_use} * block_tokens_;
-  for (const Seq& q : seqs_) {
-    st.active_sequences += q.live ? 1u : 0u;
+  for (const SeqRecord& q : seq_records_) {
+    if (!q.live) continue;
+    st.active_sequences += 1;
     st.arena_live_entries += q.seg.length;
     st.arena_reserved_entries += q.seg.capacity;
   }
   st.arena_entries = arena_.size();
   st.arena_free_entries = arena_.free_entries();
-  st.pending_descriptor_patches = dirty_ids_.size();
+  st.pending_descriptor_patches = changed_blocks_.size();
   st.pending_id_patches = arena_.pending_patches();
   return st;
 }
@@ -557,15 +603,16 @@ TableStats HeteroBlockTable::stats() const {
 // Image layout (host byte order; u32 lists are a count then the values):
 //   u64 magic "HLKVSNAP", u32 image version, u32 ABI version,
 //   u32 max_blocks, u32 block_tokens, u32 blocks in use, u64 committed format changes,
-//   u32 pool count, per pool {u32 format, u32 slot_bytes, u32 capacity, u32 list free slots},
-//   the block records (32 B each), u32 list free block ids,
+//   u32 pool count, per pool {u32 format, slot_bytes, capacity, stack top, stack depth,
+//   u32 list `below` links}, the block records (32 B each; free records carry their
+//   free-chain link in `reserved`), u32 top of the free block ids,
 //   u32 sequence count, per sequence {u32 offset, capacity, length, generation, live},
-//   u32 list free sequence ids, the id arena (IdArena::snapshot),
+//   u32 top of the free sequence ids, the id arena (IdArena::snapshot),
 //   u64 FNV-1a checksum of everything before it.
 
 namespace {
 constexpr std::uint64_t kSnapshotMagic = 0x50414E53564B4C48ull;  // bytes "HLKVSNAP" little-endian
-constexpr std::uint32_t kSnapshotVersion = 1;
+constexpr std::uint32_t kSnapshotVersion = 2;
 constexpr std::size_t kSeqBytes = 5 * sizeof(std::uint32_t);
 }  // namespace
 
@@ -575,32 +622,34 @@ std::vector<std::byte> HeteroBlockTable::snapshot() const {
   w.u64(kSnapshotMagic);
   w.u32(kSnapshotVersion);
   w.u32(kAbiVersion);
-  w.u32(static_cast<std::uint32_t>(records_.size()));
+  w.u32(max_blocks());
   w.u32(block_tokens_);
   w.u32(in_use_);
   w.u64(committed_changes_);
   std::uint32_t n_pools = 0;
-  for (const SlotPool& p : pools_) n_pools += p.present ? 1u : 0u;
+  for (const SlotStack& st : slots_) n_pools += st.present ? 1u : 0u;
   w.u32(n_pools);
   for (std::uint32_t f = 0; f < kMaxFormats; ++f) {
-    const SlotPool& p = pools_[f];
-    if (!p.present) continue;
+    const SlotStack& st = slots_[f];
+    if (!st.present) continue;
     w.u32(f);
-    w.u32(p.slot_bytes);
-    w.u32(p.capacity);
-    w.u32s(p.lifo);
+    w.u32(st.slot_bytes);
+    w.u32(st.capacity);
+    w.u32(st.top);
+    w.u32(st.depth);
+    w.u32s(st.below);
   }
-  w.bytes(records_.data(), records_.size() * sizeof(BlockDescriptor));
-  w.u32s(free_ids_);
-  w.u32(static_cast<std::uint32_t>(seqs_.size()));
-  for (const Seq& q : seqs_) {
+  w.bytes(blocks_.data(), blocks_.size() * sizeof(BlockDescriptor));
+  w.u32(free_block_top_);
+  w.u32(static_cast<std::uint32_t>(seq_records_.size()));
+  for (const SeqRecord& q : seq_records_) {
     w.u32(q.seg.offset);
     w.u32(q.seg.capacity);
     w.u32(q.seg.length);
     w.u32(q.generation);
     w.u32(q.live ? 1u : 0u);
   }
-  w.u32s(free_seqs_);
+  w.u32(free_seq_top_);
   arena_.snapshot(w);
   w.u64(detail::snapshot_checksum(out));
   return out;
@@ -622,13 +671,18 @@ Status HeteroBlockTable::restore(std::span<const std::byte> image, std::unique_p
       !r.u64(committed) || !r.u32(n_pools) || n_pools > kMaxFormats) {
     return Status::kCorrupt;
   }
+  struct Stack {
+    std::uint32_t top = kEnd, depth = 0;
+    std::vector<std::uint32_t> below;
+  };
   TableConfig config;
   config.max_blocks = max_blocks;
   config.block_tokens = block_tokens;
-  std::array<std::vector<std::uint32_t>, kMaxFormats> lifos;
+  std::array<Stack, kMaxFormats> stacks;
   for (std::uint32_t i = 0; i < n_pools; ++i) {
     std::uint32_t f = 0, slot_bytes = 0, capacity = 0;
-    if (!r.u32(f) || f >= kMaxFormats || !r.u32(slot_bytes) || !r.u32(capacity) || !r.u32s(lifos[f], capacity)) {
+    if (!r.u32(f) || f >= kMaxFormats || !r.u32(slot_bytes) || !r.u32(capacity) || !r.u32(stacks[f].top) ||
+        !r.u32(stacks[f].depth) || !r.u32s(stacks[f].below, capacity) || stacks[f].below.size() != capacity) {
       return Status::kCorrupt;
     }
     config.pools.push_back(PoolConfig{FormatId{static_cast<std::uint8_t>(f)}, slot_bytes, capacity});
@@ -637,20 +691,21 @@ Status HeteroBlockTable::restore(std::span<const std::byte> image, std::unique_p
   // The records are in the image: bound the allocation by it.
   if (std::size_t{max_blocks} * sizeof(BlockDescriptor) > r.remaining()) return Status::kCorrupt;
   auto t = std::make_unique<HeteroBlockTable>(config);
-  if (!r.bytes(t->records_.data(), std::size_t{max_blocks} * sizeof(BlockDescriptor)) ||
-      !r.u32s(t->free_ids_, max_blocks)) {
+  if (!r.bytes(t->blocks_.data(), std::size_t{max_blocks} * sizeof(BlockDescriptor)) ||
+      !r.u32(t->free_block_top_)) {
     return Status::kCorrupt;
   }
-  t->free_ids_.reserve(max_blocks);
   for (const PoolConfig& pc : config.pools) {
-    SlotPool& p = t->pools_[raw(pc.format)];
-    p.lifo = std::move(lifos[raw(pc.format)]);
-    p.lifo.reserve(p.capacity);  // the stacks never allocate when slots come back
+    SlotStack& st = t->slots_[fmt_index(pc.format)];
+    Stack& s = stacks[fmt_index(pc.format)];
+    st.top = s.top;
+    st.depth = s.depth;
+    st.below = std::move(s.below);
   }
   std::uint32_t n_seqs = 0;
   if (!r.u32(n_seqs) || std::size_t{n_seqs} * kSeqBytes > r.remaining()) return Status::kCorrupt;
-  t->seqs_.resize(n_seqs);
-  for (Seq& q : t->seqs_) {
+  t->seq_records_.resize(n_seqs);
+  for (SeqRecord& q : t->seq_records_) {
     std::uint32_t live = 0;
     if (!r.u32(q.seg.offset) || !r.u32(q.seg.capacity) || !r.u32(q.seg.length) || !r.u32(q.generation) ||
         !r.u32(live) || live > 1) {
@@ -658,117 +713,118 @@ Status HeteroBlockTable::restore(std::span<const std::byte> image, std::unique_p
     }
     q.live = live != 0;
   }
-  if (!r.u32s(t->free_seqs_, n_seqs) || !t->arena_.restore(r) || r.remaining() != 0) return Status::kCorrupt;
+  if (!r.u32(t->free_seq_top_) || !t->arena_.restore(r) || r.remaining() != 0) return Status::kCorrupt;
   t->in_use_ = in_use;
   t->committed_changes_ = committed;
-  // A fresh table already lists every descriptor as pending; the arena's restore did the
-  // same for every entry.
+  // The constructor left every descriptor pending and the arena's restore every entry, so
+  // the restored table's first delta is the whole device image.  validate() walks every
+  // chain with bounds, so a malformed image cannot loop or index out of range.
   if (!t->validate().ok()) return Status::kCorrupt;
   out = std::move(t);
   return Status::kOk;
 }
 
 ValidationReport HeteroBlockTable::validate() const {
-  const std::size_t n = records_.size();
-  std::vector<std::uint8_t> listed_free(n, 0);
-  for (const std::uint32_t id : free_ids_) {
-    if (id >= n || listed_free[id] || records_[id].state() != BlockState::kFree) {
-      return corrupt("free id list entry " + std::to_string(id) + " is invalid");
+  const std::size_t n = blocks_.size();
+  // The free block ids: a chain through free records, no repeats, ending at kEnd.
+  std::vector<bool> chained(n, false);
+  std::size_t free_count = 0;
+  for (std::uint32_t id = free_block_top_; id != kEnd; id = blocks_[id].reserved) {
+    if (id >= n || chained[id] || blocks_[id].state() != BlockState::kFree) {
+      return corrupt("free block chain is broken at id " + std::to_string(id));
     }
-    listed_free[id] = 1;
+    chained[id] = true;
+    free_count += 1;
   }
 
-  std::array<std::vector<std::uint8_t>, kMaxFormats> owned;
+  // Each pool's free slots: a chain of in-range, distinct slots of the stated depth.
+  std::array<std::vector<bool>, kMaxFormats> taken;
   for (std::uint32_t f = 0; f < kMaxFormats; ++f) {
-    const SlotPool& p = pools_[f];
-    if (!p.present) continue;
-    owned[f].assign(p.capacity, 0);
-    for (const std::uint32_t s : p.lifo) {
-      if (s >= p.capacity || owned[f][s]) {
-        return corrupt("pool " + std::to_string(f) + " lists slot " + std::to_string(s) + " badly");
-      }
-      owned[f][s] = 1;
+    const SlotStack& st = slots_[f];
+    if (!st.present) continue;
+    if (st.below.size() != st.capacity) return corrupt("pool " + std::to_string(f) + " link array size");
+    taken[f].assign(st.capacity, false);
+    std::uint32_t depth = 0;
+    for (std::uint32_t s = st.top; s != kEnd; s = st.below[s]) {
+      if (s >= st.capacity || taken[f][s]) return corrupt("pool " + std::to_string(f) + " free chain is broken");
+      taken[f][s] = true;
+      depth += 1;
     }
+    if (depth != st.depth) return corrupt("pool " + std::to_string(f) + " depth");
   }
-  auto own = [&](FormatId f, std::uint32_t slot, std::uint32_t id) -> std::string {
-    const SlotPool* p = pool(f);
-    if (p == nullptr) return "block " + std::to_string(id) + " has no pool";
-    if (slot >= p->capacity) return "block " + std::to_string(id) + " slot out of range";
-    std::uint8_t& o = owned[raw(f)][slot];
-    if (o) return "slot " + std::to_string(slot) + " owned twice";
-    o = 1;
+  auto take = [&](FormatId f, std::uint32_t slot, std::uint32_t id) -> std::string {
+    const SlotStack* st = stack(f);
+    if (st == nullptr) return "block " + std::to_string(id) + " has no pool";
+    if (slot >= st->capacity) return "block " + std::to_string(id) + " slot out of range";
+    if (taken[fmt_index(f)][slot]) return "slot " + std::to_string(slot) + " held twice";
+    taken[fmt_index(f)][slot] = true;
     return {};
   };
 
-  std::uint32_t counted = 0;
+  std::uint32_t live_blocks = 0;
   for (std::uint32_t id = 0; id < n; ++id) {
-    const BlockDescriptor& d = records_[id];
+    const BlockDescriptor& d = blocks_[id];
     if (d.exec.block_id != id) return corrupt("block " + std::to_string(id) + ": block_id field");
     if (d.state() == BlockState::kFree) {
-      if (!listed_free[id]) return corrupt("block " + std::to_string(id) + ": free but unlisted");
+      if (!chained[id]) return corrupt("block " + std::to_string(id) + ": free but not on the free chain");
       continue;
     }
-    counted += 1;
+    live_blocks += 1;
     if (d.refcount() == 0) return corrupt("block " + std::to_string(id) + ": refcount 0");
     if (d.exec.info_reserved() || d.control_reserved() || d.reserved) {
       return corrupt("block " + std::to_string(id) + ": reserved bits set");
     }
     if (d.exec.valid_tokens() > block_tokens_) return corrupt("valid_tokens above block_tokens");
-    if (!residency_ok(d.residency())) return corrupt("invalid residency");
-    if (std::string e = own(d.exec.format(), d.exec.slot, id); !e.empty()) return corrupt(e);
+    if (!valid_residency(d.residency())) return corrupt("invalid residency");
+    if (std::string e = take(d.exec.format(), d.exec.slot, id); !e.empty()) return corrupt(e);
     if (d.state() == BlockState::kTranscoding) {
       if (d.pending_format() == d.exec.format()) return corrupt("pending format == format");
-      if (std::string e = own(d.pending_format(), d.pending_slot, id); !e.empty()) return corrupt(e);
+      if (std::string e = take(d.pending_format(), d.pending_slot, id); !e.empty()) return corrupt(e);
     } else if (d.pending_slot != kNoSlot || d.pending_format() != kInvalidFormat) {
       return corrupt("pending slot outside a format change");
     }
   }
-  if (counted != in_use_) return corrupt("blocks_in_use counter");
-  if (free_ids_.size() + counted != n) return corrupt("free id list size");
+  if (live_blocks != in_use_) return corrupt("blocks_in_use counter");
+  if (free_count + live_blocks != n) return corrupt("free block chain length");
   for (std::uint32_t f = 0; f < kMaxFormats; ++f) {
-    if (pools_[f].present && std::find(owned[f].begin(), owned[f].end(), 0) != owned[f].end()) {
-      return corrupt("pool " + std::to_string(f) + " leaked a slot");
+    if (slots_[f].present && std::find(taken[f].begin(), taken[f].end(), false) != taken[f].end()) {
+      return corrupt("pool " + std::to_string(f) + " lost a slot");
     }
   }
 
-  std::vector<std::uint32_t> seq_refs(n, 0);
+  // Sequences: live ones reference live blocks (no more often than their refcounts); the
+  // released ones are exactly the free sequence chain.
+  std::vector<std::uint32_t> refs(n, 0);
   std::vector<IdArena::Segment> live;
-  std::size_t parked = 0;
-  for (std::size_t s = 0; s < seqs_.size(); ++s) {
-    const Seq& q = seqs_[s];
+  std::size_t released = 0;
+  for (std::size_t s = 0; s < seq_records_.size(); ++s) {
+    const SeqRecord& q = seq_records_[s];
     if (!q.live) {
-      parked += 1;
-      if (q.seg.capacity || q.seg.length) return corrupt("released sequence holds storage");
+      released += 1;
+      if (q.seg.capacity != 0 || q.seg.length != 0) return corrupt("released sequence holds storage");
       continue;
     }
     live.push_back(q.seg);
     for (const std::uint32_t id : arena_.view(q.seg)) {
-      if (id >= n || records_[id].state() == BlockState::kFree) {
+      if (id >= n || blocks_[id].state() == BlockState::kFree) {
         return corrupt("sequence " + std::to_string(s) + " references a free block");
       }
-      seq_refs[id] += 1;
+      refs[id] += 1;
     }
   }
   for (std::uint32_t id = 0; id < n; ++id) {
-    if (seq_refs[id] > records_[id].refcount()) return corrupt("sequence refs above refcount");
+    if (refs[id] > blocks_[id].refcount()) return corrupt("sequence references above refcount");
   }
-  if (parked != free_seqs_.size()) return corrupt("sequence free list size");
-  std::vector<std::uint8_t> seen(seqs_.size(), 0);
-  for (const std::uint32_t s : free_seqs_) {
-    if (s >= seqs_.size() || seqs_[s].live || seen[s]) return corrupt("sequence free list entry");
-    seen[s] = 1;
+  std::vector<bool> on_chain(seq_records_.size(), false);
+  std::size_t chain_len = 0;
+  for (std::uint32_t s = free_seq_top_; s != kEnd; s = seq_records_[s].seg.offset) {
+    if (s >= seq_records_.size() || seq_records_[s].live || on_chain[s]) return corrupt("free sequence chain is broken");
+    on_chain[s] = true;
+    chain_len += 1;
   }
+  if (chain_len != released) return corrupt("free sequence chain length");
   if (std::string e = arena_.validate(live); !e.empty()) return corrupt(e);
-
-  if (is_dirty_.size() != n || dirty_ids_.capacity() < n) return corrupt("dirty tracking size");
-  std::vector<std::uint8_t> in_list(n, 0);
-  for (const std::uint32_t id : dirty_ids_) {
-    if (id >= n || !is_dirty_[id] || in_list[id]) return corrupt("dirty list entry");
-    in_list[id] = 1;
-  }
-  if (static_cast<std::size_t>(std::count(is_dirty_.begin(), is_dirty_.end(), 1)) != dirty_ids_.size()) {
-    return corrupt("dirty flag without a list entry");
-  }
+  if (changed_blocks_.span() != n || !changed_blocks_.consistent()) return corrupt("descriptor change queue");
   return {};
 }
 

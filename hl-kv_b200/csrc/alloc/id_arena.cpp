@@ -1,216 +1,196 @@
 // IdArena (see include/hl_allocator/id_arena.hpp).
 //
-// Observable behaviour follows the reference's project1_allocator/src/id_arena.cpp:
-// size classes 8 << k (class of `needed` = ceil(log2(needed)) - 3, class 0 for
-// needed <= 8), LIFO reuse per class before carving new space at the end,
-// relocation copies entries in order and marks each one dirty, and collect()
-// reports dirty offsets in marking order.
+// The placement policy is the reference's (project1_allocator/src/id_arena.cpp), because
+// arena offsets and the patch stream are observable: capacities are 8 << k entries and a
+// sequence needing n entries gets the smallest class holding n; a class reuses its most
+// recently freed segment before new space is appended; a moved segment's entries are
+// written (and queued) in order, and its old segment is freed only after the new one is
+// taken.  The storage is this library's own: free segments are stacks linked through a
+// side array indexed by 8-entry unit, and the change queue is epoch-stamped.
 #include "hl_allocator/id_arena.hpp"
 #include "hl_allocator/snapshot_io.hpp"
 
-#include <algorithm>
 #include <bit>
 #include <cassert>
 
 namespace hl::alloc {
 namespace {
 
-constexpr std::uint32_t kClassShift = 3;  // kMinSegment == 1 << 3
-static_assert(IdArena::kMinSegment == (1u << kClassShift));
+constexpr std::uint32_t capacity_of(std::uint32_t cls) noexcept { return IdArena::kMinSegment << cls; }
 
-constexpr std::uint32_t class_capacity(std::uint32_t c) noexcept { return IdArena::kMinSegment << c; }
-
-// Smallest class holding `needed` (>= 1) entries.
-constexpr std::uint32_t class_holding(std::uint32_t needed) noexcept {
-  return needed <= IdArena::kMinSegment
-             ? 0u
-             : static_cast<std::uint32_t>(std::bit_width(needed - 1u)) - kClassShift;
+// The smallest class with capacity >= n (n >= 1): ceil(log2(n)) - 3, at least 0.
+constexpr std::uint32_t class_for(std::uint32_t n) noexcept {
+  const std::uint32_t bits = static_cast<std::uint32_t>(std::bit_width(n - 1u));
+  return bits > 3u ? bits - 3u : 0u;
 }
 
-// Class whose capacity is exactly `capacity`, or kNumClasses when there is none.
-constexpr std::uint32_t class_exact(std::uint32_t capacity) noexcept {
-  if (capacity < IdArena::kMinSegment || !std::has_single_bit(capacity)) return IdArena::kNumClasses;
-  const std::uint32_t c = static_cast<std::uint32_t>(std::countr_zero(capacity)) - kClassShift;
+// The class of a segment capacity, or kNumClasses when it is not a class size.
+constexpr std::uint32_t class_of_capacity(std::uint32_t cap) noexcept {
+  if (!std::has_single_bit(cap) || cap < IdArena::kMinSegment) return IdArena::kNumClasses;
+  const std::uint32_t c = static_cast<std::uint32_t>(std::countr_zero(cap)) - 3u;
   return c < IdArena::kNumClasses ? c : IdArena::kNumClasses;
 }
 
-static_assert(class_holding(1) == 0 && class_holding(8) == 0 && class_holding(9) == 1);
-static_assert(class_holding(IdArena::kMaxSegment) == IdArena::kNumClasses - 1);
-static_assert(class_exact(16) == 1 && class_exact(24) == IdArena::kNumClasses);
-
-// Grows capacity at least geometrically so amortized cost stays O(1).
-template <typename T>
-void ensure_capacity(std::vector<T>& v, std::size_t n) {
-  if (v.capacity() < n) v.reserve(std::max(n, v.capacity() * 2));
-}
+static_assert(IdArena::kMinSegment == 8u, "class arithmetic assumes 8-entry minimum segments");
+static_assert(class_for(1) == 0 && class_for(8) == 0 && class_for(9) == 1 && class_for(17) == 2);
+static_assert(class_for(IdArena::kMaxSegment) == IdArena::kNumClasses - 1);
+static_assert(class_of_capacity(64) == 3 && class_of_capacity(48) == IdArena::kNumClasses);
 
 }  // namespace
 
-Status IdArena::carve_or_reuse(std::uint32_t size_class, std::uint32_t& offset) {
-  std::vector<std::uint32_t>& parked = parked_[size_class];
-  if (!parked.empty()) {
-    offset = parked.back();
-    parked.pop_back();
+Status IdArena::obtain(std::uint32_t cls, std::uint32_t& offset) {
+  if (free_top_[cls] != kNone) {
+    offset = free_top_[cls];
+    free_top_[cls] = next_free_[offset / kMinSegment];
+    free_len_[cls] -= 1;
     return Status::kOk;
   }
-  const std::size_t old_size = ids_.size();
-  const std::size_t new_size = old_size + class_capacity(size_class);
-  if (new_size > kMaxEntries) return Status::kCapacityExceeded;
-  // Everything the noexcept paths rely on is allocated here, before any state
-  // changes: room to mark every entry dirty, and room to park every segment of
-  // this class that will ever exist.
-  ensure_capacity(ids_, new_size);
-  ensure_capacity(is_dirty_, new_size);
-  ensure_capacity(dirty_order_, new_size);
-  ensure_capacity(parked, std::size_t{carved_[size_class]} + 1);
-  ids_.resize(new_size);
-  is_dirty_.resize(new_size, 0);
-  carved_[size_class] += 1;
-  offset = static_cast<std::uint32_t>(old_size);
+  const std::size_t at = entry_.size();
+  const std::size_t grown = at + capacity_of(cls);
+  if (grown > kMaxEntries) return Status::kCapacityExceeded;
+  // Every allocation before any change: a throw leaves the arena as it was.
+  const std::size_t units = grown / kMinSegment;
+  if (entry_.capacity() < grown) entry_.reserve(grown > 2 * entry_.capacity() ? grown : 2 * entry_.capacity());
+  if (next_free_.capacity() < units) next_free_.reserve(units > 2 * next_free_.capacity() ? units : 2 * next_free_.capacity());
+  changed_.grow(grown);
+  entry_.resize(grown, 0u);
+  next_free_.resize(units, kNone);
+  offset = static_cast<std::uint32_t>(at);
   return Status::kOk;
 }
 
-void IdArena::mark(std::uint32_t offset) noexcept {
-  if (is_dirty_[offset]) return;
-  is_dirty_[offset] = 1;
-  dirty_order_.push_back(offset);  // capacity covers every entry
+void IdArena::park(std::uint32_t cls, std::uint32_t offset) noexcept {
+  next_free_[offset / kMinSegment] = free_top_[cls];
+  free_top_[cls] = offset;
+  free_len_[cls] += 1;
 }
 
 Status IdArena::reserve(Segment& seg, std::uint32_t needed) {
   if (needed <= seg.capacity) return Status::kOk;
   if (needed > kMaxSegment) return Status::kCapacityExceeded;
-  const std::uint32_t c = class_holding(needed);
-  std::uint32_t dst = 0;
-  if (const Status s = carve_or_reuse(c, dst); s != Status::kOk) return s;
+  const std::uint32_t cls = class_for(needed);
+  std::uint32_t to = 0;
+  if (const Status s = obtain(cls, to); s != Status::kOk) return s;
+  // Copy the live entries across (each one a patch for the device), then free the old
+  // segment: taking the new one first keeps a segment from being reused by its own move.
   for (std::uint32_t k = 0; k < seg.length; ++k) {
-    ids_[dst + k] = ids_[seg.offset + k];
-    mark(dst + k);
+    entry_[to + k] = entry_[seg.offset + k];
+    changed_.mark(to + k);
   }
-  if (seg.capacity != 0) parked_[class_exact(seg.capacity)].push_back(seg.offset);
-  seg.offset = dst;
-  seg.capacity = class_capacity(c);
+  if (seg.capacity != 0) park(class_of_capacity(seg.capacity), seg.offset);
+  seg.offset = to;
+  seg.capacity = capacity_of(cls);
   return Status::kOk;
 }
 
 void IdArena::push_back(Segment& seg, std::uint32_t block_id) noexcept {
   assert(seg.length < seg.capacity && "IdArena::push_back needs reserve() first");
   const std::uint32_t at = seg.offset + seg.length;
-  ids_[at] = block_id;
-  mark(at);
+  entry_[at] = block_id;
+  changed_.mark(at);
   seg.length += 1;
 }
 
 void IdArena::release(Segment& seg) noexcept {
-  if (seg.capacity != 0) parked_[class_exact(seg.capacity)].push_back(seg.offset);
+  if (seg.capacity != 0) park(class_of_capacity(seg.capacity), seg.offset);
   seg = Segment{};
 }
 
 std::span<const std::uint32_t> IdArena::view(const Segment& seg) const noexcept {
   if (seg.capacity == 0) return {};
-  return {ids_.data() + seg.offset, seg.length};
+  return std::span<const std::uint32_t>(entry_).subspan(seg.offset, seg.length);
 }
 
 void IdArena::collect(std::vector<IdPatch>& out) {
-  out.clear();
-  out.reserve(dirty_order_.size());  // the only allocation, before any state change
-  for (const std::uint32_t off : dirty_order_) {
-    out.push_back(IdPatch{off, ids_[off]});
-    is_dirty_[off] = 0;
-  }
-  dirty_order_.clear();
+  out.resize(changed_.size());  // the only allocation, before the queue is touched
+  std::size_t k = 0;
+  changed_.drain([&](std::uint32_t off) noexcept { out[k++] = IdPatch{off, entry_[off]}; });
 }
 
 std::uint64_t IdArena::free_entries() const noexcept {
-  std::uint64_t sum = 0;
-  for (std::uint32_t c = 0; c < kNumClasses; ++c) {
-    sum += std::uint64_t{parked_[c].size()} * class_capacity(c);
-  }
-  return sum;
+  std::uint64_t total = 0;
+  for (std::uint32_t c = 0; c < kNumClasses; ++c) total += std::uint64_t{free_len_[c]} * capacity_of(c);
+  return total;
 }
 
+// Image: the entries, the free-stack links (one per 8-entry unit), then per class the top
+// of its free stack and the stack's length.
 void IdArena::snapshot(detail::SnapshotWriter& w) const {
-  w.u32s(ids_);
-  for (std::uint32_t c = 0; c < kNumClasses; ++c) w.u32s(parked_[c]);
-  for (std::uint32_t c = 0; c < kNumClasses; ++c) w.u32(carved_[c]);
+  w.u32s(entry_);
+  w.u32s(next_free_);
+  for (std::uint32_t c = 0; c < kNumClasses; ++c) {
+    w.u32(free_top_[c]);
+    w.u32(free_len_[c]);
+  }
 }
 
 bool IdArena::restore(detail::SnapshotReader& r) {
-  std::vector<std::uint32_t> ids;
-  if (!r.u32s(ids, kMaxEntries)) return false;
-  std::array<std::vector<std::uint32_t>, kNumClasses> parked;
+  std::vector<std::uint32_t> entries, links;
+  if (!r.u32s(entries, kMaxEntries) || entries.size() % kMinSegment != 0) return false;
+  if (!r.u32s(links, entries.size() / kMinSegment) || links.size() != entries.size() / kMinSegment) return false;
+  std::array<std::uint32_t, kNumClasses> top{}, len{};
+  std::uint64_t parked = 0;
   for (std::uint32_t c = 0; c < kNumClasses; ++c) {
-    if (!r.u32s(parked[c], ids.size())) return false;
+    if (!r.u32(top[c]) || !r.u32(len[c])) return false;
+    // The stacks' segments fit in the arena (this also bounds the walk below); each
+    // stack holds exactly len[c] in-range links and then ends.
+    parked += std::uint64_t{len[c]} * capacity_of(c);
+    if (parked > entries.size()) return false;
+    std::uint32_t at = top[c];
+    for (std::uint32_t k = 0; k < len[c]; ++k) {
+      if (at == kNone || at % kMinSegment != 0 || std::uint64_t{at} + capacity_of(c) > entries.size()) return false;
+      at = links[at / kMinSegment];
+    }
+    if (at != kNone) return false;
   }
-  std::array<std::uint32_t, kNumClasses> carved{};
-  std::uint64_t carved_entries = 0;
-  for (std::uint32_t c = 0; c < kNumClasses; ++c) {
-    if (!r.u32(carved[c])) return false;
-    carved_entries += std::uint64_t{carved[c]} * class_capacity(c);
-  }
-  // The segments must tile the arena before anything is sized from the counts.
-  if (carved_entries != ids.size()) return false;
-  const std::size_t n = ids.size();
-  ids_ = std::move(ids);
-  is_dirty_.assign(n, 1);
-  dirty_order_.clear();
-  dirty_order_.reserve(n);
-  for (std::size_t k = 0; k < n; ++k) dirty_order_.push_back(static_cast<std::uint32_t>(k));
-  for (std::uint32_t c = 0; c < kNumClasses; ++c) {
-    parked_[c] = std::move(parked[c]);
-    ensure_capacity(parked_[c], std::max<std::size_t>(carved[c], parked_[c].size()));
-  }
-  carved_ = carved;
+  detail::ChangeQueue changed;
+  changed.grow(entries.size());
+  for (std::size_t k = 0; k < entries.size(); ++k) changed.mark(static_cast<std::uint32_t>(k));
+  entry_ = std::move(entries);
+  next_free_ = std::move(links);
+  changed_ = std::move(changed);
+  free_top_ = top;
+  free_len_ = len;
   return true;
 }
 
 std::string IdArena::validate(std::span<const Segment> live) const {
-  const std::size_t n = ids_.size();
-  if (is_dirty_.size() != n) return "arena: dirty flags do not cover the arena";
-  if (dirty_order_.capacity() < n) return "arena: dirty list cannot hold every entry";
-  std::uint64_t carved_entries = 0;
-  for (std::uint32_t c = 0; c < kNumClasses; ++c) {
-    carved_entries += std::uint64_t{carved_[c]} * class_capacity(c);
-    if (parked_[c].size() > carved_[c] || parked_[c].capacity() < carved_[c]) {
-      return "arena: free list of class " + std::to_string(c) + " is inconsistent";
-    }
-  }
-  if (carved_entries != n) return "arena: carved segments do not sum to the arena size";
-
-  std::vector<std::uint8_t> owner(n, 0);
-  auto claim = [&](std::uint32_t off, std::uint32_t cap) -> std::string {
-    if (class_exact(cap) == kNumClasses) return "arena: capacity " + std::to_string(cap) + " is not a class";
-    if (std::uint64_t{off} + cap > n) return "arena: segment at " + std::to_string(off) + " out of range";
-    for (std::uint64_t k = off; k < std::uint64_t{off} + cap; ++k) {
-      if (owner[k]) return "arena: entry " + std::to_string(k) + " owned twice";
-      owner[k] = 1;
+  const std::size_t n = entry_.size();
+  if (changed_.span() < n) return "arena: change stamps do not cover the arena";
+  if (n % kMinSegment != 0 || next_free_.size() != n / kMinSegment) return "arena: link array size";
+  if (!changed_.consistent()) return "arena: change queue inconsistent";
+  std::vector<bool> owned(n, false);
+  auto claim = [&](std::uint64_t off, std::uint32_t cap, const char* what) -> std::string {
+    if (off + cap > n) return std::string("arena: ") + what + " segment at " + std::to_string(off) + " out of range";
+    for (std::uint64_t k = off; k < off + cap; ++k) {
+      if (owned[k]) return "arena: entry " + std::to_string(k) + " in two segments";
+      owned[k] = true;
     }
     return {};
   };
   for (const Segment& s : live) {
     if (s.capacity == 0) {
-      if (s.length != 0) return "arena: storage-less segment with a length";
+      if (s.length != 0) return "arena: a segment without storage has a length";
       continue;
     }
+    if (class_of_capacity(s.capacity) == kNumClasses) return "arena: capacity " + std::to_string(s.capacity) + " is not a class";
     if (s.length > s.capacity) return "arena: length exceeds capacity";
-    if (std::string e = claim(s.offset, s.capacity); !e.empty()) return e;
+    if (std::string e = claim(s.offset, s.capacity, "live"); !e.empty()) return e;
   }
   for (std::uint32_t c = 0; c < kNumClasses; ++c) {
-    for (const std::uint32_t off : parked_[c]) {
-      if (std::string e = claim(off, class_capacity(c)); !e.empty()) return e;
+    std::uint32_t at = free_top_[c];
+    for (std::uint32_t k = 0; k < free_len_[c]; ++k) {
+      if (at == kNone || at >= n || at % kMinSegment != 0) {
+        return "arena: free stack of class " + std::to_string(c) + " is short or broken";
+      }
+      if (std::string e = claim(at, capacity_of(c), "free"); !e.empty()) return e;
+      at = next_free_[at / kMinSegment];
     }
+    if (at != kNone) return "arena: free stack of class " + std::to_string(c) + " is longer than its count";
   }
   for (std::size_t k = 0; k < n; ++k) {
-    if (!owner[k]) return "arena: entry " + std::to_string(k) + " leaked";
+    if (!owned[k]) return "arena: entry " + std::to_string(k) + " belongs to no segment";
   }
-  std::vector<std::uint8_t> listed(n, 0);
-  for (const std::uint32_t off : dirty_order_) {
-    if (off >= n || !is_dirty_[off] || listed[off]) {
-      return "arena: dirty list entry " + std::to_string(off) + " inconsistent";
-    }
-    listed[off] = 1;
-  }
-  const auto flagged = static_cast<std::size_t>(std::count(is_dirty_.begin(), is_dirty_.end(), 1));
-  if (flagged != dirty_order_.size()) return "arena: dirty flag without a list entry";
   return {};
 }
 

@@ -180,7 +180,7 @@ class HeteroBlockTable {
   void collect_delta(ExecDelta& out);
   [[nodiscard]] BlockExecDescriptor device_descriptor(std::uint32_t block_id) const noexcept;
   [[nodiscard]] std::size_t pending_descriptor_patches() const noexcept {
-    return dirty_ids_.size();
+    return changed_blocks_.size();
   }
   [[nodiscard]] std::size_t pending_id_patches() const noexcept {
     return arena_.pending_patches();
@@ -189,7 +189,7 @@ class HeteroBlockTable {
   // -- introspection -----------------------------------------------------------------
   [[nodiscard]] std::uint32_t block_tokens() const noexcept { return block_tokens_; }
   [[nodiscard]] std::uint32_t max_blocks() const noexcept {
-    return static_cast<std::uint32_t>(records_.size());
+    return static_cast<std::uint32_t>(blocks_.size());
   }
   [[nodiscard]] std::uint32_t blocks_in_use() const noexcept { return in_use_; }
   [[nodiscard]] bool has_pool(FormatId format) const noexcept;
@@ -215,39 +215,49 @@ class HeteroBlockTable {
   [[nodiscard]] ValidationReport validate() const;
 
  private:
-  struct SlotPool {
+  static constexpr std::uint32_t kEnd = 0xFFFF'FFFFu;  // end of a free chain
+
+  // The free slots of one pool, handed out last-freed-first: a stack threaded through
+  // `below` (below[s] = the slot under s while s is free).  Sized once; never allocates.
+  struct SlotStack {
     bool present = false;
     std::uint32_t slot_bytes = 0;
     std::uint32_t capacity = 0;
-    std::vector<std::uint32_t> lifo;  // free slots; back() is handed out next
+    std::uint32_t top = kEnd;
+    std::uint32_t depth = 0;
+    std::vector<std::uint32_t> below;
   };
-  struct Seq {
+  // A sequence: its arena segment, or -- once released -- a link in the chain of free
+  // sequence ids (seg.offset, with capacity and length 0).
+  struct SeqRecord {
     IdArena::Segment seg;
     std::uint32_t generation = 0;
     bool live = false;
   };
 
-  [[nodiscard]] Status verify(BlockHandle h) const noexcept;
-  [[nodiscard]] Status verify(SequenceHandle s) const noexcept;
-  [[nodiscard]] Status verify(const AllocRequest& r) const noexcept;
-  [[nodiscard]] SlotPool* pool(FormatId f) noexcept;
-  [[nodiscard]] const SlotPool* pool(FormatId f) const noexcept;
-  void reset_record(std::uint32_t id, std::uint32_t generation) noexcept;
-  void drop_reference(std::uint32_t id) noexcept;
-  void retire(std::uint32_t id) noexcept;
-  void touch(std::uint32_t id) noexcept;
+  [[nodiscard]] Status find(BlockHandle h, BlockDescriptor*& out) noexcept;
+  [[nodiscard]] Status find(BlockHandle h, const BlockDescriptor*& out) const noexcept;
+  [[nodiscard]] Status find(SequenceHandle h, SeqRecord*& out) noexcept;
+  [[nodiscard]] Status find(SequenceHandle h, const SeqRecord*& out) const noexcept;
+  [[nodiscard]] Status admissible(const AllocRequest& r) const noexcept;
+  [[nodiscard]] SlotStack* stack(FormatId f) noexcept;
+  [[nodiscard]] const SlotStack* stack(FormatId f) const noexcept;
+  static bool pop(SlotStack& st, std::uint32_t& slot) noexcept;
+  static void push(SlotStack& st, std::uint32_t slot) noexcept;
+  void init_free_record(std::uint32_t id, std::uint32_t generation) noexcept;
+  void unreference(std::uint32_t id) noexcept;
+  void free_block(std::uint32_t id) noexcept;
 
   std::uint32_t block_tokens_;
   std::uint32_t in_use_ = 0;
   std::uint64_t committed_changes_ = 0;
-  std::vector<BlockDescriptor> records_;
-  std::vector<std::uint32_t> free_ids_;  // LIFO
-  std::array<SlotPool, kMaxFormats> pools_{};
-  std::vector<Seq> seqs_;
-  std::vector<std::uint32_t> free_seqs_;  // LIFO
+  std::vector<BlockDescriptor> blocks_;   // by id; a free record's `reserved` links the free ids
+  std::uint32_t free_block_top_ = kEnd;   // next id allocate() hands out
+  std::array<SlotStack, kMaxFormats> slots_{};
+  std::vector<SeqRecord> seq_records_;
+  std::uint32_t free_seq_top_ = kEnd;     // next id create_sequence() reuses
   IdArena arena_;
-  std::vector<std::uint8_t> is_dirty_;   // per block id
-  std::vector<std::uint32_t> dirty_ids_; // unique, capacity max_blocks
+  detail::ChangeQueue changed_blocks_;    // ids whose device descriptor is out of date
 };
 
 }  // namespace hl::alloc

@@ -6,20 +6,25 @@
 // (same public API, same observable results: offsets, capacities and patch
 // order).  A sequence owns one segment whose capacity is a power-of-two size
 // class (8 << k entries, 8 .. 2^31).  A full segment moves to one of the next
-// class, copying its entries; freed segments are kept per class (LIFO) and
-// reused; the array only grows.  Every write marks its entry; collect() turns
-// the marked entries into {offset, block_id} patches, each offset once, so a
+// class, copying its entries; freed segments are reused per class, last freed
+// first; the array only grows.  Every write queues its entry; collect() turns
+// the queued entries into {offset, block_id} patches, each offset once, so a
 // device can apply them in any order.
 //
-// reserve() gives the strong guarantee: all allocation happens before any
-// state changes, so push_back(), release() and the dirty bookkeeping never
-// allocate and are noexcept.
+// Storage: the entries in one array; the free segments of a class form a stack
+// linked through a side array with one slot per 8-entry unit (segments start on
+// unit boundaries), so freeing never allocates and never touches an entry -- a
+// freed entry still waiting to be patched keeps the id it was written with; the
+// entries to patch are a detail::ChangeQueue.  reserve() gives the strong guarantee: all
+// allocation happens before any state changes, so push_back(), release() and the
+// change bookkeeping never allocate and are noexcept.
 #include <array>
 #include <cstdint>
 #include <span>
 #include <string>
 #include <vector>
 
+#include "hl_allocator/change_queue.hpp"
 #include "hl_allocator/status.hpp"
 
 namespace hl::alloc {
@@ -72,36 +77,47 @@ class IdArena {
                              : SequenceSegment{seg.offset, seg.length};
   }
 
-  /// Replaces `out` with one patch per dirty entry (in marking order) and clears the marks.
+  /// Replaces `out` with one patch per changed entry (first change first) and empties the queue.
   void collect(std::vector<IdPatch>& out);
 
   [[nodiscard]] std::uint32_t size() const noexcept {
-    return static_cast<std::uint32_t>(ids_.size());
+    return static_cast<std::uint32_t>(entry_.size());
   }
-  [[nodiscard]] std::size_t pending_patches() const noexcept { return dirty_order_.size(); }
+  [[nodiscard]] std::size_t pending_patches() const noexcept { return changed_.size(); }
   /// Total capacity parked on the free lists.
   [[nodiscard]] std::uint64_t free_entries() const noexcept;
 
-  /// Appends the arena (entries, free lists, carved segment counts) to a table snapshot.
+  /// Appends the arena (entries, and per class the top and length of its free stack) to a
+  /// table snapshot.
   void snapshot(detail::SnapshotWriter& w) const;
   /// Replaces the arena with one that snapshot() wrote; every entry is then pending, so
   /// the next collect() reports all of them.  False, with nothing changed, on a malformed
   /// image.
   [[nodiscard]] bool restore(detail::SnapshotReader& r);
 
-  /// Checks that `live` plus the free lists tile the array exactly and that the
-  /// dirty bookkeeping is consistent; "" when it holds, else the first problem.
+  /// Checks that `live` plus the free stacks tile the array exactly and that the
+  /// change queue is consistent; "" when it holds, else the first problem.
   [[nodiscard]] std::string validate(std::span<const Segment> live) const;
 
  private:
-  [[nodiscard]] Status carve_or_reuse(std::uint32_t size_class, std::uint32_t& offset);
-  void mark(std::uint32_t offset) noexcept;
+  static constexpr std::uint32_t kNone = 0xFFFF'FFFFu;  // end of a free stack
 
-  std::vector<std::uint32_t> ids_;
-  std::vector<std::uint8_t> is_dirty_;       // per entry
-  std::vector<std::uint32_t> dirty_order_;   // offsets, unique; capacity >= ids_.size()
-  std::array<std::vector<std::uint32_t>, kNumClasses> parked_{};  // free offsets per class
-  std::array<std::uint32_t, kNumClasses> carved_{};               // segments created per class
+  /// A segment of class `cls` for a sequence: the last one freed, else new space at the end.
+  [[nodiscard]] Status obtain(std::uint32_t cls, std::uint32_t& offset);
+  /// Puts a segment of class `cls` on top of its free stack.
+  void park(std::uint32_t cls, std::uint32_t offset) noexcept;
+
+  static constexpr std::array<std::uint32_t, kNumClasses> no_free_segments() {
+    std::array<std::uint32_t, kNumClasses> a{};
+    for (std::uint32_t& x : a) x = kNone;
+    return a;
+  }
+
+  std::vector<std::uint32_t> entry_;      // the arena
+  std::vector<std::uint32_t> next_free_;  // per 8-entry unit: the free segment under this one
+  detail::ChangeQueue changed_;           // entries the device copy lacks, first change first
+  std::array<std::uint32_t, kNumClasses> free_top_ = no_free_segments();  // per class, kNone: empty
+  std::array<std::uint32_t, kNumClasses> free_len_{};                     // segments on each stack
 };
 
 }  // namespace hl::alloc

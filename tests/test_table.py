@@ -279,7 +279,7 @@ def test_snapshot_rejects_damaged_images(hlkv_lib):
         assert h.Table.restore(bad)[0] == corrupt
     # a foreign version with a valid checksum is still rejected
     body = bytearray(image[:-8])
-    body[8] = 2
+    body[8] = 0xEE  # an image version this library does not know
     fnv = 0xCBF29CE484222325
     for byte in body:
         fnv = ((fnv ^ byte) * 0x100000001B3) & 0xFFFFFFFFFFFFFFFF
