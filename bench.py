@@ -424,9 +424,13 @@ def run_hlkv(args) -> None:
         if updates is not None:
             launches[0] += updates.launch(stream, err)
         moved[0] += updates.sweep_bytes if updates is not None else wl.algorithmic_bytes
-        for segs in layer_segs:
+        # Each layer's launch overlaps its prologue with the previous gather's tail
+        # (HLKV_LAUNCH_OVERLAP_PREVIOUS), except right after kernel (3), which writes the
+        # tables the prologue reads.
+        for i, segs in enumerate(layer_segs):
             hlkv.gather_dequant(pools, wl.layout, wl.dt.table_ptr, wl.dt.table_size,
-                                wl.dt.arena_ptr, wl.dt.arena_size, segs, out, err, stream=stream)
+                                wl.dt.arena_ptr, wl.dt.arena_size, segs, out, err, stream=stream,
+                                overlap_previous=not args.no_overlap and (updates is None or i > 0))
         launches[0] += len(layer_segs)
 
     def barrier():
@@ -1266,6 +1270,8 @@ def main() -> None:
     ap.add_argument("--workload", choices=sorted(WORKLOADS), default="llama8b")
     ap.add_argument("--e2e-steps", type=int, default=10)
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--no-overlap", action="store_true",
+                    help="gather workloads: launch every layer without programmatic dependent launch")
     ap.add_argument("--ctas", type=int, default=0,
                     help="attention workloads: balanced mode over this many CTAs (0 = balanced over 4 per SM "
                          "when sequence lengths are uneven, else split mode)")

@@ -73,9 +73,10 @@ constexpr uint32_t kSkip = 0xFFu;
 constexpr uint32_t kWide = 0x100u;
 
 // Resolves block j of sequence `seq` into an Item; on a failed check the item
-// is skipped and its bit reported.  Check order matches the oracle's
+// is skipped and its bit collected in *s_err (this CTA's shared error word,
+// written to *p.err once the CTA is done).  Check order matches the oracle's
 // resolve_block().
-__device__ Item resolve(const Params& p, uint32_t seq, uint64_t j, uint64_t blocks_before) {
+__device__ Item resolve(const Params& p, uint32_t seq, uint64_t j, uint64_t blocks_before, uint32_t* s_err) {
   Item it{nullptr, nullptr, kSkip, 0, 0, 0, make_float2(0.0f, 0.0f)};
   uint32_t bad = 0;
   const uint64_t base = p.out_offsets ? p.out_offsets[seq] : blocks_before * p.block_elems;
@@ -110,7 +111,7 @@ __device__ Item resolve(const Params& p, uint32_t seq, uint64_t j, uint64_t bloc
       }
     }
   }
-  if (bad) atomicOr(p.err, bad);
+  if (bad) atomicOr(s_err, bad);
   return it;
 }
 
@@ -223,13 +224,33 @@ __device__ uint64_t exclusive_scan(uint64_t x, uint64_t* s_out, uint64_t* s_warp
   return total;
 }
 
+// Programmatic dependent launch (griddepcontrol, sm_90 and later).  launch_dependents lets a
+// kernel launched after this one with programmatic stream serialization start its CTAs as
+// this grid's CTAs retire; wait blocks until every grid this one depends on has completed
+// and its memory is visible (a no-op for an ordinary launch).
+__device__ __forceinline__ void allow_dependents_to_launch() {
+  asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
+}
+__device__ __forceinline__ void wait_for_prerequisites() {
+  asm volatile("griddepcontrol.wait;" ::: "memory");
+}
+
+// Before wait_for_prerequisites() the kernel reads only the segments, the output offsets,
+// the arena and the descriptor table (the segment scan and the block resolution of the
+// first batch); pools, the output and *p.err are touched only after it.  So, launched
+// with programmatic serialization after a kernel that writes none of those four inputs
+// (the gather of the previous layer), this launch's prologue overlaps that kernel's tail.
 template <int kD>
 __global__ void __launch_bounds__(kThreads, kMinCtasPerSm) gather_dequant_kernel(const Params p) {
   __shared__ uint64_t s_prefix[kThreads + 1];
   __shared__ uint64_t s_warp[kThreads / 32];
   __shared__ Item s_item[kThreads];
   __shared__ __align__(128) uint4 s_tile[kThreads / 32][32 * kUnroll];  // one output tile per warp
+  __shared__ uint32_t s_err;
 
+  allow_dependents_to_launch();
+  if (threadIdx.x == 0) s_err = 0;  // ordered before use by the scan's barriers
+  bool waited = false;
   const uint64_t G = gridDim.x, c = blockIdx.x;
   const uint32_t ntiles = static_cast<uint32_t>(((p.block_elems >> 3) + kTileChunks - 1) / kTileChunks);
   uint64_t base = 0;   // blocks before the current chunk of sequences
@@ -256,13 +277,17 @@ __global__ void __launch_bounds__(kThreads, kMinCtasPerSm) gather_dequant_kernel
           const uint32_t mid = (lo + hi) >> 1;
           if (s_prefix[mid] <= local) lo = mid; else hi = mid;
         }
-        Item it = resolve(p, chunk + lo, local - s_prefix[lo], base + s_prefix[lo]);
+        Item it = resolve(p, chunk + lo, local - s_prefix[lo], base + s_prefix[lo], &s_err);
         const uint32_t per_part = (ntiles + parts - 1) / parts;
         it.tile_begin = static_cast<uint32_t>(lq % parts) * per_part;
         it.tile_end = min(ntiles, it.tile_begin + per_part);
         s_item[threadIdx.x] = it;
       }
       __syncthreads();
+      if (!waited) {  // uniform over the CTA
+        wait_for_prerequisites();
+        waited = true;
+      }
       const uint32_t n_items =
           static_cast<uint32_t>(min(uint64_t{kThreads}, (pend - first + G - 1) / G));
       for (uint32_t k = 0; k < n_items; ++k) {
@@ -277,6 +302,11 @@ __global__ void __launch_bounds__(kThreads, kMinCtasPerSm) gather_dequant_kernel
   }
   // Shared memory must outlive the bulk stores that read it.
   if ((threadIdx.x & 31) == 0) dev::bulk_wait_all();
+  __syncthreads();
+  if (threadIdx.x == 0 && s_err != 0) {
+    if (!waited) wait_for_prerequisites();
+    atomicOr(p.err, s_err);
+  }
 }
 
 // Grid = one wave of SMs x resident CTAs (more waves measured no faster).
@@ -301,13 +331,14 @@ int grid_for() {
 }  // namespace
 }  // namespace hlkv
 
-extern "C" int hlkv_gather_dequant(const HlkvPools* pools, const HlkvLayout* layout,
-                                   const HlkvExecDescriptor* d_table, uint32_t table_size,
-                                   const uint32_t* d_arena, uint32_t arena_size,
-                                   const HlkvSegment* d_segs, uint32_t nseq, uint16_t* d_out,
-                                   const uint64_t* d_out_offsets, uint32_t* d_err,
-                                   hlkv_stream_t stream) {
+extern "C" int hlkv_gather_dequant_ex(const HlkvPools* pools, const HlkvLayout* layout,
+                                      const HlkvExecDescriptor* d_table, uint32_t table_size,
+                                      const uint32_t* d_arena, uint32_t arena_size,
+                                      const HlkvSegment* d_segs, uint32_t nseq, uint16_t* d_out,
+                                      const uint64_t* d_out_offsets, uint32_t* d_err, uint32_t flags,
+                                      hlkv_stream_t stream) {
   using namespace hlkv;
+  if ((flags & ~uint32_t{HLKV_LAUNCH_OVERLAP_PREVIOUS}) != 0) return HLKV_INVALID_ARGUMENT;
   if (pools == nullptr || !layout_ok(layout) || d_err == nullptr) return HLKV_INVALID_ARGUMENT;
   if (nseq == 0) return HLKV_OK;
   if (d_segs == nullptr || d_out == nullptr || (reinterpret_cast<uintptr_t>(d_out) & 15u) != 0) {
@@ -343,22 +374,36 @@ extern "C" int hlkv_gather_dequant(const HlkvPools* pools, const HlkvLayout* lay
   p.layout_id = layout->layout_id;
   p.rows_per_kv = layout->block_tokens * layout->kv_heads;
   const cudaStream_t s = reinterpret_cast<cudaStream_t>(stream);
+  void (*kernel)(Params) = nullptr;
   int grid = 0;
   switch (layout->head_dim) {
-    case 64:
-      grid = grid_for<64>();
-      if (grid > 0) gather_dequant_kernel<64><<<grid, kThreads, 0, s>>>(p);
-      break;
-    case 128:
-      grid = grid_for<128>();
-      if (grid > 0) gather_dequant_kernel<128><<<grid, kThreads, 0, s>>>(p);
-      break;
-    default:
-      grid = grid_for<256>();
-      if (grid > 0) gather_dequant_kernel<256><<<grid, kThreads, 0, s>>>(p);
-      break;
+    case 64: kernel = gather_dequant_kernel<64>; grid = grid_for<64>(); break;
+    case 128: kernel = gather_dequant_kernel<128>; grid = grid_for<128>(); break;
+    default: kernel = gather_dequant_kernel<256>; grid = grid_for<256>(); break;
   }
-  const cudaError_t e = cudaGetLastError();
-  if (grid <= 0) return cuda_status(e != cudaSuccess ? e : cudaErrorInvalidDevice);
-  return cuda_status(e);
+  if (grid <= 0) {
+    const cudaError_t e = cudaGetLastError();
+    return cuda_status(e != cudaSuccess ? e : cudaErrorInvalidDevice);
+  }
+  cudaLaunchConfig_t cfg{};
+  cfg.gridDim = dim3(static_cast<unsigned>(grid));
+  cfg.blockDim = dim3(kThreads);
+  cfg.dynamicSmemBytes = 0;
+  cfg.stream = s;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = (flags & HLKV_LAUNCH_OVERLAP_PREVIOUS) ? 1 : 0;
+  return cuda_status(cudaLaunchKernelEx(&cfg, kernel, p));
+}
+
+extern "C" int hlkv_gather_dequant(const HlkvPools* pools, const HlkvLayout* layout,
+                                   const HlkvExecDescriptor* d_table, uint32_t table_size,
+                                   const uint32_t* d_arena, uint32_t arena_size,
+                                   const HlkvSegment* d_segs, uint32_t nseq, uint16_t* d_out,
+                                   const uint64_t* d_out_offsets, uint32_t* d_err,
+                                   hlkv_stream_t stream) {
+  return hlkv_gather_dequant_ex(pools, layout, d_table, table_size, d_arena, arena_size, d_segs, nseq,
+                                d_out, d_out_offsets, d_err, 0u, stream);
 }

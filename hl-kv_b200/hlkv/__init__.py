@@ -39,6 +39,7 @@ ERR_NONFINITE = 1 << 9
 ERR_TOKEN_RANGE = 1 << 10
 ERR_PATCH_RANGE = 1 << 11
 ERR_OUT_ALIGN = 1 << 12
+ERR_WAIT_TIMEOUT = 1 << 13
 
 
 class Status:
@@ -131,6 +132,8 @@ SIGNATURES: list[tuple[str, object, list]] = [
     ("hlkv_last_cuda_error", _int, []),
     ("hlkv_gather_dequant", _int, [_P(Pools), _P(Layout), _vp, _u32, _vp, _u32, _vp, _u32, _vp,
                                    _vp, _vp, _vp]),
+    ("hlkv_gather_dequant_ex", _int, [_P(Pools), _P(Layout), _vp, _u32, _vp, _u32, _vp, _u32, _vp,
+                                      _vp, _vp, _u32, _vp]),
     ("hlkv_decode_attention", _int, [_P(Pools), _P(Layout), _vp, _u32, _vp, _u32, _vp, _u32, _vp,
                                      _u32, C.c_float, _vp, _vp, _vp]),
     ("hlkv_decode_attention_workspace_bytes", _sz, [_u32, _u32, _u32, _u32]),
@@ -514,14 +517,26 @@ def make_pools(pools: Mapping[int, tuple[object, int, int]]) -> Pools:
     return p
 
 
+LAUNCH_OVERLAP_PREVIOUS = 1
+
+
 def gather_dequant(pools: Pools, layout: Layout, table_ptr: int, table_size: int, arena_ptr: int,
-                   arena_size: int, segs, out, err, out_offsets=None, stream=None) -> int:
+                   arena_size: int, segs, out, err, out_offsets=None, stream=None,
+                   overlap_previous: bool = False) -> int:
     """Kernel (1).  segs: device int32 tensor [nseq, 2]; out: device 16-bit tensor; err:
-    device int32 tensor [1].  Raises on a non-OK status."""
+    device int32 tensor [1].  overlap_previous: launch with HLKV_LAUNCH_OVERLAP_PREVIOUS
+    (only after a kernel that does not write the segments, offsets, arena or table, such as
+    the previous layer's gather).  Raises on a non-OK status."""
     nseq = 0 if segs is None else int(segs.shape[0])
-    st = lib().hlkv_gather_dequant(C.byref(pools), C.byref(layout), table_ptr or None, table_size,
-                                   arena_ptr or None, arena_size, _ptr(segs), nseq, _ptr(out),
-                                   _ptr(out_offsets), _ptr(err), _stream_handle(stream))
+    if overlap_previous:
+        st = lib().hlkv_gather_dequant_ex(C.byref(pools), C.byref(layout), table_ptr or None, table_size,
+                                          arena_ptr or None, arena_size, _ptr(segs), nseq, _ptr(out),
+                                          _ptr(out_offsets), _ptr(err), LAUNCH_OVERLAP_PREVIOUS,
+                                          _stream_handle(stream))
+    else:
+        st = lib().hlkv_gather_dequant(C.byref(pools), C.byref(layout), table_ptr or None, table_size,
+                                       arena_ptr or None, arena_size, _ptr(segs), nseq, _ptr(out),
+                                       _ptr(out_offsets), _ptr(err), _stream_handle(stream))
     check(st, "hlkv_gather_dequant")
     return st
 

@@ -80,7 +80,10 @@ enum {
   HLKV_ERR_NONFINITE = 1u << 9,       /* a group with a non-finite value was skipped  */
   HLKV_ERR_TOKEN_RANGE = 1u << 10,    /* append target token >= block_tokens          */
   HLKV_ERR_PATCH_RANGE = 1u << 11,    /* delta patch target out of range              */
-  HLKV_ERR_OUT_ALIGN = 1u << 12       /* output offset not a multiple of 8 elements   */
+  HLKV_ERR_OUT_ALIGN = 1u << 12,      /* output offset not a multiple of 8 elements   */
+  HLKV_ERR_WAIT_TIMEOUT = 1u << 13    /* a bounded wait of a kernel on its own copies
+                                         ran out; that work was skipped (a safety net:
+                                         not expected to happen)                      */
 };
 
 /* ---- ABI records (byte-identical to hl::alloc, block_descriptor.hpp:137-150 and
@@ -158,6 +161,24 @@ int hlkv_gather_dequant(const HlkvPools* pools, const HlkvLayout* layout,
                         const uint32_t* d_arena, uint32_t arena_size, const HlkvSegment* d_segs,
                         uint32_t nseq, uint16_t* d_out, const uint64_t* d_out_offsets,
                         uint32_t* d_err, hlkv_stream_t stream);
+
+/*
+ * hlkv_gather_dequant with launch flags.  HLKV_LAUNCH_OVERLAP_PREVIOUS launches the gather
+ * with programmatic dependent launch: its CTAs may start while the kernel queued before it
+ * on `stream` is still running, and do the segment scan and block resolution (reads of
+ * d_segs, d_out_offsets, d_arena and d_table only) before waiting for that kernel to
+ * complete; the pools, d_out and *d_err are touched only after it.  Set the flag only when
+ * the kernel before it on the stream writes none of d_segs, d_out_offsets, d_arena and
+ * d_table -- typically the gather of the previous layer of the same cache (writing the
+ * same or another d_out is fine).  Not when it follows kernel (3) or any kernel that
+ * changes the tables.  flags == 0 is hlkv_gather_dequant.  No counterpart in the reference.
+ */
+#define HLKV_LAUNCH_OVERLAP_PREVIOUS 1u
+int hlkv_gather_dequant_ex(const HlkvPools* pools, const HlkvLayout* layout,
+                           const HlkvExecDescriptor* d_table, uint32_t table_size,
+                           const uint32_t* d_arena, uint32_t arena_size, const HlkvSegment* d_segs,
+                           uint32_t nseq, uint16_t* d_out, const uint64_t* d_out_offsets,
+                           uint32_t* d_err, uint32_t flags, hlkv_stream_t stream);
 
 /* ---- kernel (2): append-encode ---------------------------------------------------------- */
 typedef struct {
@@ -263,7 +284,12 @@ int hlkv_decode_attention_balanced(const HlkvPools* pools, const HlkvLayout* lay
  *   HLKV_NOALLOC_SCRATCH_BYTES is rejected with HLKV_BUFFER_TOO_SMALL; nothing is launched.
  * - The scratch of the current device is used (the stream must belong to it).  The first call
  *   on each device looks up the scratch's address (cudaGetSymbolAddress) and caches it; make
- *   that first call before any stream capture.
+ *   that first call before any stream capture.  The cached address belongs to the CUDA
+ *   runtime's primary context of that device: do not call cudaDeviceReset on a device after
+ *   its first call here, and do not call this entry point with another (driver-API) context
+ *   current -- the cache would then point into a destroyed or foreign context.
+ * - A grid of 2^31 CTAs or more (nseq * kv_heads * splits) returns HLKV_INVALID_ARGUMENT,
+ *   not HLKV_BUFFER_TOO_SMALL, as hlkv_decode_attention_split rejects it; nothing is launched.
  * - All calls on a device share the scratch: calls that overlap on the GPU race.  Order them
  *   (one stream, or events).
  */

@@ -260,3 +260,54 @@ def test_block_wide_scale_modes(hlkv_lib, oracle, cuda_device, T, H, D):
     decoded = sum(1 for k in range(len(ids)) if k % 3 != 2)
     per_block = out.reshape(len(ids), -1)
     assert (per_block != 0xABCD).all(axis=1).sum() >= decoded // 2
+
+
+def test_overlapped_layer_launches(hlkv_lib, oracle, cuda_device):
+    """Back-to-back per-layer gathers launched with HLKV_LAUNCH_OVERLAP_PREVIOUS (programmatic
+    dependent launch): each launch's prologue may overlap the previous layer's gather, but its
+    output writes wait for it.  Eight layers into one shared scratch (the last layer must win)
+    and into separate buffers (each layer exact), with an error-bit case in the middle layer."""
+    import torch
+    from hlkv.workload import build_workload, mixed_formats
+    layers, nseq = 8, 6
+    rows = []
+    for l in range(layers):
+        rows += mixed_formats(nseq, [5, 0, 9, 3, 17, 2], probs=(0.25, 0.3, 0.2, 0.25), seed=40 + l)
+    wl = build_workload(rows, seed=41)
+    segs = [wl.segs[l * nseq:(l + 1) * nseq] for l in range(layers)]
+    lb = [int(wl.segs_host[l * nseq:(l + 1) * nseq, 1].sum()) for l in range(layers)]
+    n = max(lb) * wl.block_elems
+    err = torch.zeros(1, dtype=torch.int32, device="cuda")
+    pools = wl.hlkv_pools()
+    shared = torch.full((n,), 0x5A5A, dtype=torch.int16, device="cuda")
+    sep = [torch.full((lb[l] * wl.block_elems,), 0x5A5A, dtype=torch.int16, device="cuda") for l in range(layers)]
+    for rep in range(3):
+        for l in range(layers):
+            hlkv_lib.gather_dequant(pools, wl.layout, wl.dt.table_ptr, wl.dt.table_size, wl.dt.arena_ptr,
+                                    wl.dt.arena_size, segs[l], shared, err, overlap_previous=True)
+        for l in range(layers):
+            hlkv_lib.gather_dequant(pools, wl.layout, wl.dt.table_ptr, wl.dt.table_size, wl.dt.arena_ptr,
+                                    wl.dt.arena_size, segs[l], sep[l], err, overlap_previous=(l > 0))
+    torch.cuda.synchronize()
+    assert int(err.item()) == 0
+    table, arena = device_table_words(wl), device_arena(wl)
+    for l in range(layers):
+        s = np.ascontiguousarray(wl.segs_host[l * nseq:(l + 1) * nseq])
+        want, oerr = oracle_gather(oracle, wl, out_elems=lb[l] * wl.block_elems, table=table, arena=arena, segs=s)
+        assert oerr == 0
+        assert_bits_equal(sep[l].cpu().numpy().view(np.uint16), want, f"layer {l}")
+        if l == layers - 1:
+            got = shared.cpu().numpy().view(np.uint16)
+            assert_bits_equal(got[:want.size], want, "shared scratch holds the last layer")
+    # A bad arena entry in the middle layer: its bit arrives through the overlapped launch.
+    bad = np.ascontiguousarray(wl.segs_host[3 * nseq:4 * nseq]).copy()
+    bad[0, 0] = wl.dt.arena_size  # the first sequence's 5 blocks lie past the arena (same total)
+    bad_t = torch.from_numpy(bad.astype(np.int32)).cuda()
+    err.zero_()
+    torch.cuda.synchronize()
+    hlkv_lib.gather_dequant(pools, wl.layout, wl.dt.table_ptr, wl.dt.table_size, wl.dt.arena_ptr,
+                            wl.dt.arena_size, segs[2], shared, err, overlap_previous=False)
+    hlkv_lib.gather_dequant(pools, wl.layout, wl.dt.table_ptr, wl.dt.table_size, wl.dt.arena_ptr,
+                            wl.dt.arena_size, bad_t, shared, err, overlap_previous=True)
+    torch.cuda.synchronize()
+    assert int(err.item()) == hlkv_lib.ERR_ARENA_RANGE
