@@ -39,7 +39,6 @@ ERR_NONFINITE = 1 << 9
 ERR_TOKEN_RANGE = 1 << 10
 ERR_PATCH_RANGE = 1 << 11
 ERR_OUT_ALIGN = 1 << 12
-ERR_WAIT_TIMEOUT = 1 << 13
 
 
 class Status:

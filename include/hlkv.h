@@ -80,10 +80,7 @@ enum {
   HLKV_ERR_NONFINITE = 1u << 9,       /* a group with a non-finite value was skipped  */
   HLKV_ERR_TOKEN_RANGE = 1u << 10,    /* append target token >= block_tokens          */
   HLKV_ERR_PATCH_RANGE = 1u << 11,    /* delta patch target out of range              */
-  HLKV_ERR_OUT_ALIGN = 1u << 12,      /* output offset not a multiple of 8 elements   */
-  HLKV_ERR_WAIT_TIMEOUT = 1u << 13    /* a bounded wait of a kernel on its own copies
-                                         ran out; that work was skipped (a safety net:
-                                         not expected to happen)                      */
+  HLKV_ERR_OUT_ALIGN = 1u << 12       /* output offset not a multiple of 8 elements   */
 };
 
 /* ---- ABI records (byte-identical to hl::alloc, block_descriptor.hpp:137-150 and
