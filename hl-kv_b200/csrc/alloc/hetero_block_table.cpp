@@ -507,6 +507,15 @@ Status HeteroBlockTable::build_exec_table(std::span<const SequenceHandle> seqs, 
   return Status::kOk;
 }
 
+Status HeteroBlockTable::compact_arena(std::vector<SegmentMove>& moves) {
+  std::vector<IdArena::Segment*> live;
+  live.reserve(seq_records_.size());
+  for (SeqRecord& q : seq_records_) {
+    if (q.live) live.push_back(&q.seg);
+  }
+  return arena_.compact(live, moves);
+}
+
 // ---- device-facing state -----------------------------------------------------------------
 
 Status HeteroBlockTable::batch_segments(std::span<const SequenceHandle> seqs,

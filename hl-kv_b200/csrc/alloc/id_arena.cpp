@@ -10,6 +10,7 @@
 #include "hl_allocator/id_arena.hpp"
 #include "hl_allocator/snapshot_io.hpp"
 
+#include <algorithm>
 #include <bit>
 #include <cassert>
 
@@ -105,6 +106,45 @@ void IdArena::collect(std::vector<IdPatch>& out) {
   out.resize(changed_.size());  // the only allocation, before the queue is touched
   std::size_t k = 0;
   changed_.drain([&](std::uint32_t off) noexcept { out[k++] = IdPatch{off, entry_[off]}; });
+}
+
+Status IdArena::compact(std::span<Segment* const> live, std::vector<SegmentMove>& moves) {
+  if (changed_.size() != 0) return Status::kInvalidState;
+  // Everything is built aside first; the swap at the end cannot fail.
+  std::vector<Segment*> order;
+  order.reserve(live.size());
+  std::uint64_t total = 0;
+  for (Segment* seg : live) {
+    if (seg->capacity == 0) continue;
+    order.push_back(seg);
+    total += seg->capacity;
+  }
+  std::sort(order.begin(), order.end(), [](const Segment* a, const Segment* b) { return a->offset < b->offset; });
+  std::vector<std::uint32_t> packed(total, 0u);
+  std::vector<std::uint32_t> links(total / kMinSegment, kNone);
+  std::vector<std::uint32_t> offsets(order.size());
+  std::vector<SegmentMove> out;
+  out.reserve(order.size());
+  std::uint64_t at = 0, scratch = 0;
+  for (std::size_t k = 0; k < order.size(); ++k) {
+    const Segment& seg = *order[k];
+    std::copy_n(entry_.begin() + seg.offset, seg.length, packed.begin() + static_cast<std::ptrdiff_t>(at));
+    if (at != seg.offset && seg.length != 0) {
+      out.push_back(SegmentMove{seg.offset, static_cast<std::uint32_t>(at), seg.length,
+                                static_cast<std::uint32_t>(scratch)});
+      scratch += (seg.length + 7u) & ~7u;  // 8-entry units keep every copy 32-byte aligned
+    }
+    offsets[k] = static_cast<std::uint32_t>(at);
+    at += seg.capacity;
+  }
+  if (scratch > kMaxEntries) return Status::kCapacityExceeded;
+  for (std::size_t k = 0; k < order.size(); ++k) order[k]->offset = offsets[k];
+  entry_.swap(packed);
+  next_free_.swap(links);
+  free_top_ = no_free_segments();
+  free_len_ = {};
+  moves.swap(out);
+  return Status::kOk;
 }
 
 std::uint64_t IdArena::free_entries() const noexcept {

@@ -28,6 +28,8 @@ struct hlkv_device_tables {
 static_assert(sizeof(HlkvExecDescriptor) == sizeof(BlockExecDescriptor));
 static_assert(sizeof(HlkvIdPatch) == sizeof(IdPatch));
 static_assert(sizeof(HlkvSegment) == sizeof(SequenceSegment));
+static_assert(sizeof(HlkvSegmentMove) == sizeof(SegmentMove) && offsetof(HlkvSegmentMove, scratch) ==
+                                                                    offsetof(SegmentMove, scratch));
 static_assert(sizeof(HlkvHandle) == sizeof(SequenceHandle) && offsetof(HlkvHandle, generation) ==
                                                                   offsetof(SequenceHandle, generation));
 static_assert(sizeof(HlkvAppendTarget) == sizeof(TokenTarget) &&
@@ -297,6 +299,24 @@ int hlkv_table_collect_delta(hlkv_table* t, HlkvExecDescriptor* desc, size_t des
   return HLKV_STATUS_OK;
 }
 
+int hlkv_table_compact_arena(hlkv_table* t, HlkvSegmentMove* out, size_t cap, size_t* n_moves) {
+  // A compaction makes at most one move per live sequence: check the room before changing
+  // anything.
+  const std::uint32_t live = t->t.stats().active_sequences;
+  if (n_moves != nullptr) *n_moves = 0;
+  if (cap < live || (live > 0 && out == nullptr)) return HLKV_STATUS_INVALID_ARGUMENT;
+  try {
+    std::vector<SegmentMove> moves;
+    const Status s = t->t.compact_arena(moves);
+    if (s != Status::kOk) return st(s);
+    if (!moves.empty()) std::memcpy(out, moves.data(), moves.size() * sizeof(SegmentMove));
+    if (n_moves != nullptr) *n_moves = moves.size();
+    return HLKV_STATUS_OK;
+  } catch (const std::bad_alloc&) {
+    return HLKV_STATUS_CAPACITY_EXCEEDED;
+  }
+}
+
 HlkvExecDescriptor hlkv_table_device_descriptor(const hlkv_table* t, uint32_t block_id) {
   return out_of(t->t.device_descriptor(block_id));
 }
@@ -359,6 +379,21 @@ int hlkv_device_tables_collect(hlkv_device_tables* dt, hlkv_table* t) {
   } catch (const std::bad_alloc&) {
     return HLKV_BUFFER_TOO_SMALL;
   }
+}
+
+int hlkv_device_tables_relocate(hlkv_device_tables* dt, const HlkvSegmentMove* moves, size_t n,
+                                uint32_t new_arena_size, hlkv_stream_t stream) {
+  if (dt == nullptr || (n > 0 && moves == nullptr) || n > 0xFFFFFFFFu) return HLKV_INVALID_ARGUMENT;
+  try {
+    const std::span<const SegmentMove> mv(reinterpret_cast<const SegmentMove*>(moves), n);
+    return static_cast<int>(dt->dt.relocate(mv, new_arena_size, reinterpret_cast<cudaStream_t>(stream)).status);
+  } catch (const std::bad_alloc&) {
+    return HLKV_BUFFER_TOO_SMALL;
+  }
+}
+
+uint64_t hlkv_device_tables_arena_capacity_bytes(const hlkv_device_tables* dt) {
+  return dt->dt.arena_capacity_bytes();
 }
 
 int hlkv_device_tables_flush(hlkv_device_tables* dt, hlkv_stream_t stream) {

@@ -1,10 +1,13 @@
 // hl::kv::DeviceTables (include/hl_kv/device_tables.hpp).
 #include "hl_kv/device_tables.hpp"
 
+#include <cuda.h>  // types of the virtual memory management calls (reached at run time)
 #include <cuda_runtime_api.h>
 
 #include <cstring>
+#include <mutex>
 #include <unordered_map>
+#include <vector>
 
 #include "hlkv.h"
 
@@ -14,6 +17,8 @@ int launch_apply_delta(uint4* table, uint32_t table_size, uint32_t* arena, uint3
                        const uint4* desc, uint32_t n_desc, const uint2* ids, uint32_t n_id,
                        const uint2* copy_src, uint2* copy_dst, uint32_t n_copy, uint32_t* err,
                        cudaStream_t s);
+int launch_relocate(uint32_t* arena, uint32_t arena_size, const HlkvSegmentMove* moves, uint32_t n,
+                    uint32_t* scratch, uint64_t scratch_entries, uint32_t* err, cudaStream_t s);
 }
 
 namespace hl::kv {
@@ -51,7 +56,140 @@ class DeviceGuard {
   bool restore_ = false;
 };
 
+// The driver's virtual memory management calls, looked up once through the runtime
+// (cudaGetDriverEntryPoint), so the library needs no link-time dependency on the driver.
+struct VmmCalls {
+  CUresult (*granularity)(size_t*, const CUmemAllocationProp*, CUmemAllocationGranularity_flags) = nullptr;
+  CUresult (*reserve)(CUdeviceptr*, size_t, size_t, CUdeviceptr, unsigned long long) = nullptr;
+  CUresult (*release_range)(CUdeviceptr, size_t) = nullptr;
+  CUresult (*create)(CUmemGenericAllocationHandle*, size_t, const CUmemAllocationProp*, unsigned long long) = nullptr;
+  CUresult (*release)(CUmemGenericAllocationHandle) = nullptr;
+  CUresult (*map)(CUdeviceptr, size_t, size_t, CUmemGenericAllocationHandle, unsigned long long) = nullptr;
+  CUresult (*unmap)(CUdeviceptr, size_t) = nullptr;
+  CUresult (*set_access)(CUdeviceptr, size_t, const CUmemAccessDesc*, size_t) = nullptr;
+  bool ok = false;
+};
+
+const VmmCalls& vmm() {
+  static VmmCalls calls;
+  static std::once_flag once;
+  std::call_once(once, [] {
+    auto get = [](const char* name, auto& fn) {
+      void* p = nullptr;
+      cudaDriverEntryPointQueryResult found{};
+      if (cudaGetDriverEntryPoint(name, &p, cudaEnableDefault, &found) != cudaSuccess ||
+          found != cudaDriverEntryPointSuccess || p == nullptr) {
+        return false;
+      }
+      fn = reinterpret_cast<std::remove_reference_t<decltype(fn)>>(p);
+      return true;
+    };
+    calls.ok = get("cuMemGetAllocationGranularity", calls.granularity) && get("cuMemAddressReserve", calls.reserve) &&
+               get("cuMemAddressFree", calls.release_range) && get("cuMemCreate", calls.create) &&
+               get("cuMemRelease", calls.release) && get("cuMemMap", calls.map) && get("cuMemUnmap", calls.unmap) &&
+               get("cuMemSetAccess", calls.set_access);
+  });
+  return calls;
+}
+
 }  // namespace
+
+// The arena's device storage under virtual memory management: one address range
+// reserved for the largest possible arena (2^32 - 1 entries), backed from its start by
+// physical chunks mapped as the arena grows and unmapped from its end when it shrinks.
+// Every mapped byte belongs to the arena, and kernels never read past the arena's size,
+// which is at most the mapped size.
+struct DeviceTables::ArenaSpace {
+  CUdeviceptr base = 0;
+  size_t reserved = 0;
+  size_t granularity = 0;
+  size_t mapped = 0;
+  int device = 0;
+  struct Chunk {
+    CUmemGenericAllocationHandle handle;
+    size_t bytes;
+  };
+  std::vector<Chunk> chunks;
+
+  CUmemAllocationProp prop() const {
+    CUmemAllocationProp p{};
+    p.type = CU_MEM_ALLOCATION_TYPE_PINNED;
+    p.location.type = CU_MEM_LOCATION_TYPE_DEVICE;
+    p.location.id = device;
+    return p;
+  }
+
+  // Reserves the range; false (nothing held) when the driver cannot.
+  bool open(int dev) {
+    const VmmCalls& v = vmm();
+    if (!v.ok) return false;
+    device = dev;
+    const CUmemAllocationProp p = prop();
+    if (v.granularity(&granularity, &p, CU_MEM_ALLOC_GRANULARITY_MINIMUM) != CUDA_SUCCESS || granularity == 0) {
+      return false;
+    }
+    const size_t want = size_t{0xFFFFFFFFull} * sizeof(std::uint32_t);
+    reserved = (want + granularity - 1) / granularity * granularity;
+    // Aligned to the granularity, so that every chunk maps at an aligned address.
+    if (v.reserve(&base, reserved, granularity, 0, 0) != CUDA_SUCCESS) {
+      base = 0;
+      return false;
+    }
+    return true;
+  }
+
+  // Maps chunks at the end of the mapped part until at least `bytes` are mapped.
+  bool grow(size_t bytes) {
+    const VmmCalls& v = vmm();
+    if (bytes > reserved) return false;
+    while (mapped < bytes) {
+      // Pieces of about an eighth of what is mapped (at least one granule, at most 256 MiB):
+      // few map calls as the arena grows, and fine enough for trim() to give most of it back.
+      size_t chunk = mapped / 8;
+      if (chunk > (size_t{256} << 20)) chunk = size_t{256} << 20;
+      chunk = (chunk + granularity - 1) / granularity * granularity;
+      if (chunk < granularity) chunk = granularity;
+      if (mapped + chunk > reserved) chunk = reserved - mapped;
+      const CUmemAllocationProp p = prop();
+      CUmemGenericAllocationHandle h{};
+      if (v.create(&h, chunk, &p, 0) != CUDA_SUCCESS) return false;
+      if (v.map(base + mapped, chunk, 0, h, 0) != CUDA_SUCCESS) {
+        (void)v.release(h);
+        return false;
+      }
+      CUmemAccessDesc access{};
+      access.location.type = CU_MEM_LOCATION_TYPE_DEVICE;
+      access.location.id = device;
+      access.flags = CU_MEM_ACCESS_FLAGS_PROT_READWRITE;
+      if (v.set_access(base + mapped, chunk, &access, 1) != CUDA_SUCCESS) {
+        (void)v.unmap(base + mapped, chunk);
+        (void)v.release(h);
+        return false;
+      }
+      chunks.push_back(Chunk{h, chunk});
+      mapped += chunk;
+    }
+    return true;
+  }
+
+  // Unmaps whole chunks from the end while at least `keep` bytes stay mapped.  The
+  // caller has made sure that no queued work reads the unmapped part.
+  void trim(size_t keep) {
+    const VmmCalls& v = vmm();
+    while (!chunks.empty() && mapped - chunks.back().bytes >= keep) {
+      const Chunk c = chunks.back();
+      chunks.pop_back();
+      mapped -= c.bytes;
+      (void)v.unmap(base + mapped, c.bytes);
+      (void)v.release(c.handle);
+    }
+  }
+
+  ~ArenaSpace() {
+    trim(0);
+    if (base != 0) (void)vmm().release_range(base, reserved);
+  }
+};
 
 DeviceTables::DeviceTables() { (void)cudaGetDevice(&device_); }
 
@@ -64,8 +202,12 @@ DeviceTables::~DeviceTables() {
   // The owner must not destroy the tables while kernels that read them are
   // queued; a device-wide sync makes the frees below safe regardless.
   (void)cudaDeviceSynchronize();
+  if (moves_free_ != nullptr) (void)cudaEventDestroy(moves_free_);
   if (d_table_ != nullptr) (void)cudaFree(d_table_);
-  if (d_arena_ != nullptr) (void)cudaFree(d_arena_);
+  if (space_ == nullptr && d_arena_ != nullptr) (void)cudaFree(d_arena_);
+  space_.reset();
+  if (d_scratch_ != nullptr) (void)cudaFree(d_scratch_);
+  if (h_moves_ != nullptr) (void)cudaFreeHost(h_moves_);
   if (d_err_ != nullptr) (void)cudaFree(d_err_);
   if (d_staging_ != nullptr) (void)cudaFree(d_staging_);
   if (h_staging_ != nullptr) (void)cudaFreeHost(h_staging_);
@@ -203,28 +345,7 @@ DeviceStatus DeviceTables::upload_and_apply(const alloc::ExecDelta& delta, cudaS
     table_size_ = delta.descriptor_table_size;
   }
   if (delta.arena_size > arena_capacity_) {
-    // Room for a quarter more than asked, and at least double the old capacity, so that
-    // growth (an allocation, a copy and a stream drain) stays rare.
-    std::uint64_t cap = arena_capacity_ == 0 ? 1024 : 2ull * arena_capacity_;
-    const std::uint64_t want = std::uint64_t{delta.arena_size} + delta.arena_size / 4;
-    if (cap < want) cap = want;
-    if (cap > 0xFFFFFFFFull) cap = 0xFFFFFFFFull;
-    std::uint32_t* fresh = nullptr;
-    if (const cudaError_t e = device_alloc(&fresh, cap * 4); e != cudaSuccess) return from_cuda(e);
-    if (d_arena_ != nullptr) {
-      // Keep the contents (the protocol grows the arena, it never rewrites it).
-      if (const cudaError_t e = cudaMemcpyAsync(fresh, d_arena_, std::size_t{arena_size_} * 4,
-                                                cudaMemcpyDeviceToDevice, stream);
-          e != cudaSuccess) {
-        (void)cudaFree(fresh);
-        return from_cuda(e);
-      }
-      // The old buffer may still be read by queued kernels on this stream.
-      if (const cudaError_t e = cudaStreamSynchronize(stream); e != cudaSuccess) return from_cuda(e);
-      (void)cudaFree(d_arena_);
-    }
-    d_arena_ = fresh;
-    arena_capacity_ = static_cast<std::uint32_t>(cap);
+    if (DeviceStatus st = grow_arena(delta.arena_size, stream); !st.ok()) return st;
   }
   arena_size_ = delta.arena_size;
 
@@ -265,6 +386,113 @@ DeviceStatus DeviceTables::upload_and_apply(const alloc::ExecDelta& delta, cudaS
   }
   // The staging buffers are free again once kernel (3) has read them.
   if (const cudaError_t e = cudaEventRecord(staging_free_, stream); e != cudaSuccess) return from_cuda(e);
+  return {};
+}
+
+DeviceStatus DeviceTables::grow_arena(std::uint32_t entries, cudaStream_t stream) {
+  // Room for a quarter more than asked, and at least double the old capacity, so that
+  // growth stays rare.
+  std::uint64_t cap = arena_capacity_ == 0 ? 1024 : 2ull * arena_capacity_;
+  const std::uint64_t want = std::uint64_t{entries} + entries / 4;
+  if (cap < want) cap = want;
+  if (cap > 0xFFFFFFFFull) cap = 0xFFFFFFFFull;
+  if (!space_tried_) {
+    space_tried_ = true;
+    auto space = std::make_unique<ArenaSpace>();
+    if (d_arena_ == nullptr && space->open(device_)) space_ = std::move(space);
+  }
+  if (space_ != nullptr) {
+    // Map more memory behind the same address: no copy, queued kernels keep reading the
+    // part that is already mapped.
+    if (!space_->grow(static_cast<size_t>(cap) * sizeof(std::uint32_t))) return from_cuda(cudaErrorMemoryAllocation);
+    d_arena_ = reinterpret_cast<std::uint32_t*>(space_->base);
+    const std::uint64_t mapped_entries = space_->mapped / sizeof(std::uint32_t);
+    arena_capacity_ = static_cast<std::uint32_t>(mapped_entries > 0xFFFFFFFFull ? 0xFFFFFFFFull : mapped_entries);
+    return {};
+  }
+  std::uint32_t* fresh = nullptr;
+  if (const cudaError_t e = device_alloc(&fresh, cap * 4); e != cudaSuccess) return from_cuda(e);
+  if (d_arena_ != nullptr) {
+    // Keep the contents (the protocol grows the arena, it never rewrites it).
+    if (const cudaError_t e = cudaMemcpyAsync(fresh, d_arena_, std::size_t{arena_size_} * 4,
+                                              cudaMemcpyDeviceToDevice, stream);
+        e != cudaSuccess) {
+      (void)cudaFree(fresh);
+      return from_cuda(e);
+    }
+    // The old buffer may still be read by queued kernels on this stream.
+    if (const cudaError_t e = cudaStreamSynchronize(stream); e != cudaSuccess) return from_cuda(e);
+    (void)cudaFree(d_arena_);
+  }
+  d_arena_ = fresh;
+  arena_capacity_ = static_cast<std::uint32_t>(cap);
+  return {};
+}
+
+DeviceStatus DeviceTables::relocate(std::span<const alloc::SegmentMove> moves, std::uint32_t new_arena_size,
+                                    cudaStream_t stream) {
+  if (DeviceStatus st = flush(stream); !st.ok()) return st;
+  DeviceGuard g(device_);
+  if (!g.ok()) return from_cuda(cudaErrorInvalidDevice);
+  if (DeviceStatus st = ensure_error_word(stream); !st.ok()) return st;
+  if (!moves.empty()) {
+    if (d_arena_ == nullptr) return from_cuda(cudaErrorInvalidValue);
+    const std::uint64_t need = alloc::IdArena::scratch_entries(moves);
+    if (need > scratch_entries_) {
+      if (d_scratch_ != nullptr) {
+        if (const cudaError_t e = cudaStreamSynchronize(stream); e != cudaSuccess) return from_cuda(e);
+        (void)cudaFree(d_scratch_);
+      }
+      d_scratch_ = nullptr;
+      scratch_entries_ = 0;
+      if (const cudaError_t e = device_alloc(&d_scratch_, need * sizeof(std::uint32_t)); e != cudaSuccess) {
+        d_scratch_ = nullptr;
+        return from_cuda(e);
+      }
+      scratch_entries_ = need;
+    }
+    const std::size_t bytes = moves.size() * sizeof(alloc::SegmentMove);
+    if (moves_free_ == nullptr) {
+      if (const cudaError_t e = cudaEventCreateWithFlags(&moves_free_, cudaEventDisableTiming); e != cudaSuccess) {
+        moves_free_ = nullptr;
+        return from_cuda(e);
+      }
+    } else if (const cudaError_t e = cudaEventSynchronize(moves_free_); e != cudaSuccess) {
+      return from_cuda(e);  // the previous relocation has read the staged moves
+    }
+    if (bytes > h_moves_bytes_) {
+      if (h_moves_ != nullptr) (void)cudaFreeHost(h_moves_);
+      h_moves_ = nullptr;
+      h_moves_bytes_ = 0;
+      if (const cudaError_t e = cudaMallocHost(&h_moves_, bytes); e != cudaSuccess) {
+        h_moves_ = nullptr;
+        return from_cuda(e);
+      }
+      h_moves_bytes_ = bytes;
+    }
+    std::memcpy(h_moves_, moves.data(), bytes);
+    cudaPointerAttributes attr{};
+    if (const cudaError_t e = cudaPointerGetAttributes(&attr, h_moves_); e != cudaSuccess) return from_cuda(e);
+    const int rs = hlkv::launch_relocate(d_arena_, arena_size_, static_cast<const HlkvSegmentMove*>(attr.devicePointer),
+                                         static_cast<std::uint32_t>(moves.size()), d_scratch_, scratch_entries_,
+                                         d_err_, stream);
+    if (rs != HLKV_OK) {
+      return DeviceStatus{static_cast<quant::QuantStatus>(rs), static_cast<cudaError_t>(hlkv_last_cuda_error())};
+    }
+    if (const cudaError_t e = cudaEventRecord(moves_free_, stream); e != cudaSuccess) return from_cuda(e);
+  }
+  arena_size_ = new_arena_size;
+  // Give back mapped memory beyond a quarter of headroom, once nothing queued can read it.
+  if (space_ != nullptr) {
+    const std::uint64_t keep_entries = std::uint64_t{new_arena_size} + new_arena_size / 4;
+    const size_t keep = static_cast<size_t>(keep_entries) * sizeof(std::uint32_t);
+    if (space_->mapped > keep + space_->granularity) {
+      if (const cudaError_t e = cudaDeviceSynchronize(); e != cudaSuccess) return from_cuda(e);
+      space_->trim(keep);
+      const std::uint64_t mapped_entries = space_->mapped / sizeof(std::uint32_t);
+      arena_capacity_ = static_cast<std::uint32_t>(mapped_entries > 0xFFFFFFFFull ? 0xFFFFFFFFull : mapped_entries);
+    }
+  }
   return {};
 }
 

@@ -195,6 +195,11 @@ SIGNATURES: list[tuple[str, object, list]] = [
     ("hlkv_device_tables_collect", _int, [_vp, _vp]),
     ("hlkv_device_tables_flush", _int, [_vp, _vp]),
     ("hlkv_decode_step_queue", _int, [_vp, _P(Pools), _P(Layout), _vp, _vp, _u32, _vp, _vp, _vp, _vp]),
+    ("hlkv_table_compact_arena", _int, [_vp, _vp, _sz, _P(_sz)]),
+    ("hlkv_segment_moves_scratch_entries", _u64, [_vp, _sz]),
+    ("hlkv_arena_relocate", _int, [_vp, _u32, _vp, _u32, _vp, _u64, _vp, _vp]),
+    ("hlkv_device_tables_relocate", _int, [_vp, _vp, _sz, _u32, _vp]),
+    ("hlkv_device_tables_arena_capacity_bytes", _u64, [_vp]),
     ("hlkv_device_tables_table", _vp, [_vp]),
     ("hlkv_device_tables_table_size", _u32, [_vp]),
     ("hlkv_device_tables_arena", _vp, [_vp]),
@@ -435,6 +440,16 @@ class Table:
             raise HlkvError(f"collect_delta: status {st}")
         return Delta(desc[: a.value], ids[: b.value], ts.value, ar.value)
 
+    def compact_arena(self):
+        """HeteroBlockTable::compact_arena.  Returns (status, moves: uint32 [n, 4] of
+        {from, to, length, scratch}); nothing changes on a non-OK status."""
+        import numpy as np
+        live = self.stats()["active_sequences"]
+        moves = np.zeros((max(live, 1), 4), dtype=np.uint32)
+        n = _sz()
+        st = lib().hlkv_table_compact_arena(self.h, moves.ctypes.data, moves.shape[0], C.byref(n))
+        return st, moves[: n.value].copy()
+
     def device_descriptor(self, block_id: int) -> tuple[int, int, int, int]:
         d = lib().hlkv_table_device_descriptor(self.h, block_id)
         return (d.slot, d.info, d.scale_ref, d.block_id)
@@ -492,6 +507,16 @@ class DeviceTables:
     def flush(self, stream=None) -> None:
         """Device half of sync(): uploads and applies the collected changes on `stream`."""
         check(lib().hlkv_device_tables_flush(self.h, _stream_handle(stream)), "device_tables_flush")
+
+    def relocate(self, moves, new_arena_size: int, stream=None) -> None:
+        """Applies an arena compaction (moves from Table.compact_arena) to the device arena."""
+        import numpy as np
+        m = np.ascontiguousarray(moves, dtype=np.uint32).reshape(-1, 4)
+        check(lib().hlkv_device_tables_relocate(self.h, m.ctypes.data if m.size else None, m.shape[0],
+                                                new_arena_size, _stream_handle(stream)), "device_tables_relocate")
+
+    @property
+    def arena_capacity_bytes(self) -> int: return lib().hlkv_device_tables_arena_capacity_bytes(self.h)
 
     @property
     def table_ptr(self) -> int: return lib().hlkv_device_tables_table(self.h) or 0

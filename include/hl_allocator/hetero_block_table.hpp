@@ -174,6 +174,15 @@ class HeteroBlockTable {
   [[nodiscard]] Status build_exec_table(std::span<const SequenceHandle> seqs,
                                         ExecTable& out) const;
 
+  /// Packs the id arena (IdArena::compact over every live sequence's segment): the
+  /// storage a burst of long sequences left behind is given back and the live segments
+  /// become contiguous.  `moves` receives the segment moves the device copy of the arena
+  /// must make before any later delta is applied (hlkv_device_tables_relocate).  Sequence
+  /// contents and handles are unchanged; batch_segments() reports the new offsets.
+  /// kInvalidState while id patches are pending: collect the delta first.  No counterpart
+  /// in the reference.
+  [[nodiscard]] Status compact_arena(std::vector<SegmentMove>& moves);
+
   // -- device-facing state -----------------------------------------------------------
   [[nodiscard]] Status batch_segments(std::span<const SequenceHandle> seqs,
                                       std::vector<SequenceSegment>& out) const;

@@ -36,6 +36,17 @@ struct IdPatch {
   friend constexpr bool operator==(IdPatch, IdPatch) noexcept = default;
 };
 
+/// A live segment's move in an arena compaction: entries [from, from + length) go to
+/// [to, to + length).  `scratch` places the segment in a relocation scratch buffer
+/// (moves are made in two phases through it; see IdArena::compact).
+struct SegmentMove {
+  std::uint32_t from;
+  std::uint32_t to;
+  std::uint32_t length;
+  std::uint32_t scratch;
+  friend constexpr bool operator==(SegmentMove, SegmentMove) noexcept = default;
+};
+
 /// What a kernel needs per sequence: block ids arena[offset .. offset + length).
 struct SequenceSegment {
   std::uint32_t offset;
@@ -75,6 +86,22 @@ class IdArena {
   [[nodiscard]] static SequenceSegment kernel_view(const Segment& seg) noexcept {
     return seg.capacity == 0 ? SequenceSegment{0u, seg.length}
                              : SequenceSegment{seg.offset, seg.length};
+  }
+
+  /// Packs the `live` segments (every segment that holds storage) to the front of the
+  /// arena in their current offset order, each keeping its capacity; empties the free
+  /// stacks and shrinks the arena to the packed size.  Each segment's offset is updated;
+  /// `moves` receives the moves a device copy must make (segments that hold entries and
+  /// whose offset changed), in increasing offset order, with scratch offsets packed in
+  /// 8-entry units (scratch_entries() of them in all).  Nothing is queued for patching:
+  /// the device copy makes the same moves.  kInvalidState, nothing changed, while
+  /// patches are pending (collect() first), since they name pre-compaction offsets.
+  /// Strong guarantee.  No counterpart in the reference, whose arena never compacts
+  /// (hl_allocator_abi.md, section 9, item 5).
+  [[nodiscard]] Status compact(std::span<Segment* const> live, std::vector<SegmentMove>& moves);
+  /// Entries of relocation scratch that `moves` needs.
+  [[nodiscard]] static std::uint64_t scratch_entries(std::span<const SegmentMove> moves) noexcept {
+    return moves.empty() ? 0 : std::uint64_t{moves.back().scratch} + ((moves.back().length + 7u) & ~7u);
   }
 
   /// Replaces `out` with one patch per changed entry (first change first) and empties the queue.

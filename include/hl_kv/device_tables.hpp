@@ -7,10 +7,14 @@
 // host (tests/project1/exec_mirror.hpp).  Here sync() runs it for real, in
 // stream order on the caller's stream:
 //   1. table.collect_delta() on the host;
-//   2. grow the device arena when delta.arena_size exceeds its capacity (a
-//      larger allocation with a quarter to spare, the old contents copied
-//      device-to-device, then the old buffer freed after the stream drains);
-//      the descriptor table is allocated once at max_blocks entries;
+//   2. grow the device arena when delta.arena_size exceeds its capacity.  The
+//      arena lives in a reserved virtual address range (CUDA virtual memory
+//      management, reached through the runtime's driver entry points): growth
+//      maps more device memory behind the same address, with a quarter to
+//      spare -- no copy, no stream drain, and the arena pointer never changes.
+//      Where the driver offers no virtual memory management, growth falls back
+//      to a larger allocation, a device-to-device copy and a stream drain.  The
+//      descriptor table is allocated once at max_blocks entries;
 //   3. copy the patches into pinned staging;
 //   4. run kernel (3) (hlkv_apply_delta), which reads the staged patches in
 //      place: under unified addressing a kernel reads page-locked host memory
@@ -24,6 +28,8 @@
 #include <cuda_runtime_api.h>
 
 #include <cstdint>
+#include <memory>
+#include <span>
 
 #include "hl_allocator/hetero_block_table.hpp"
 #include "hl_quant/cuda_dequant.hpp"
@@ -57,6 +63,17 @@ class DeviceTables {
                                    std::uint32_t n_copy);
   /// Uploads and applies an already collected delta.
   [[nodiscard]] DeviceStatus apply(const alloc::ExecDelta& delta, cudaStream_t stream);
+  /// Applies an arena compaction (HeteroBlockTable::compact_arena) on `stream`: flushes
+  /// what collect() gathered, makes the segment moves (two launches through a scratch
+  /// buffer), sets the arena size to new_arena_size and, when more than a quarter of
+  /// headroom above it is mapped, waits for the device to go idle and unmaps the rest.
+  /// No counterpart in the reference.
+  [[nodiscard]] DeviceStatus relocate(std::span<const alloc::SegmentMove> moves, std::uint32_t new_arena_size,
+                                      cudaStream_t stream);
+  /// Device memory behind the arena, in bytes.
+  [[nodiscard]] std::uint64_t arena_capacity_bytes() const noexcept {
+    return std::uint64_t{arena_capacity_} * sizeof(std::uint32_t);
+  }
 
   [[nodiscard]] const alloc::BlockExecDescriptor* table() const noexcept { return d_table_; }
   [[nodiscard]] std::uint32_t table_size() const noexcept { return table_size_; }
@@ -73,6 +90,16 @@ class DeviceTables {
   [[nodiscard]] DeviceStatus launch(const void* desc, std::uint32_t n_desc, const void* ids, std::uint32_t n_id,
                                     const void* copy_src, void* copy_dst, std::uint32_t n_copy,
                                     cudaStream_t stream);
+  [[nodiscard]] DeviceStatus grow_arena(std::uint32_t entries, cudaStream_t stream);
+
+  struct ArenaSpace;                     // the reserved address range and its mapped chunks
+  std::unique_ptr<ArenaSpace> space_;    // null: no virtual memory management (plain allocation)
+  bool space_tried_ = false;
+  std::uint32_t* d_scratch_ = nullptr;   // relocation scratch
+  std::uint64_t scratch_entries_ = 0;
+  void* h_moves_ = nullptr;              // pinned staging of relocation moves
+  std::size_t h_moves_bytes_ = 0;
+  cudaEvent_t moves_free_ = nullptr;     // recorded after the relocation reads the moves
 
   int device_ = 0;
   alloc::BlockExecDescriptor* d_table_ = nullptr;

@@ -214,6 +214,35 @@ int hlkv_apply_delta(HlkvExecDescriptor* d_table, uint32_t table_size, uint32_t*
                      uint32_t n_desc, const HlkvIdPatch* d_id_patches, uint32_t n_id,
                      uint32_t* d_err, hlkv_stream_t stream);
 
+/* ---- arena relocation ------------------------------------------------------------------- */
+/* A live segment's move in an arena compaction (hl::alloc::SegmentMove): entries
+ * [from, from + length) go to [to, to + length) through scratch[scratch ...].  from, to and
+ * scratch are multiples of 8 entries. */
+typedef struct {
+  uint32_t from;
+  uint32_t to;
+  uint32_t length;
+  uint32_t scratch;
+} HlkvSegmentMove;
+
+/* Scratch entries (uint32) that a compaction's moves need: the last move's scratch offset
+ * plus its length rounded up to 8 (0 for no moves). */
+uint64_t hlkv_segment_moves_scratch_entries(const HlkvSegmentMove* moves, size_t n);
+
+/*
+ * Makes the moves of hlkv_table_compact_arena on a device copy of the arena, in stream
+ * order: a first launch gathers every moved segment into d_scratch (at least
+ * hlkv_segment_moves_scratch_entries entries), a second scatters it to its new offset, so
+ * overlapping moves are safe.  arena_size is the device arena's current (pre-compaction)
+ * size.  `moves` must be device-readable (device or page-locked host memory) and 16-byte
+ * aligned, as must d_arena and d_scratch.  Apply it before any delta collected after the
+ * compaction.  A move outside the arena or the scratch is skipped with
+ * HLKV_ERR_PATCH_RANGE.  No counterpart in the reference, whose arena never compacts.
+ */
+int hlkv_arena_relocate(uint32_t* d_arena, uint32_t arena_size, const HlkvSegmentMove* moves,
+                        uint32_t n, uint32_t* d_scratch, uint64_t scratch_entries, uint32_t* d_err,
+                        hlkv_stream_t stream);
+
 /* ---- decode attention over the quantized blocks ------------------------------------------ */
 /*
  * One query token per sequence attends to the sequence's cached K and V, read from the
@@ -450,6 +479,16 @@ int hlkv_table_batch_segments(const hlkv_table* t, const HlkvHandle* seqs, size_
 int hlkv_table_append_tokens(hlkv_table* t, const HlkvHandle* seqs, size_t n,
                              const uint32_t* new_formats, uint32_t layout,
                              HlkvAppendTarget* out, size_t* n_done);
+/*
+ * HeteroBlockTable::compact_arena: packs the id arena (live segments to the front, in offset
+ * order, free storage given back) and writes the segment moves the device copy must make to
+ * out (at most one per live sequence: cap must be at least the number of live sequences,
+ * else HLKV_STATUS_INVALID_ARGUMENT and nothing changes).  HLKV_STATUS_INVALID_STATE while
+ * id patches are pending (collect the delta first).  Follow it with
+ * hlkv_device_tables_relocate (or hlkv_arena_relocate) before the next delta is applied.
+ * No counterpart in the reference.
+ */
+int hlkv_table_compact_arena(hlkv_table* t, HlkvSegmentMove* out, size_t cap, size_t* n_moves);
 /* CSR reference path: indptr[n+1], blocks[cap]; *total = number of blocks. */
 int hlkv_table_build_exec_table(const hlkv_table* t, const HlkvHandle* seqs, size_t n,
                                 uint32_t* indptr, HlkvExecDescriptor* blocks, size_t cap,
@@ -492,8 +531,25 @@ int hlkv_device_tables_sync(hlkv_device_tables* dt, hlkv_table* t, hlkv_stream_t
  */
 int hlkv_device_tables_collect(hlkv_device_tables* dt, hlkv_table* t);
 int hlkv_device_tables_flush(hlkv_device_tables* dt, hlkv_stream_t stream);
+/*
+ * Applies a compaction to the device arena (after flushing what collect gathered): the moves
+ * of hlkv_table_compact_arena (host memory) through the mirror's own staging and scratch,
+ * then the arena's size becomes new_arena_size (the table's arena size after compacting),
+ * and device memory beyond a quarter of headroom above it is returned.  Returning memory
+ * waits for the device to go idle (cudaDeviceSynchronize): compaction is maintenance, not
+ * a per-step call.  No counterpart in the reference.
+ */
+int hlkv_device_tables_relocate(hlkv_device_tables* dt, const HlkvSegmentMove* moves, size_t n,
+                                uint32_t new_arena_size, hlkv_stream_t stream);
+/* Device memory behind the arena, in bytes (the capacity it can grow into without mapping
+ * more). */
+uint64_t hlkv_device_tables_arena_capacity_bytes(const hlkv_device_tables* dt);
 const HlkvExecDescriptor* hlkv_device_tables_table(const hlkv_device_tables* dt);
 uint32_t hlkv_device_tables_table_size(const hlkv_device_tables* dt);
+/* The device arena.  Where the driver supports virtual memory management, the arena lives in
+ * a reserved address range and growth maps more memory behind it: the address never changes
+ * (kernels already queued, or a captured CUDA graph, keep a valid pointer).  Otherwise growth
+ * reallocates and copies, and the address changes at growth. */
 const uint32_t* hlkv_device_tables_arena(const hlkv_device_tables* dt);
 uint32_t hlkv_device_tables_arena_size(const hlkv_device_tables* dt);
 /* Device word the sync's kernel (3) reports into (zeroed at creation). */

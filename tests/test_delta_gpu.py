@@ -200,3 +200,129 @@ def test_restored_table_gathers_like_the_original(hlkv_lib, oracle, cuda_device)
         assert int(err.item()) == 0
         outs.append(out.cpu().numpy())
     assert np.array_equal(outs[0], outs[1])
+
+
+def test_arena_compaction_relocates_the_device_arena(hlkv_lib, oracle, cuda_device):
+    """Bursts of long sequences, releases and arena compactions: after each compaction
+    (HeteroBlockTable::compact_arena + DeviceTables::relocate, i.e. the two relocation
+    launches) and after each later delta, every live sequence's device arena entries equal
+    its block ids; the arena pointer never changes (virtual memory management); a gather
+    through the compacted tables equals the oracle's."""
+    import torch
+    from helpers import oracle_gather
+    from hlkv.workload import KVWorkload
+    h = hlkv_lib
+    T, H, D = 4, 2, 64
+    layout = h.Layout(T, H, D, 1)
+    sb = {f: (h.layout_slot_bytes(f, layout) + 15) // 16 * 16 for f in (1, 3)}
+    t = h.Table(30000, [(1, sb[1], 15000), (3, sb[3], 15000)], block_tokens=T)
+    dt = h.DeviceTables()
+    rng = np.random.default_rng(99)
+    seqs = []
+    arena_ptr = None
+    for rnd in range(12):
+        # a burst: a few long sequences, many short ones
+        for _ in range(int(rng.integers(20, 60))):
+            st, s = t.create_sequence()
+            assert st == 0
+            seqs.append(s)
+            n = int(rng.integers(200, 900)) if rng.random() < 0.15 else int(rng.integers(1, 12))
+            for _ in range(n):
+                if t.append_block(s, int(rng.choice([1, 3])), int(rng.integers(1, T + 1)))[0] != 0:
+                    break
+        dt.sync(t)
+        arena_ptr = arena_ptr or dt.arena_ptr
+        assert dt.arena_ptr == arena_ptr  # growth mapped more memory behind the same address
+        # release most of the long ones, then compact
+        for i in sorted(rng.choice(len(seqs), size=len(seqs) // 2, replace=False), reverse=True):
+            assert t.release_sequence(seqs.pop(int(i))) == 0
+        dt.sync(t)
+        st, moves = t.compact_arena()
+        assert st == 0
+        dt.relocate(moves, t.stats()["arena_entries"])
+        torch.cuda.synchronize()
+        assert dt.arena_ptr == arena_ptr
+        assert dt.arena_size == t.stats()["arena_entries"]
+        _, arena = _device_state(dt)
+        st, segs = t.batch_segments(seqs)
+        for s, (off, ln) in zip(seqs, segs):
+            assert list(arena[off:off + ln]) == t.sequence_block_ids(s)[1], f"round {rnd}"
+        # more appends after the compaction go through ordinary deltas
+        for s in seqs[: len(seqs) // 3]:
+            t.append_block(s, 3, 1)
+        dt.sync(t)
+        _, arena = _device_state(dt)
+        st, segs = t.batch_segments(seqs)
+        for s, (off, ln) in zip(seqs, segs):
+            assert list(arena[off:off + ln]) == t.sequence_block_ids(s)[1], f"round {rnd} after"
+    assert d2h(dt.error_word_ptr, 4).view(np.uint32)[0] == 0
+
+    # A gather through the compacted tables, against the oracle on the same bytes.
+    gen = torch.Generator(device="cuda")
+    gen.manual_seed(5)
+    pools = {}
+    for f in (1, 3):
+        buf = torch.randint(0, 256, (15000, sb[f]), generator=gen, device="cuda", dtype=torch.uint8)
+        if f == 1:  # keep the scales finite and moderate: bytes of binary32 values in [1/4, 1)
+            rows = 2 * T * H
+            scales = torch.rand((15000, rows), generator=gen, device="cuda") * 0.75 + 0.25
+            buf[:, T * H * D * 2:T * H * D * 2 + 4 * rows] = scales.view(torch.uint8)
+        else:
+            rows = 2 * T * H
+            sbias = torch.rand((15000, rows, 2), generator=gen, device="cuda") + 0.1
+            buf[:, T * H * D:T * H * D + 8 * rows] = sbias.reshape(15000, -1).view(torch.uint8)
+        pools[f] = (buf, sb[f], 15000)
+    st, segs_host = t.batch_segments(seqs)
+    wl = KVWorkload(T, H, D, layout, t, dt, pools, seqs,
+                    torch.from_numpy(segs_host.astype(np.int32).reshape(-1, 2)).cuda(), segs_host)
+    out = torch.empty(max(1, wl.total_blocks) * wl.block_elems, dtype=torch.int16, device="cuda")
+    err = torch.zeros(1, dtype=torch.int32, device="cuda")
+    h.gather_dequant(wl.hlkv_pools(), layout, dt.table_ptr, dt.table_size, dt.arena_ptr, dt.arena_size,
+                     wl.segs, out, err)
+    torch.cuda.synchronize()
+    want, oerr = oracle_gather(oracle, wl)
+    assert int(err.item()) == 0 and oerr == 0
+    got = out.cpu().numpy().view(np.uint16)[:want.size]
+    assert np.array_equal(got, want)
+
+
+def test_arena_memory_returned_after_compaction(hlkv_lib, cuda_device):
+    """An arena of several MB (16 sequences of 40,000 blocks), most of it released and
+    compacted: the device memory behind the arena shrinks to about the packed size plus a
+    quarter, at the same address, and the remaining sequences are intact."""
+    h = hlkv_lib
+    t = h.Table(700000, [(1, 64, 700000)], block_tokens=16)
+    dt = h.DeviceTables()
+    seqs = [t.create_sequence()[1] for _ in range(16)]
+    for s in seqs:
+        for _ in range(40000):
+            assert t.append_block(s, 1, 16)[0] == 0
+    dt.sync(t)
+    ptr, cap0 = dt.arena_ptr, dt.arena_capacity_bytes
+    assert cap0 >= 16 * 65536 * 4  # 16 segments of the 65,536-entry class
+    for s in seqs[:14]:
+        assert t.release_sequence(s) == 0
+    seqs = seqs[14:]
+    dt.sync(t)
+    st, moves = t.compact_arena()
+    assert st == 0
+    size = t.stats()["arena_entries"]
+    assert size == 2 * 65536
+    dt.relocate(moves, size)
+    assert dt.arena_ptr == ptr
+    assert dt.arena_capacity_bytes < cap0
+    assert size * 4 <= dt.arena_capacity_bytes <= size * 4 * 5 // 4 + (2 << 20)
+    _, arena = _device_state(dt)
+    st, segs = t.batch_segments(seqs)
+    for s, (off, ln) in zip(seqs, segs):
+        assert list(arena[off:off + ln]) == t.sequence_block_ids(s)[1]
+    # and it grows again behind the same address
+    for s in seqs:
+        for _ in range(30000):
+            assert t.append_block(s, 1, 16)[0] == 0
+    dt.sync(t)
+    assert dt.arena_ptr == ptr
+    _, arena = _device_state(dt)
+    st, segs = t.batch_segments(seqs)
+    for s, (off, ln) in zip(seqs, segs):
+        assert list(arena[off:off + ln]) == t.sequence_block_ids(s)[1]

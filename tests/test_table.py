@@ -289,3 +289,104 @@ def test_snapshot_rejects_damaged_images(hlkv_lib):
     small = (C.c_char * 8)()
     assert h.lib().hlkv_table_snapshot(t.h, small, 8, C.byref(n)) == 6  # INVALID_ARGUMENT
     assert n.value == len(image) and bytes(small) == b"\0" * 8
+
+
+def _apply_delta_model(dev: "np.ndarray", delta) -> "np.ndarray":
+    """A device arena model: grow to the delta's arena size, then scatter its id patches."""
+    if delta.arena_size > dev.size:
+        dev = np.concatenate([dev, np.full(delta.arena_size - dev.size, 0xDEADBEEF, np.uint32)])
+    for off, bid in delta.id_patches:
+        dev[off] = bid
+    return dev
+
+
+def _apply_moves_model(dev: "np.ndarray", moves) -> "np.ndarray":
+    """The two phases of hlkv_arena_relocate: every moved segment to scratch, then to its
+    new offset (lengths rounded up to 4 entries, as the kernel copies them)."""
+    dev = dev.copy()
+    if len(moves) == 0:
+        return dev
+    n_scratch = int(moves[-1, 3]) + ((int(moves[-1, 2]) + 7) & ~7)
+    scratch = np.zeros(n_scratch, np.uint32)
+    for frm, to, ln, sc in moves:
+        l4 = (int(ln) + 3) & ~3
+        scratch[sc:sc + l4] = dev[frm:frm + l4]
+    for frm, to, ln, sc in moves:
+        l4 = (int(ln) + 3) & ~3
+        dev[to:to + l4] = scratch[sc:sc + l4]
+    return dev
+
+
+def test_arena_compaction_keeps_sequences_and_packs_the_arena(hlkv_lib):
+    """compact_arena over a random walk: every live sequence keeps its blocks, the arena
+    shrinks to the live segments' capacity with no free storage, and a device arena model
+    kept by the deltas plus the returned moves (made as the relocation kernels make them)
+    equals the host's segments after every step."""
+    h = hlkv_lib
+    rng = np.random.default_rng(17)
+    t = h.Table(4000, [(1, 2048, 2000), (3, 1088, 2000)], block_tokens=4)
+    dev = np.zeros(0, np.uint32)
+    seqs = []
+    compactions = 0
+    for step in range(1500):
+        r = rng.random()
+        if r < 0.08 or not seqs:
+            st, s = t.create_sequence()
+            assert st == 0
+            seqs.append(s)
+        elif r < 0.75:
+            s = seqs[rng.integers(len(seqs))]
+            for _ in range(int(rng.integers(1, 40 if rng.random() < 0.1 else 4))):
+                st, _ = t.append_block(s, int(rng.choice([1, 3])), 2)
+                if st != 0:
+                    break
+        elif r < 0.85:
+            s = seqs.pop(int(rng.integers(len(seqs))))
+            assert t.release_sequence(s) == 0
+        else:
+            dev = _apply_delta_model(dev, t.collect_delta())
+            before = {(s.id, s.generation): list(t.sequence_block_ids(s)[1]) for s in seqs}
+            stats0 = t.stats()
+            st, moves = t.compact_arena()
+            assert st == 0
+            compactions += 1
+            dev = _apply_moves_model(dev, moves)
+            stats = t.stats()
+            assert stats["arena_free_entries"] == 0
+            assert stats["arena_entries"] == stats["arena_reserved_entries"] <= stats0["arena_entries"]
+            assert stats["pending_id_patches"] == 0  # the moves replace patches
+            assert t.validate()[0] == 0
+            st, segs = t.batch_segments(seqs)
+            assert st == 0
+            offs = sorted(int(o) for o, n in segs if n)
+            assert all(moves[k, 0] > moves[k, 1] for k in range(len(moves)))
+            for s, (off, n) in zip(seqs, segs):
+                ids = list(t.sequence_block_ids(s)[1])
+                assert ids == before[(s.id, s.generation)]
+                assert list(dev[off:off + n]) == ids, (step, s)
+            dev = dev[:stats["arena_entries"]]
+    dev = _apply_delta_model(dev, t.collect_delta())
+    st, segs = t.batch_segments(seqs)
+    for s, (off, n) in zip(seqs, segs):
+        assert list(dev[off:off + n]) == list(t.sequence_block_ids(s)[1])
+    assert compactions > 50
+
+
+def test_arena_compaction_refusals_change_nothing(hlkv_lib):
+    import ctypes as C
+    h = hlkv_lib
+    t = h.Table(64, [(1, 2048, 64)], block_tokens=4)
+    seqs = [t.create_sequence()[1] for _ in range(3)]
+    for s in seqs:
+        for _ in range(9):
+            assert t.append_block(s, 1, 1)[0] == 0
+    image = t.snapshot()
+    st, _ = t.compact_arena()  # id patches pending: collect first
+    assert st == h.Status.INVALID_STATE
+    t.collect_delta()
+    image = t.snapshot()
+    n = C.c_size_t()
+    moves = (C.c_uint32 * 8)()
+    assert h.lib().hlkv_table_compact_arena(t.h, moves, 2, C.byref(n)) == h.Status.INVALID_ARGUMENT  # 3 live
+    assert t.snapshot() == image
+    assert t.compact_arena()[0] == 0
