@@ -1105,11 +1105,29 @@ def measure_e2e(args, wl, layer_segs, nseq_rank, out, err, stream, world, e2e_st
     assert int(err.item()) == 0
     h2d = host_segs.numel() * 4 + staged[0] // e2e_steps
     d2h = 2 * sum(layer_elems)
+
+    # The ceiling: plain pinned device-to-host copies of one layer's output, nothing else
+    # running, on every rank at once (the ranks share the host's memory and PCIe root).
+    barrier()
+    c0 = torch.cuda.Event(enable_timing=True)
+    c1 = torch.cuda.Event(enable_timing=True)
+    reps = 3
+    with torch.cuda.stream(s_out):
+        c0.record(s_out)
+        for _ in range(reps):
+            host_out[0][:layer_elems[0]].copy_(dev_out[0][:layer_elems[0]], non_blocking=True)
+        c1.record(s_out)
+    torch.cuda.synchronize()
+    (copy_ms,) = max_over_ranks([c0.elapsed_time(c1)], world, "cuda")
+    ceiling = 2 * layer_elems[0] * reps / (copy_ms / 1e3) / 1e9
     return {"value": round(e2e_value, 2), "unit": "GB/s", "steps": e2e_steps,
             "per_gpu": round(e2e_value / world, 2),
             "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h,
             "ms_per_step": round(max(e2e_ms, wall_ms) / e2e_steps, 3),
             "d2h_gbs_per_gpu": round(d2h / (max(e2e_ms, wall_ms) / e2e_steps / 1e3) / 1e9, 2),
+            "d2h_ceiling_gbs_per_gpu": round(ceiling, 2),
+            "limit": "the device-to-host copy of every layer's FP16 output: d2h_gbs_per_gpu against "
+                     "d2h_ceiling_gbs_per_gpu, plain pinned copies of the same size on all ranks at once",
             "path": ("host table updates + collect_delta (pinned staging read in place by kernel 3) -> "
                      if updates is not None else "") +
                     "pinned host segments -> H2D -> hlkv_gather_dequant per layer (pools resident "
