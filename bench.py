@@ -79,6 +79,11 @@ WORKLOADS = {
     "llama8b": dict(nseq=64, tokens=8192, tiers=(512, 2048), layers=32, scaling="strong", cpu_sample_seqs=2,
                     name="Llama-3-8B cache: 32 layers, 64 seq x 8192 tok sharded by sequence, "
                          "8 KV heads x 128, K+V; newest 512 tok FP16, previous 2048 E4M3, rest INT4"),
+    # One layer of that cache (2.97 GB per launch): the same launch as each of llama8b's, small
+    # enough (0.8 GB of pools + 2.1 GB of output) for a full ncu capture.
+    "llama8b_layer": dict(nseq=64, tokens=8192, tiers=(512, 2048), layers=1, scaling="strong", cpu_sample_seqs=2,
+                          name="one layer of the Llama-3-8B cache: 64 seq x 8192 tok sharded by sequence, "
+                               "8 KV heads x 128, K+V; newest 512 tok FP16, previous 2048 E4M3, rest INT4"),
     # Llama-3-70B-shaped long context sharded by sequence; 8 resident layers per GPU (the
     # 80-layer payload of 234 GB does not fit one GPU), one launch per layer per step.
     "llama70b": dict(nseq=16, blocks=8192, probs=(0.05, 0.10, 0.0, 0.85), layers=8,
@@ -317,7 +322,7 @@ def sample_inputs(wl, rows):
 
 
 def cpu_gather_sample(wl, rows, out_dev, out_first_elem: int, timed: bool, min_wall_s: float = 10.0,
-                      max_reps: int = 200):
+                      max_reps: int = 5000):
     """The reference's CPU path (oracle/_ref: its dequantize_reference_to_fp16 per parameter
     group, walked through the same descriptor table) -- or the C restatement when the
     reference library is absent -- on the table sequences `rows`.  Its output is compared
@@ -531,7 +536,8 @@ def run_hlkv(args) -> None:
             "roofline": {"bound": "hbm", "achieved": round(achieved, 2), "peak": peak,
                          "unit": "GB/s", "frac": round(achieved / peak, 4),
                          "peak_source": f"{peak_kind} (MEASURED_PEAKS.json hbm_gbs, copy bandwidth)",
-                         "traffic": traffic_from_profile(args.workload),
+                         "traffic": traffic_from_profile("llama8b_layer" if args.workload == "llama8b"
+                                                         else args.workload),
                          "kernel": "gather_dequant_kernel<128>",
                          "launch_ms": round(mean_launch_ms, 5)},
             "parity": parity["ok"] if parity is not None else None,
