@@ -578,9 +578,9 @@ def run_decode(args) -> None:
     steps_total = args.warmup + args.steps
     nb = -(-stream_len // T)
     init_fmt = rng.choice(quant, size=int(nb.sum()))
-    new_fmt = rng.choice(quant, size=(steps_total, n)).astype(np.uint32)
+    new_fmt = rng.choice(quant, size=(steps_total + 1, n)).astype(np.uint32)  # + the parity step
     layout = hlkv.Layout(T, H, D, 1)
-    extra = n * (steps_total // T + 2)
+    extra = n * ((steps_total + 1) // T + 2)
     slots = {int(f): int((init_fmt == f).sum()) + extra for f in quant}
     sbytes = {f: (hlkv.layout_slot_bytes(f, layout) + 15) // 16 * 16 for f in slots}
     t_build = time.perf_counter()
@@ -677,6 +677,21 @@ def run_decode(args) -> None:
     peak, peak_kind = measured_peak_gbs()
     achieved = nbytes["encode"] / args.steps / (enc_mean / 1e3) / 1e9
 
+    # Parity, outside the timed region: one more step; the rows it wrote for a sample of
+    # its targets (codes and parameters in the pools) against the reference's own
+    # quantize_reference of the same tokens, bit for bit.
+    parity = None
+    if rank == 0:
+        k = steps_total
+        b = k & 1
+        copied[b].synchronize()
+        st, tg, done = table.append_tokens(handles, new_fmt[k], 1, out=pinned_np[b])
+        assert st == 0 and done == n
+        dt.collect(table)
+        hlkv.decode_step_queue(dt, pools, layout, pinned[b], d_targets[b], tokens[k % 4], err, stream=stream)
+        torch.cuda.synchronize()
+        parity = decode_parity(table, pools_t, tokens[k % 4], tg, T, H, D, layout, int(err.item()))
+
     cpu = None
     if world == 1 and not args.no_cpu_baseline:
         cpu = cpu_encode_sample(tokens[0], tail_fmt, H, D, n)
@@ -707,6 +722,8 @@ def run_decode(args) -> None:
                     "path": "host table ops + collect_delta -> hlkv_decode_step_queue (H2D of "
                             "targets and delta -> apply_delta -> append_encode), wall clock per step "
                             "(tokens resident)"},
+            "parity": parity["ok"] if parity is not None else None,
+            "parity_detail": parity,
             "gpu_launches": 2 * args.steps,  # apply_delta + append_encode per step
             "clocks": clocks.summary(c0, c1),
             "cpu_baseline": cpu,
@@ -714,6 +731,52 @@ def run_decode(args) -> None:
     if world > 1:
         dist.barrier()
         dist.destroy_process_group()
+
+
+def decode_parity(table, pools_t, tokens, targets, T: int, H: int, D: int, layout, err_bits: int,
+                  sample_size: int = 256) -> dict:
+    """The rows a decode step wrote for a sample of its targets -- codes and parameters as
+    the pools hold them -- against the reference's quantize_reference (oracle/_ref; the C
+    restatement when the reference library is absent) of the same FP16 tokens."""
+    import numpy as np
+    import torch
+    import hlkv
+    from oracle.oracle import Oracle, Ref, ref_available
+    kind = "reference" if ref_available() else "port"
+    impl = Ref() if kind == "reference" else Oracle()
+    n = targets.shape[0]
+    sample = np.unique(np.linspace(0, n - 1, num=min(n, sample_size)).astype(np.int64))
+    ids = targets[sample, 0]
+    desc = np.array([table.device_descriptor(int(i)) for i in ids], np.uint32).reshape(-1, 4)
+    fmts = desc[:, 1] & 0xF
+    x = tokens[torch.from_numpy(sample).to(tokens.device)].float().cpu().numpy().reshape(-1, D)
+    rows = x.shape[0]
+    params = np.zeros((rows, 2), np.float32)
+    codes = np.zeros((rows, D), np.uint8)
+    rejected = impl.quantize_rows(np.repeat(fmts.astype(np.uint8), 2 * H), np.ascontiguousarray(x), params, codes,
+                                  os.cpu_count() or 1)
+    differing = 0
+    for f in np.unique(fmts):
+        sel = np.nonzero(fmts == f)[0]
+        buf, sb, _ = pools_t[int(f)]
+        slots = buf[torch.from_numpy(desc[sel, 0].astype(np.int64)).to(buf.device)].cpu().numpy()
+        cb = D if f == hlkv.FP8_E4M3 else D // 2           # code bytes per row
+        code_region = 2 * T * H * cb
+        pw = 1 if f == hlkv.FP8_E4M3 else 2                # parameter words per row
+        for j, t in enumerate(sel):
+            tok = int(targets[sample[t], 1])
+            for rr in range(2 * H):
+                kv, h = divmod(rr, H)
+                row = (kv * T + tok) * H + h
+                r = t * 2 * H + rr
+                got_codes = slots[j, row * cb:(row + 1) * cb]
+                got_prm = slots[j, code_region + row * 4 * pw:code_region + (row + 1) * 4 * pw].view(np.uint32)
+                want_prm = params[r, :pw].view(np.uint32)
+                differing += int(not np.array_equal(got_codes, codes[r, :cb])) + int(not np.array_equal(got_prm, want_prm))
+    ok = err_bits == 0 and rejected == 0 and differing == 0
+    return {"ok": bool(ok), "differing_rows": differing,
+            "checked": f"{len(sample)} of {n} targets of one more decode step ({rows} rows: codes and "
+                       f"parameters in the pools) against quantize_reference ({kind}), bit for bit"}
 
 
 def cpu_encode_sample(tokens, tail_fmt, H: int, D: int, n: int, min_wall_s: float = 2.0):
