@@ -190,6 +190,21 @@ while True:
 """
 
 
+class TimedRange:
+    """An NVTX push/pop range named "timed" around a timed region, so that a profiler's
+    launch list can be restricted to it (ncu --nvtx --nvtx-include timed/)."""
+
+    def __enter__(self):
+        import torch
+        torch.cuda.nvtx.range_push("timed")
+        return self
+
+    def __exit__(self, *exc):
+        import torch
+        torch.cuda.nvtx.range_pop()
+        return False
+
+
 class ClockSampler:
     """Samples SM clock and throttle reasons of one GPU through NVML in a child process
     (NVML calls made from the benchmarked process contend with its CUDA calls).  The
@@ -270,12 +285,15 @@ class ClockSampler:
 
 def traffic_from_profile(workload: str) -> int | None:
     """DRAM bytes (read + write) per launch of the gather kernel, from the committed ncu
-    summary of the same workload (profiles/gather_dequant_<workload>_full.md), or None."""
+    summary of the same workload (profiles/gather_dequant_<workload>_full.md), or None.
+    The summary's table row "traffic (read + write) per launch" lists one capture per
+    column, the current kernel last."""
     import re
     try:
         with open(os.path.join(ROOT, "profiles", f"gather_dequant_{workload}_full.md")) as f:
-            m = re.search(r"traffic \(read \+ write\) per launch \| ([0-9,]+) B", f.read())
-        return int(m.group(1).replace(",", "")) if m else None
+            row = re.search(r"^\| traffic \(read \+ write\) per launch \|(.*)$", f.read(), re.M)
+        cells = re.findall(r"([0-9,]+) B", row.group(1)) if row else []
+        return int(cells[-1].replace(",", "")) if cells else None
     except OSError:
         return None
 
@@ -465,15 +483,16 @@ def run_hlkv(args) -> None:
         host_update_s[0] = 0.0
         launches[0] = 0
         h0 = time.time()
-        t_start.record(stream)
-        for k in range(args.steps):
-            if flush is not None:
-                flush.fill_(k & 0xFF)
-            prepare()
-            ev[k][0].record(stream)
-            step()
-            ev[k][1].record(stream)
-        t_end.record(stream)
+        with TimedRange():
+            t_start.record(stream)
+            for k in range(args.steps):
+                if flush is not None:
+                    flush.fill_(k & 0xFF)
+                prepare()
+                ev[k][0].record(stream)
+                step()
+                ev[k][1].record(stream)
+            t_end.record(stream)
         torch.cuda.synchronize()
         h1 = time.time()
         barrier()
@@ -659,8 +678,9 @@ def run_decode(args) -> None:
             dist.barrier()
         torch.cuda.synchronize()
         w0, c0 = time.perf_counter(), time.time()
-        for k in range(args.warmup, steps_total):
-            step(k, True)
+        with TimedRange():
+            for k in range(args.warmup, steps_total):
+                step(k, True)
         torch.cuda.synchronize()
         w1, c1 = time.perf_counter(), time.time()
     assert int(err.item()) == 0, f"error bits {int(err.item()):#x}"
@@ -884,12 +904,13 @@ def run_attention(args) -> None:
             dist.barrier()
         torch.cuda.synchronize()
         c0 = time.time()
-        for k in range(args.steps):
-            if flush is not None:
-                flush.fill_(k & 0xFF)
-            ev[k][0].record(stream)
-            step()
-            ev[k][1].record(stream)
+        with TimedRange():
+            for k in range(args.steps):
+                if flush is not None:
+                    flush.fill_(k & 0xFF)
+                ev[k][0].record(stream)
+                step()
+                ev[k][1].record(stream)
         torch.cuda.synchronize()
         c1 = time.time()
     ms = [a.elapsed_time(b) for a, b in ev]
@@ -992,7 +1013,8 @@ def run_flat(args) -> None:
         if world > 1:
             dist.barrier()
         c0 = time.time()
-        ms = timed(ours)
+        with TimedRange():
+            ms = timed(ours)
         c1 = time.time()
     total_ms, mean_ms = max_over_ranks([sum(ms), statistics.mean(ms)], world, "cuda")
     value = world * nbytes * args.steps / (total_ms / 1e3) / 1e9

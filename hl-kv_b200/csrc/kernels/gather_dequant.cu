@@ -18,7 +18,8 @@
 //  * the descriptor chain segment -> arena -> table (three dependent loads) of
 //    up to 256 owned blocks is resolved in parallel, one block per thread, into
 //    shared memory; blocks are then streamed back to back without a barrier;
-//  * per block the format is CTA-uniform; each thread handles 8-element
+//  * per block the format is CTA-uniform and selects one of four instantiations
+//    of the streaming loop; each thread handles 8-element
 //    chunks: a 16-byte (FP16), 8-byte (FP8) or 4-byte (INT4) coalesced load,
 //    register-level byte/nibble unpack into the warp's shared-memory tile;
 //    one lane writes each 2 KB tile to HBM with a TMA bulk store
@@ -126,17 +127,17 @@ __device__ Item resolve(const Params& p, uint32_t seq, uint64_t j, uint64_t bloc
 // write ceiling with few resident warps, where per-thread stores need twice
 // the occupancy this kernel's registers allow.  Only __syncwarp is needed.
 //
-// One register set serves every format (raw chunk words + row parameters) and
-// the format test is CTA-uniform, so the compiler keeps one allocation
-// instead of one per format.
-template <int kD>
+// One instantiation per format (kF): the load widths, the parameter loads and the
+// conversion are straight-line code, with no format test per chunk.  The format is
+// CTA-uniform per block, so stream_item's switch costs one branch per block.
+template <int kD, uint32_t kF>
 __device__ __forceinline__ void stream_block(const Params& p, const Item& it, uint4* tile) {
   constexpr uint32_t kChunksPerRowLog2 = kD == 64 ? 3 : (kD == 128 ? 4 : 5);
   constexpr uint32_t kTile = 32 * kUnroll;  // chunks per warp tile
   const uint32_t lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
   const uint32_t nchunks = static_cast<uint32_t>(p.block_elems >> 3);
   const uint32_t rpk = p.rows_per_kv;
-  const uint32_t f = it.fmt & 0xFFu;
+  constexpr uint32_t f = kF;
   const bool wide = (it.fmt & kWide) != 0;  // the same item for every warp of the CTA
   const uint8_t* payload = it.payload;
   const uint8_t* params = payload + p.code_bytes[f];
@@ -156,9 +157,9 @@ __device__ __forceinline__ void stream_block(const Params& p, const Item& it, ui
       prm[u] = make_float2(0.0f, 0.0f);
       if (v < nchunks && r < it.valid_rows) {
         live |= 1u << u;
-        if (f == dev::kFp16) {
+        if constexpr (f == dev::kFp16) {
           raw[u] = dev::ld_stream256(reinterpret_cast<const uint4*>(payload) + v);
-        } else if (f == dev::kInt4) {
+        } else if constexpr (f == dev::kInt4) {
           raw[u].x = dev::ld_stream256(reinterpret_cast<const uint32_t*>(payload) + v);
           prm[u] = wide ? it.prm : __ldg(reinterpret_cast<const float2*>(params) + row);
         } else {
@@ -176,12 +177,9 @@ __device__ __forceinline__ void stream_block(const Params& p, const Item& it, ui
     for (int u = 0; u < kUnroll; ++u) {
       uint4 o = make_uint4(0u, 0u, 0u, 0u);
       if (live & (1u << u)) {
-        switch (f) {
-          case dev::kFp16: o = dev::canon_f16x8(raw[u]); break;
-          case dev::kE4M3: o = dev::fp8x8_to_f16_bits<dev::kE4M3>(make_uint2(raw[u].x, raw[u].y), prm[u].x); break;
-          case dev::kE5M2: o = dev::fp8x8_to_f16_bits<dev::kE5M2>(make_uint2(raw[u].x, raw[u].y), prm[u].x); break;
-          default: o = dev::int4x8_to_f16(raw[u].x, prm[u].x, prm[u].y); break;
-        }
+        if constexpr (f == dev::kFp16) o = dev::canon_f16x8(raw[u]);
+        else if constexpr (f == dev::kInt4) o = dev::int4x8_to_f16(raw[u].x, prm[u].x, prm[u].y);
+        else o = dev::fp8x8_to_f16_bits<f>(make_uint2(raw[u].x, raw[u].y), prm[u].x);
       }
       tile[u * 32 + lane] = o;
     }
@@ -192,6 +190,16 @@ __device__ __forceinline__ void stream_block(const Params& p, const Item& it, ui
       dev::bulk_store(out + t0, tile, n * 16u);
       dev::bulk_commit();
     }
+  }
+}
+
+template <int kD>
+__device__ __forceinline__ void stream_item(const Params& p, const Item& it, uint4* tile) {
+  switch (it.fmt & 0xFFu) {
+    case dev::kFp16: stream_block<kD, dev::kFp16>(p, it, tile); break;
+    case dev::kE4M3: stream_block<kD, dev::kE4M3>(p, it, tile); break;
+    case dev::kE5M2: stream_block<kD, dev::kE5M2>(p, it, tile); break;
+    default: stream_block<kD, dev::kInt4>(p, it, tile); break;
   }
 }
 
@@ -292,7 +300,7 @@ __global__ void __launch_bounds__(kThreads, kMinCtasPerSm) gather_dequant_kernel
           static_cast<uint32_t>(min(uint64_t{kThreads}, (pend - first + G - 1) / G));
       for (uint32_t k = 0; k < n_items; ++k) {
         const Item it = s_item[k];
-        if (it.fmt != kSkip) stream_block<kD>(p, it, s_tile[threadIdx.x >> 5]);
+        if (it.fmt != kSkip) stream_item<kD>(p, it, s_tile[threadIdx.x >> 5]);
       }
       __syncthreads();  // s_item is rewritten by the next batch
     }
