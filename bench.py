@@ -638,8 +638,9 @@ def run_decode(args) -> None:
     rows_in = 2 * H * D * 2
     enc_out = {int(hlkv.FP8_E4M3): 2 * H * D + 2 * H * 4, int(hlkv.INT4): 2 * H * D // 2 + 2 * H * 8}
     ev = [[torch.cuda.Event(enable_timing=True) for _ in range(3)] for _ in range(steps_total)]
-    for e in ev:
-        e[1].record(stream)  # torch creates the CUDA event at its first record
+    for e in ev:  # torch creates the CUDA event at its first record
+        e[0].record(stream)
+        e[1].record(stream)
     host = {"table_s": 0.0, "sync_s": 0.0}
     nbytes = {"encode": 0, "delta": 0}
 
@@ -655,10 +656,10 @@ def run_decode(args) -> None:
         h1 = time.perf_counter()
         dt.collect(table)  # host half of the delta protocol: nothing queued on the GPU yet
         h2 = time.perf_counter()
-        ev[k][0].record(stream)
-        # targets H2D, delta upload + kernel (3), ev[k][1], kernel (2): one native call
+        # ev[k][0], kernel (3) with the delta and the targets, ev[k][1], kernel (2): one
+        # native call, which records ev[k][0] just before its first launch
         hlkv.decode_step_queue(dt, pools, layout, pinned[b], d_targets[b], tokens[k % 4], err,
-                               encode_event=ev[k][1], stream=stream)
+                               start_event=ev[k][0], encode_event=ev[k][1], stream=stream)
         ev[k][2].record(stream)
         copied[b].record(stream)
         tail_fmt = np.where(tg[:, 1] == 0, new_fmt[k], tail_fmt)
@@ -799,7 +800,7 @@ def decode_parity(table, pools_t, tokens, targets, T: int, H: int, D: int, layou
                        f"parameters in the pools) against quantize_reference ({kind}), bit for bit"}
 
 
-def cpu_encode_sample(tokens, tail_fmt, H: int, D: int, n: int, min_wall_s: float = 2.0):
+def cpu_encode_sample(tokens, tail_fmt, H: int, D: int, n: int, min_wall_s: float = 10.0):
     """The reference's quantize_reference per row (oracle/_ref), on all host threads, over
     one step's tokens: n targets x 2*H rows of D values, in the formats of their blocks."""
     import numpy as np
@@ -817,7 +818,7 @@ def cpu_encode_sample(tokens, tail_fmt, H: int, D: int, n: int, min_wall_s: floa
         bad = impl.quantize_rows(fm, x, params, codes, threads)
         reps += 1
         wall = time.perf_counter() - t0
-        if wall >= min_wall_s or reps >= 50:
+        if wall >= min_wall_s or reps >= 2000:
             break
     assert bad == 0
     n8 = int((tail_fmt == 1).sum())
@@ -1084,7 +1085,7 @@ def run_flat(args) -> None:
         dist.destroy_process_group()
 
 
-def cpu_flat_sample(codes, params, fmt: int, group: int, min_wall_s: float = 2.0):
+def cpu_flat_sample(codes, params, fmt: int, group: int, min_wall_s: float = 10.0):
     """The reference's dequantize_reference_to_fp16 (oracle/_ref) on one thread, over the
     first 1,048,576 values of the same array."""
     import numpy as np
@@ -1099,7 +1100,7 @@ def cpu_flat_sample(codes, params, fmt: int, group: int, min_wall_s: float = 2.0
         st, _ = impl.dequantize_to_fp16(fmt, c, m, p, group)
         reps += 1
         wall = time.perf_counter() - t0
-        if wall >= min_wall_s or reps >= 50:
+        if wall >= min_wall_s or reps >= 2000:
             break
     assert st == 0
     nbytes = m + 4 * p.shape[0] + 2 * m

@@ -403,8 +403,8 @@ int hlkv_device_tables_flush(hlkv_device_tables* dt, hlkv_stream_t stream) {
 
 int hlkv_decode_step_queue(hlkv_device_tables* dt, const HlkvPools* pools, const HlkvLayout* layout,
                            const HlkvAppendTarget* h_targets, HlkvAppendTarget* d_targets, uint32_t n,
-                           const uint16_t* d_tokens, uint32_t* d_err, void* encode_event,
-                           hlkv_stream_t stream) {
+                           const uint16_t* d_tokens, uint32_t* d_err, void* start_event,
+                           void* encode_event, hlkv_stream_t stream) {
   if (dt == nullptr || pools == nullptr || layout == nullptr || d_err == nullptr) return HLKV_INVALID_ARGUMENT;
   if (n > 0 && (h_targets == nullptr || d_targets == nullptr || d_tokens == nullptr)) {
     return HLKV_INVALID_ARGUMENT;
@@ -420,6 +420,9 @@ int hlkv_decode_step_queue(hlkv_device_tables* dt, const HlkvPools* pools, const
       return HLKV_INVALID_ARGUMENT;  // pageable memory: not readable by a kernel
     }
     src = attr.devicePointer;
+  }
+  if (start_event != nullptr) {
+    if (cudaEventRecord(static_cast<cudaEvent_t>(start_event), s) != cudaSuccess) return HLKV_CUDA_ERROR;
   }
   if (const int f = static_cast<int>(dt->dt.flush(s, src, d_targets, n).status); f != HLKV_OK) return f;
   if (encode_event != nullptr) {

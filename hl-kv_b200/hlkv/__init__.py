@@ -194,7 +194,7 @@ SIGNATURES: list[tuple[str, object, list]] = [
     ("hlkv_device_tables_sync", _int, [_vp, _vp, _vp]),
     ("hlkv_device_tables_collect", _int, [_vp, _vp]),
     ("hlkv_device_tables_flush", _int, [_vp, _vp]),
-    ("hlkv_decode_step_queue", _int, [_vp, _P(Pools), _P(Layout), _vp, _vp, _u32, _vp, _vp, _vp, _vp]),
+    ("hlkv_decode_step_queue", _int, [_vp, _P(Pools), _P(Layout), _vp, _vp, _u32, _vp, _vp, _vp, _vp, _vp]),
     ("hlkv_table_compact_arena", _int, [_vp, _vp, _sz, _P(_sz)]),
     ("hlkv_segment_moves_scratch_entries", _u64, [_vp, _sz]),
     ("hlkv_arena_relocate", _int, [_vp, _u32, _vp, _u32, _vp, _u64, _vp, _vp]),
@@ -577,14 +577,15 @@ def append_encode(pools: Pools, layout: Layout, table_ptr: int, table_size: int,
 
 
 def decode_step_queue(dt: "DeviceTables", pools: Pools, layout: Layout, h_targets, d_targets, tokens, err,
-                      encode_event=None, stream=None) -> int:
+                      encode_event=None, stream=None, start_event=None) -> int:
     """Device half of a decode step, queued from native code: targets H2D (h_targets: pinned
     host int32 [n, 2], as table.append_tokens wrote them), the collected delta's upload and
-    kernel (3), then kernel (2) into d_targets' blocks.  encode_event: a recorded
-    torch.cuda.Event (or None) to record just before kernel (2)."""
+    kernel (3), then kernel (2) into d_targets' blocks.  start_event / encode_event: recorded
+    torch.cuda.Events (or None) to record just before kernel (3) / kernel (2)."""
     n = int(d_targets.shape[0])
     st = lib().hlkv_decode_step_queue(dt.h, C.byref(pools), C.byref(layout), _ptr(h_targets), _ptr(d_targets),
-                                      n, _ptr(tokens), _ptr(err), encode_event, _stream_handle(stream))
+                                      n, _ptr(tokens), _ptr(err), start_event, encode_event,
+                                      _stream_handle(stream))
     check(st, "hlkv_decode_step_queue")
     return st
 

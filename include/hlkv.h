@@ -561,7 +561,9 @@ uint32_t* hlkv_device_tables_error_word(const hlkv_device_tables* dt);
  * hlkv_device_tables_flush) and, in the same launch, copies the n append targets that
  * hlkv_table_append_tokens wrote to h_targets into d_targets; then encode_event (a
  * cudaEvent_t, or NULL) is recorded and d_tokens[k] is encoded into target k through the
- * device tables (hlkv_append_encode).  h_targets must be page-locked host memory (or device
+ * device tables (hlkv_append_encode).  start_event (a cudaEvent_t, or NULL) is recorded
+ * just before kernel (3) is queued, after the call's host-side checks, so that the two events
+ * and one recorded after the call bracket the step's device work.  h_targets must be page-locked host memory (or device
  * memory), which the kernel reads in place (HLKV_INVALID_ARGUMENT for pageable memory), and
  * must stay untouched until the stream has passed kernel (3).  Returns the first failing
  * status; what was queued before it stays queued.  No counterpart in the reference: the
@@ -569,8 +571,8 @@ uint32_t* hlkv_device_tables_error_word(const hlkv_device_tables* dt);
  */
 int hlkv_decode_step_queue(hlkv_device_tables* dt, const HlkvPools* pools, const HlkvLayout* layout,
                            const HlkvAppendTarget* h_targets, HlkvAppendTarget* d_targets, uint32_t n,
-                           const uint16_t* d_tokens, uint32_t* d_err, void* encode_event,
-                           hlkv_stream_t stream);
+                           const uint16_t* d_tokens, uint32_t* d_err, void* start_event,
+                           void* encode_event, hlkv_stream_t stream);
 
 #ifdef __cplusplus
 }

@@ -212,7 +212,7 @@ def test_decode_step_queue_matches_oracle(hlkv_lib, oracle, cuda_device):
     pageable = np.zeros((n, 2), np.uint32)
     st = hlkv.lib().hlkv_decode_step_queue(wl.dt.h, C.byref(wl.hlkv_pools()), C.byref(wl.layout),
                                            pageable.ctypes.data, d_targets.data_ptr(), n,
-                                           d_targets.data_ptr(), err.data_ptr(), None, None)
+                                           d_targets.data_ptr(), err.data_ptr(), None, None, None)
     assert st == hlkv.INVALID_ARGUMENT
     st, segs_host = wl.table.batch_segments(wl.seqs)
     assert st == hlkv.Status.OK
