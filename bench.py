@@ -595,11 +595,13 @@ def run_decode(args) -> None:
     rng = np.random.default_rng(3001 + rank)
     quant = np.array([hlkv.FP8_E4M3, hlkv.INT4], dtype=np.uint32)
     steps_total = args.warmup + args.steps
+    split_steps = 8  # after the timed steps: the two kernels timed apart (an event between them)
+    all_steps = steps_total + split_steps + 1  # + the parity step
     nb = -(-stream_len // T)
     init_fmt = rng.choice(quant, size=int(nb.sum()))
-    new_fmt = rng.choice(quant, size=(steps_total + 1, n)).astype(np.uint32)  # + the parity step
+    new_fmt = rng.choice(quant, size=(all_steps, n)).astype(np.uint32)
     layout = hlkv.Layout(T, H, D, 1)
-    extra = n * ((steps_total + 1) // T + 2)
+    extra = n * (all_steps // T + 2)
     slots = {int(f): int((init_fmt == f).sum()) + extra for f in quant}
     sbytes = {f: (hlkv.layout_slot_bytes(f, layout) + 15) // 16 * 16 for f in slots}
     t_build = time.perf_counter()
@@ -637,14 +639,14 @@ def run_decode(args) -> None:
 
     rows_in = 2 * H * D * 2
     enc_out = {int(hlkv.FP8_E4M3): 2 * H * D + 2 * H * 4, int(hlkv.INT4): 2 * H * D // 2 + 2 * H * 8}
-    ev = [[torch.cuda.Event(enable_timing=True) for _ in range(3)] for _ in range(steps_total)]
+    ev = [[torch.cuda.Event(enable_timing=True) for _ in range(3)] for _ in range(steps_total + split_steps)]
     for e in ev:  # torch creates the CUDA event at its first record
         e[0].record(stream)
         e[1].record(stream)
     host = {"table_s": 0.0, "sync_s": 0.0}
     nbytes = {"encode": 0, "delta": 0}
 
-    def step(k: int, timed: bool) -> None:
+    def step(k: int, timed: bool, split: bool = False) -> None:
         nonlocal tail_fmt
         b = k & 1
         if k >= 2:
@@ -656,10 +658,12 @@ def run_decode(args) -> None:
         h1 = time.perf_counter()
         dt.collect(table)  # host half of the delta protocol: nothing queued on the GPU yet
         h2 = time.perf_counter()
-        # ev[k][0], kernel (3) with the delta and the targets, ev[k][1], kernel (2): one
-        # native call, which records ev[k][0] just before its first launch
+        # ev[k][0], kernel (3) with the delta and the targets, kernel (2): one native call,
+        # which records ev[k][0] just before its first launch.  Kernel (2) overlaps kernel (3)'s
+        # tail (programmatic serialization) unless ev[k][1] is recorded between them (split).
         hlkv.decode_step_queue(dt, pools, layout, pinned[b], d_targets[b], tokens[k % 4], err,
-                               start_event=ev[k][0], encode_event=ev[k][1], stream=stream)
+                               start_event=ev[k][0], encode_event=ev[k][1] if split else None,
+                               stream=stream)
         ev[k][2].record(stream)
         copied[b].record(stream)
         tail_fmt = np.where(tg[:, 1] == 0, new_fmt[k], tail_fmt)
@@ -685,10 +689,13 @@ def run_decode(args) -> None:
         torch.cuda.synchronize()
         w1, c1 = time.perf_counter(), time.time()
     assert int(err.item()) == 0, f"error bits {int(err.item()):#x}"
-    timed = ev[args.warmup:]
-    dev_ms = [e[0].elapsed_time(e[2]) for e in timed]
-    enc_ms = [e[1].elapsed_time(e[2]) for e in timed]
-    delta_ms = [e[0].elapsed_time(e[1]) for e in timed]
+    for k in range(steps_total, steps_total + split_steps):
+        step(k, False, split=True)
+    torch.cuda.synchronize()
+    assert int(err.item()) == 0, f"error bits {int(err.item()):#x}"
+    dev_ms = [e[0].elapsed_time(e[2]) for e in ev[args.warmup:steps_total]]
+    enc_ms = [e[1].elapsed_time(e[2]) for e in ev[steps_total:]]
+    delta_ms = [e[0].elapsed_time(e[1]) for e in ev[steps_total:]]
     wall_ms = 1e3 * (w1 - w0)
     dev_total, enc_mean, delta_mean, wall_ms = max_over_ranks(
         [sum(dev_ms), statistics.mean(enc_ms), statistics.mean(delta_ms), wall_ms], world, "cuda")
@@ -703,7 +710,7 @@ def run_decode(args) -> None:
     # quantize_reference of the same tokens, bit for bit.
     parity = None
     if rank == 0:
-        k = steps_total
+        k = steps_total + split_steps
         b = k & 1
         copied[b].synchronize()
         st, tg, done = table.append_tokens(handles, new_fmt[k], 1, out=pinned_np[b])
@@ -730,6 +737,9 @@ def run_decode(args) -> None:
             "us_per_step": {"device": round(1e3 * dev_total / args.steps, 2),
                             "encode_kernel": round(1e3 * enc_mean, 2),
                             "delta_upload_and_apply": round(1e3 * delta_mean, 2),
+                            "split": f"device: the timed steps, kernel (2) overlapping kernel (3); "
+                                     f"encode_kernel and delta_upload_and_apply: {split_steps} further "
+                                     f"steps with an event between the two kernels",
                             "host_table_ops": round(1e6 * host["table_s"] / args.steps, 2),
                             "host_collect_delta": round(1e6 * host["sync_s"] / args.steps, 2),
                             "wall": round(1e3 * wall_ms / args.steps, 2)},

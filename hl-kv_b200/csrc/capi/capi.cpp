@@ -12,6 +12,12 @@
 #include "hl_quant/cuda_dequant.hpp"
 #include "hlkv.h"
 
+namespace hlkv {
+int launch_append_encode(const HlkvPools* pools, const HlkvLayout* layout, const HlkvExecDescriptor* d_table,
+                         uint32_t table_size, const HlkvAppendTarget* d_targets, uint32_t n,
+                         const uint16_t* d_tokens, uint32_t* d_err, bool overlap_previous, cudaStream_t s);
+}
+
 using namespace hl::alloc;
 
 struct hlkv_table {
@@ -424,12 +430,24 @@ int hlkv_decode_step_queue(hlkv_device_tables* dt, const HlkvPools* pools, const
   if (start_event != nullptr) {
     if (cudaEventRecord(static_cast<cudaEvent_t>(start_event), s) != cudaSuccess) return HLKV_CUDA_ERROR;
   }
-  if (const int f = static_cast<int>(dt->dt.flush(s, src, d_targets, n).status); f != HLKV_OK) return f;
-  if (encode_event != nullptr) {
-    if (cudaEventRecord(static_cast<cudaEvent_t>(encode_event), s) != cudaSuccess) return HLKV_CUDA_ERROR;
+  // Kernel (3) and then kernel (2) with programmatic serialization: kernel (2)'s first token
+  // loads overlap kernel (3), and it waits for kernel (3) before reading the targets and the
+  // table.  The staging buffers' release is recorded after kernel (2), so that no event
+  // separates the two kernels.
+  if (const int f = static_cast<int>(dt->dt.flush_deferred(s, src, d_targets, n).status); f != HLKV_OK) {
+    (void)dt->dt.release_staging(s);
+    return f;
   }
-  return hlkv_append_encode(pools, layout, hlkv_device_tables_table(dt), dt->dt.table_size(), d_targets, n,
-                            d_tokens, d_err, stream);
+  if (encode_event != nullptr) {
+    if (cudaEventRecord(static_cast<cudaEvent_t>(encode_event), s) != cudaSuccess) {
+      (void)dt->dt.release_staging(s);
+      return HLKV_CUDA_ERROR;
+    }
+  }
+  const int st = hlkv::launch_append_encode(pools, layout, hlkv_device_tables_table(dt), dt->dt.table_size(),
+                                            d_targets, n, d_tokens, d_err, true, s);
+  const int r = static_cast<int>(dt->dt.release_staging(s).status);
+  return st != HLKV_OK ? st : r;
 }
 
 const HlkvExecDescriptor* hlkv_device_tables_table(const hlkv_device_tables* dt) {

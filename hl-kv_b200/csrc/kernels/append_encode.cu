@@ -56,6 +56,7 @@ __global__ void __launch_bounds__(kThreads, 6) append_encode_kernel(const Params
   constexpr int kRowsPerIter = kThreads / kLanes;
   const uint32_t lane = threadIdx.x % kLanes;
   const uint32_t mask = dev::row_mask<kD, kChunks>();
+  bool waited = false;
   for (uint32_t g = blockIdx.x * kRowsPerIter + threadIdx.x / kLanes; g < p.rows_total;
        g += gridDim.x * kRowsPerIter) {
     // Everything below is uniform over the lanes of row g.
@@ -63,11 +64,17 @@ __global__ void __launch_bounds__(kThreads, 6) append_encode_kernel(const Params
     const uint32_t r = g - k * p.two_h.d;
     const uint32_t kv = r >= p.H ? 1u : 0u, h = r - kv * p.H;
 
-    // The token row does not depend on the descriptor: both loads go out together.
-    const uint2 t = __ldg(p.targets + k);
+    // The token row does not depend on the descriptor: both loads go out together.  Launched
+    // with programmatic serialization after kernel (3), the first token loads are issued
+    // before waiting for kernel (3), which writes the targets and the descriptor table.
     uint4 raw[kChunks];
 #pragma unroll
     for (int c = 0; c < kChunks; ++c) raw[c] = __ldcs(p.tokens + uint64_t{g} * (kD / 8) + c * kLanes + lane);
+    if (!waited) {
+      dev::wait_for_prerequisites();
+      waited = true;
+    }
+    const uint2 t = __ldg(p.targets + k);
     uint32_t bad = 0, f = 0, slot = 0;
     const uint32_t id = t.x, tok = t.y;
     if (id >= p.table_size) {
@@ -100,11 +107,14 @@ __global__ void __launch_bounds__(kThreads, 6) append_encode_kernel(const Params
 }  // namespace
 }  // namespace hlkv
 
-extern "C" int hlkv_append_encode(const HlkvPools* pools, const HlkvLayout* layout,
-                                  const HlkvExecDescriptor* d_table, uint32_t table_size,
-                                  const HlkvAppendTarget* d_targets, uint32_t n,
-                                  const uint16_t* d_tokens, uint32_t* d_err, hlkv_stream_t stream) {
-  using namespace hlkv;
+namespace hlkv {
+
+// hlkv_append_encode; with overlap_previous the kernel is launched with programmatic stream
+// serialization (its prologue may run while the kernel before it finishes; see the kernel).
+int launch_append_encode(const HlkvPools* pools, const HlkvLayout* layout, const HlkvExecDescriptor* d_table,
+                         uint32_t table_size, const HlkvAppendTarget* d_targets, uint32_t n,
+                         const uint16_t* d_tokens, uint32_t* d_err, bool overlap_previous,
+                         cudaStream_t s) {
   if (pools == nullptr || !layout_ok(layout) || d_err == nullptr) return HLKV_INVALID_ARGUMENT;
   if (n == 0) return HLKV_OK;
   if (d_targets == nullptr || d_tokens == nullptr || (table_size > 0 && d_table == nullptr) ||
@@ -136,16 +146,33 @@ extern "C" int hlkv_append_encode(const HlkvPools* pools, const HlkvLayout* layo
   p.T = layout->block_tokens;
   p.H = layout->kv_heads;
   p.layout_id = layout->layout_id;
-  const cudaStream_t s = reinterpret_cast<cudaStream_t>(stream);
   const int lanes = static_cast<int>(layout->head_dim / (8 * kChunks));
   const uint64_t rows_per_cta = kThreads / lanes;
   const uint64_t want = (p.rows_total + rows_per_cta - 1) / rows_per_cta;
   const uint64_t cap = uint64_t{static_cast<uint32_t>(sm_count())} * 16;
   const unsigned grid = static_cast<unsigned>(want < cap ? want : cap);
-  switch (layout->head_dim) {
-    case 64: append_encode_kernel<64><<<grid, kThreads, 0, s>>>(p); break;
-    case 128: append_encode_kernel<128><<<grid, kThreads, 0, s>>>(p); break;
-    default: append_encode_kernel<256><<<grid, kThreads, 0, s>>>(p); break;
-  }
-  return cuda_status(cudaGetLastError());
+  void (*kernel)(Params) = layout->head_dim == 64    ? append_encode_kernel<64>
+                           : layout->head_dim == 128 ? append_encode_kernel<128>
+                                                     : append_encode_kernel<256>;
+  cudaLaunchConfig_t cfg{};
+  cfg.gridDim = dim3(grid);
+  cfg.blockDim = dim3(kThreads);
+  cfg.dynamicSmemBytes = 0;
+  cfg.stream = s;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = overlap_previous ? 1 : 0;
+  return cuda_status(cudaLaunchKernelEx(&cfg, kernel, p));
+}
+
+}  // namespace hlkv
+
+extern "C" int hlkv_append_encode(const HlkvPools* pools, const HlkvLayout* layout,
+                                  const HlkvExecDescriptor* d_table, uint32_t table_size,
+                                  const HlkvAppendTarget* d_targets, uint32_t n,
+                                  const uint16_t* d_tokens, uint32_t* d_err, hlkv_stream_t stream) {
+  return hlkv::launch_append_encode(pools, layout, d_table, table_size, d_targets, n, d_tokens, d_err, false,
+                                    reinterpret_cast<cudaStream_t>(stream));
 }

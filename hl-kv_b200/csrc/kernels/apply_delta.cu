@@ -28,6 +28,9 @@ __global__ void __launch_bounds__(kThreads)
                        uint32_t arena_size, const uint4* __restrict__ desc, uint32_t n_desc,
                        const uint2* __restrict__ ids, uint32_t n_id, const uint2* __restrict__ copy_src,
                        uint2* __restrict__ copy_dst, uint32_t n_copy, uint32_t* err) {
+  // A kernel launched after this one with programmatic serialization (the decode step's
+  // encoder) may start now; it waits for this grid before it reads what this grid writes.
+  dev::allow_dependents_to_launch();
   const uint64_t n_patch = uint64_t{n_desc} + n_id;
   const uint64_t total = n_patch + n_copy;
   const uint64_t stride = uint64_t{gridDim.x} * kThreads;

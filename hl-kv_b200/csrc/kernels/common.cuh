@@ -42,6 +42,17 @@ struct FastDiv {
 
 namespace dev {
 
+// Programmatic dependent launch (griddepcontrol, sm_90 and later).  launch_dependents lets a
+// kernel launched after this one with programmatic stream serialization start its CTAs
+// before this grid has finished; wait blocks until every grid this one depends on has
+// completed and its memory is visible (a no-op for an ordinary launch).
+__device__ __forceinline__ void allow_dependents_to_launch() {
+  asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
+}
+__device__ __forceinline__ void wait_for_prerequisites() {
+  asm volatile("griddepcontrol.wait;" ::: "memory");
+}
+
 // Streaming (evict-first) global loads and stores: the payload is read once and
 // the FP16 output is consumed by another kernel, so neither should displace
 // the descriptor table and arena from L2.

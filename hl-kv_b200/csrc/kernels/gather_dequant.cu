@@ -232,16 +232,8 @@ __device__ uint64_t exclusive_scan(uint64_t x, uint64_t* s_out, uint64_t* s_warp
   return total;
 }
 
-// Programmatic dependent launch (griddepcontrol, sm_90 and later).  launch_dependents lets a
-// kernel launched after this one with programmatic stream serialization start its CTAs as
-// this grid's CTAs retire; wait blocks until every grid this one depends on has completed
-// and its memory is visible (a no-op for an ordinary launch).
-__device__ __forceinline__ void allow_dependents_to_launch() {
-  asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
-}
-__device__ __forceinline__ void wait_for_prerequisites() {
-  asm volatile("griddepcontrol.wait;" ::: "memory");
-}
+using dev::allow_dependents_to_launch;
+using dev::wait_for_prerequisites;
 
 // Before wait_for_prerequisites() the kernel reads only the segments, the output offsets,
 // the arena and the descriptor table (the segment scan and the block resolution of the

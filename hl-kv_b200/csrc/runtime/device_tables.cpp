@@ -290,6 +290,23 @@ DeviceStatus DeviceTables::flush(cudaStream_t stream, const void* copy_src, void
   return launch(nullptr, 0, nullptr, 0, copy_src, copy_dst, n_copy, stream);
 }
 
+DeviceStatus DeviceTables::flush_deferred(cudaStream_t stream, const void* copy_src, void* copy_dst,
+                                          std::uint32_t n_copy) {
+  defer_release_ = true;
+  const DeviceStatus s = flush(stream, copy_src, copy_dst, n_copy);
+  defer_release_ = false;
+  return s;
+}
+
+DeviceStatus DeviceTables::release_staging(cudaStream_t stream) {
+  if (!release_pending_) return {};
+  release_pending_ = false;
+  DeviceGuard g(device_);
+  if (!g.ok()) return from_cuda(cudaErrorInvalidDevice);
+  if (const cudaError_t e = cudaEventRecord(staging_free_, stream); e != cudaSuccess) return from_cuda(e);
+  return {};
+}
+
 DeviceStatus DeviceTables::apply(const alloc::ExecDelta& delta, cudaStream_t stream) {
   if (DeviceStatus s = stage(delta); !s.ok()) return s;
   return upload_and_apply(delta, stream, nullptr, nullptr, 0);
@@ -384,7 +401,12 @@ DeviceStatus DeviceTables::upload_and_apply(const alloc::ExecDelta& delta, cudaS
       !s.ok()) {
     return s;
   }
-  // The staging buffers are free again once kernel (3) has read them.
+  // The staging buffers are free again once kernel (3) has read them (flush_deferred: once
+  // the caller's next launch has been queued, release_staging records it).
+  if (defer_release_) {
+    release_pending_ = true;
+    return {};
+  }
   if (const cudaError_t e = cudaEventRecord(staging_free_, stream); e != cudaSuccess) return from_cuda(e);
   return {};
 }

@@ -61,6 +61,14 @@ class DeviceTables {
   /// (device memory).  The decode step moves its append targets this way.
   [[nodiscard]] DeviceStatus flush(cudaStream_t stream, const void* copy_src, void* copy_dst,
                                    std::uint32_t n_copy);
+  /// flush(stream, copy_src, copy_dst, n_copy) that leaves the staging buffers marked busy
+  /// past the next operation queued on `stream`: no event is recorded after kernel (3), so a
+  /// kernel queued next may overlap it (programmatic dependent launch).  The caller queues
+  /// that kernel and then calls release_staging(stream).
+  [[nodiscard]] DeviceStatus flush_deferred(cudaStream_t stream, const void* copy_src, void* copy_dst,
+                                            std::uint32_t n_copy);
+  /// Records the staging buffers' release on `stream` after a flush_deferred (no-op otherwise).
+  [[nodiscard]] DeviceStatus release_staging(cudaStream_t stream);
   /// Uploads and applies an already collected delta.
   [[nodiscard]] DeviceStatus apply(const alloc::ExecDelta& delta, cudaStream_t stream);
   /// Applies an arena compaction (HeteroBlockTable::compact_arena) on `stream`: flushes
@@ -115,6 +123,8 @@ class DeviceTables {
   unsigned char* d_staging_ = nullptr;  // device copy of large deltas
   std::size_t d_staging_bytes_ = 0;
   cudaEvent_t staging_free_ = nullptr;  // recorded after kernel (3), the staging's reader
+  bool defer_release_ = false;    // inside flush_deferred: no staging event after kernel (3)
+  bool release_pending_ = false;  // a flush_deferred read the staging; release_staging records it
   alloc::ExecDelta delta_;    // collected, not yet flushed
   alloc::ExecDelta scratch_;  // the next collect_delta() before merging into delta_
   bool pending_ = false;

@@ -208,6 +208,9 @@ int hlkv_append_encode(const HlkvPools* pools, const HlkvLayout* layout,
  * Targets are unique per list, so all patches go in parallel.  Out-of-range
  * targets are skipped with HLKV_ERR_PATCH_RANGE.  The device restatement of
  * the reference's ExecMirror::apply (tests/project1/exec_mirror.hpp:23-49).
+ * The kernel allows a kernel queued after it with programmatic dependent launch to start
+ * before it completes; such a kernel must wait for it (griddepcontrol.wait) before reading
+ * d_table or d_arena.  An ordinarily launched kernel is not affected.
  */
 int hlkv_apply_delta(HlkvExecDescriptor* d_table, uint32_t table_size, uint32_t* d_arena,
                      uint32_t arena_size, const HlkvExecDescriptor* d_desc_patches,
@@ -565,8 +568,12 @@ uint32_t* hlkv_device_tables_error_word(const hlkv_device_tables* dt);
  * just before kernel (3) is queued, after the call's host-side checks, so that the two events
  * and one recorded after the call bracket the step's device work.  h_targets must be page-locked host memory (or device
  * memory), which the kernel reads in place (HLKV_INVALID_ARGUMENT for pageable memory), and
- * must stay untouched until the stream has passed kernel (3).  Returns the first failing
- * status; what was queued before it stays queued.  No counterpart in the reference: the
+ * must stay untouched until the stream has passed kernel (3).  Kernel (2) is launched with
+ * programmatic dependent launch: its first token loads overlap the end of kernel (3), and it
+ * waits for kernel (3) before reading d_targets and the descriptor table (d_tokens must
+ * be complete when the call is made, as for any work queued before kernel (3)).  With
+ * encode_event the event sits between the two kernels and they do not overlap.  Returns
+ * the first failing status; what was queued before it stays queued.  No counterpart in the reference: the
  * device side of the decode loop its plan describes.
  */
 int hlkv_decode_step_queue(hlkv_device_tables* dt, const HlkvPools* pools, const HlkvLayout* layout,
