@@ -190,9 +190,19 @@ def test_decode_step_queue_matches_oracle(hlkv_lib, oracle, cuda_device):
         tokens = _tokens(n, H, D, seed=100 + step)
         before = host_pools(wl)
         wl.dt.collect(wl.table)
+        # odd steps: the start and encode events (the kernels then do not overlap)
+        ev = [torch.cuda.Event(enable_timing=True) for _ in range(3)] if step % 2 else None
+        if ev:
+            for e in ev:
+                e.record()  # torch creates the CUDA event at its first record
         hlkv_lib.decode_step_queue(wl.dt, wl.hlkv_pools(), wl.layout, h_targets, d_targets,
-                                   torch.from_numpy(tokens.view(np.int16).copy()).cuda(), err)
+                                   torch.from_numpy(tokens.view(np.int16).copy()).cuda(), err,
+                                   start_event=ev[0] if ev else None, encode_event=ev[1] if ev else None)
+        if ev:
+            ev[2].record()
         torch.cuda.synchronize()
+        if ev:
+            assert ev[0].elapsed_time(ev[1]) > 0 and ev[1].elapsed_time(ev[2]) > 0
         assert int(err.item()) == 0
         assert np.array_equal(d_targets.cpu().numpy().view(np.uint32), targets)
         table = device_table_words(wl)
