@@ -283,14 +283,13 @@ class ClockSampler:
                 "reasons": reasons, "samples": len(inside), "window": window}
 
 
-def traffic_from_profile(workload: str) -> int | None:
-    """DRAM bytes (read + write) per launch of the gather kernel, from the committed ncu
-    summary of the same workload (profiles/gather_dequant_<workload>_full.md), or None.
-    The summary's table row "traffic (read + write) per launch" lists one capture per
-    column, the current kernel last."""
+def traffic_from_profile(summary: str) -> int | None:
+    """DRAM bytes (read + write) per launch of a kernel, from the committed ncu summary
+    profiles/<summary>.md, or None.  The summary's table row "traffic (read + write) per
+    launch" lists one capture per column, the current kernel last."""
     import re
     try:
-        with open(os.path.join(ROOT, "profiles", f"gather_dequant_{workload}_full.md")) as f:
+        with open(os.path.join(ROOT, "profiles", f"{summary}.md")) as f:
             row = re.search(r"^\| traffic \(read \+ write\) per launch \|(.*)$", f.read(), re.M)
         cells = re.findall(r"([0-9,]+) B", row.group(1)) if row else []
         return int(cells[-1].replace(",", "")) if cells else None
@@ -555,8 +554,8 @@ def run_hlkv(args) -> None:
             "roofline": {"bound": "hbm", "achieved": round(achieved, 2), "peak": peak,
                          "unit": "GB/s", "frac": round(achieved / peak, 4),
                          "peak_source": f"{peak_kind} (MEASURED_PEAKS.json hbm_gbs, copy bandwidth)",
-                         "traffic": traffic_from_profile("llama8b_layer" if args.workload == "llama8b"
-                                                         else args.workload),
+                         "traffic": traffic_from_profile("gather_dequant_" + (
+                             "llama8b_layer" if args.workload == "llama8b" else args.workload) + "_full"),
                          "kernel": "gather_dequant_kernel<128>",
                          "launch_ms": round(mean_launch_ms, 5)},
             "parity": parity["ok"] if parity is not None else None,
@@ -746,7 +745,9 @@ def run_decode(args) -> None:
             "roofline": {"bound": "hbm", "achieved": round(achieved, 2), "peak": peak, "unit": "GB/s",
                          "frac": round(achieved / peak, 4),
                          "peak_source": f"{peak_kind} (MEASURED_PEAKS.json hbm_gbs)",
-                         "traffic": None, "kernel": "append_encode_kernel<128>",
+                         # the profiled launch (decode_small) encodes the same 8192 appends
+                         "traffic": traffic_from_profile("append_encode_decode_small_full"),
+                         "kernel": "append_encode_kernel<128>",
                          "launch_ms": round(enc_mean, 5)},
             "e2e": {"value": round(job_bytes * args.steps / (wall_ms / 1e3) / 1e9, 2), "unit": "GB/s",
                     "h2d_bytes_per_step": n * 8, "d2h_bytes_per_step": 0,

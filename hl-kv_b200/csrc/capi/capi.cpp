@@ -444,8 +444,9 @@ int hlkv_decode_step_queue(hlkv_device_tables* dt, const HlkvPools* pools, const
       return HLKV_CUDA_ERROR;
     }
   }
+  // An event between the kernels leaves nothing to overlap: kernel (2) is then launched plainly.
   const int st = hlkv::launch_append_encode(pools, layout, hlkv_device_tables_table(dt), dt->dt.table_size(),
-                                            d_targets, n, d_tokens, d_err, true, s);
+                                            d_targets, n, d_tokens, d_err, encode_event == nullptr, s);
   const int r = static_cast<int>(dt->dt.release_staging(s).status);
   return st != HLKV_OK ? st : r;
 }

@@ -58,8 +58,10 @@ def test_decode_parity_reports_one_flipped_byte(hlkv_lib, oracle):
 def test_traffic_is_read_from_the_current_kernel_column():
     from bench import traffic_from_profile
     # one config-4 layer: the per-format kernel's capture is the last column
-    assert traffic_from_profile("llama8b_layer") == 2_915_823_616
-    assert traffic_from_profile("no_such_workload") is None
+    assert traffic_from_profile("gather_dequant_llama8b_layer_full") == 2_915_823_616
+    # the decode step's encoder, captured on the same 8192 appends
+    assert traffic_from_profile("append_encode_decode_small_full") == 34_006_528
+    assert traffic_from_profile("no_such_summary") is None
 
 
 if __name__ == "__main__":
