@@ -643,7 +643,7 @@ def run_decode(args) -> None:
         e[0].record(stream)
         e[1].record(stream)
     host = {"table_s": 0.0, "sync_s": 0.0}
-    nbytes = {"encode": 0, "delta": 0}
+    nbytes = {"encode": 0, "delta": 0, "h2d": 0}
 
     def step(k: int, timed: bool, split: bool = False) -> None:
         nonlocal tail_fmt
@@ -672,6 +672,7 @@ def run_decode(args) -> None:
             n8 = int((tail_fmt == hlkv.FP8_E4M3).sum())
             nbytes["encode"] += n * (rows_in + 16) + n8 * enc_out[1] + (n - n8) * enc_out[3]
             nbytes["delta"] += nd * 32 + ni * 12
+            nbytes["h2d"] += n * 8 + nd * 16 + ni * 8  # targets + staged delta, read in place
 
     for k in range(args.warmup):
         step(k, False)
@@ -750,7 +751,7 @@ def run_decode(args) -> None:
                          "kernel": "append_encode_kernel<128>",
                          "launch_ms": round(enc_mean, 5)},
             "e2e": {"value": round(job_bytes * args.steps / (wall_ms / 1e3) / 1e9, 2), "unit": "GB/s",
-                    "h2d_bytes_per_step": n * 8, "d2h_bytes_per_step": 0,
+                    "h2d_bytes_per_step": round(nbytes["h2d"] / args.steps), "d2h_bytes_per_step": 0,
                     "path": "host table ops + collect_delta -> hlkv_decode_step_queue (H2D of "
                             "targets and delta -> apply_delta -> append_encode), wall clock per step "
                             "(tokens resident)"},
