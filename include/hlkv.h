@@ -565,17 +565,18 @@ uint32_t* hlkv_device_tables_error_word(const hlkv_device_tables* dt);
  * hlkv_table_append_tokens wrote to h_targets into d_targets; then encode_event (a
  * cudaEvent_t, or NULL) is recorded and d_tokens[k] is encoded into target k through the
  * device tables (hlkv_append_encode).  start_event (a cudaEvent_t, or NULL) is recorded
- * just before kernel (3) is queued, after the call's host-side checks, so that the two events
- * and one recorded after the call bracket the step's device work.  h_targets must be page-locked host memory (or device
- * memory), which the kernel reads in place (HLKV_INVALID_ARGUMENT for pageable memory), and
- * must stay untouched until the stream has passed kernel (3).  Kernel (2) is launched with
- * programmatic dependent launch: while kernel (3) runs, it prefetches d_tokens into L2 and
- * issues its first token loads, and it waits for kernel (3) before reading d_targets and the
- * descriptor table (d_tokens must be complete when the call is made, as for any work queued
- * before kernel (3)).  With encode_event the event sits between the two kernels, and kernel
- * (2) is launched plainly after it.  Returns
- * the first failing status; what was queued before it stays queued.  No counterpart in the reference: the
- * device side of the decode loop its plan describes.
+ * just before kernel (3) is queued, after the call's host-side checks, so that the two
+ * events and one recorded after the call bracket the step's device work.
+ * h_targets must be page-locked host memory (or device memory), which the kernel reads in
+ * place (HLKV_INVALID_ARGUMENT for pageable memory), and must stay untouched until the
+ * stream has passed kernel (3).
+ * Kernel (2) is launched with programmatic dependent launch: while kernel (3) runs, it
+ * prefetches d_tokens into L2 and issues its first token loads, and it waits for kernel
+ * (3) before reading d_targets and the descriptor table (d_tokens must be complete when
+ * the call is made, as for any work queued before kernel (3)).  With encode_event the
+ * event sits between the two kernels, and kernel (2) is launched plainly after it.
+ * Returns the first failing status; what was queued before it stays queued.  No
+ * counterpart in the reference: the device side of the decode loop its plan describes.
  */
 int hlkv_decode_step_queue(hlkv_device_tables* dt, const HlkvPools* pools, const HlkvLayout* layout,
                            const HlkvAppendTarget* h_targets, HlkvAppendTarget* d_targets, uint32_t n,
