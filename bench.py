@@ -161,6 +161,20 @@ def shard_range(n: int, world: int, rank: int) -> tuple[int, int]:
     return lo, lo + base + (1 if rank < extra else 0)
 
 
+def cpu_model() -> str:
+    """The host CPU's model name (the first "model name" of /proc/cpuinfo), for the CPU
+    baseline's record."""
+    try:
+        with open("/proc/cpuinfo") as f:
+            for line in f:
+                if line.startswith("model name"):
+                    return line.split(":", 1)[1].strip()
+    except OSError:
+        pass
+    import platform
+    return platform.processor() or "unknown"
+
+
 def max_over_ranks(values, world: int, device) -> list[float]:
     """Element-wise maximum of per-rank timings (all ranks take part; a no-op at world 1)."""
     import torch
@@ -378,7 +392,7 @@ def cpu_gather_sample(wl, rows, out_dev, out_first_elem: int, timed: bool, min_w
             break
     assert err == 0
     gbs = nbytes * reps / wall / 1e9
-    return parity, {"value": round(gbs, 3), "unit": "GB/s", "cores": threads, "kind": kind,
+    return parity, {"value": round(gbs, 3), "unit": "GB/s", "cores": threads, "cpu_model": cpu_model(), "kind": kind,
                     "sample": f"{len(rows)} sequences of one layer ({nblocks} blocks, {nbytes / 1e6:.1f} MB "
                               f"algorithmic) x {reps} passes, {wall:.2f} s wall"}
 
@@ -503,7 +517,8 @@ def run_hlkv(args) -> None:
     if flush is not None or updates is not None:
         # the timed work is the launches, not the flushes or the host table updates between them
         total_ms = sum(step_ms)
-    total_ms, mean_step_ms = max_over_ranks([total_ms, statistics.mean(step_ms)], world, "cuda")
+    total_ms, mean_step_ms, median_step_ms = max_over_ranks(
+        [total_ms, statistics.mean(step_ms), statistics.median(step_ms)], world, "cuda")
 
     if spec["scaling"] == "weak":
         job_bytes = world * bytes_per_step
@@ -531,7 +546,8 @@ def run_hlkv(args) -> None:
         line = {
             "metric": METRIC, "value": round(value, 2), "unit": "GB/s", "n_gpus": world,
             "steps": args.steps, "warmup": args.warmup,
-            "ms_per_step": round(total_ms / args.steps, 5), "higher_is_better": True,
+            "ms_per_step": round(total_ms / args.steps, 5), "median_ms_per_step": round(median_step_ms, 5),
+            "higher_is_better": True,
             "scaling": spec["scaling"], "vs_baseline": None, "dtype": "fp16 out; fp16/e4m3/int4 in",
             "data": "synthetic (seeded N(0,1) + outlier channels, quantized on the GPU)",
             "config": static_config(args.workload, world),
@@ -836,7 +852,8 @@ def cpu_encode_sample(tokens, tail_fmt, H: int, D: int, n: int, min_wall_s: floa
     n8 = int((tail_fmt == 1).sum())
     nbytes = n * (2 * H * D * 2 + 16) + n8 * (2 * H * D + 2 * H * 4) + (n - n8) * (H * D + 2 * H * 8)
     return {"value": round(nbytes * reps / wall / 1e9, 3), "unit": "GB/s", "cores": threads,
-            "kind": kind, "sample": f"one step's {n} appended tokens ({x.shape[0]} rows of {D}) "
+            "cpu_model": cpu_model(), "kind": kind,
+            "sample": f"one step's {n} appended tokens ({x.shape[0]} rows of {D}) "
                                     f"x {reps} passes, {wall:.2f} s wall"}
 
 
@@ -1116,7 +1133,7 @@ def cpu_flat_sample(codes, params, fmt: int, group: int, min_wall_s: float = 10.
             break
     assert st == 0
     nbytes = m + 4 * p.shape[0] + 2 * m
-    return {"value": round(nbytes * reps / wall / 1e9, 3), "unit": "GB/s", "cores": 1, "kind": kind,
+    return {"value": round(nbytes * reps / wall / 1e9, 3), "unit": "GB/s", "cores": 1, "cpu_model": cpu_model(), "kind": kind,
             "sample": f"{m} of {codes.size} values x {reps} passes, {wall:.2f} s wall"}
 
 
@@ -1291,7 +1308,7 @@ def run_reference(args) -> None:
         "scaling": spec["scaling"], "vs_baseline": None, "dtype": "fp16 out; fp16/e4m3/int4 in",
         "data": "synthetic (seeded N(0,1) + outlier channels, quantize_reference)",
         "config": static_config(args.workload, world),
-        "cpu_baseline": {"value": round(value, 3), "unit": "GB/s", "cores": threads, "kind": kind,
+        "cpu_baseline": {"value": round(value, 3), "unit": "GB/s", "cores": threads, "cpu_model": cpu_model(), "kind": kind,
                          "sample": sample},
         "e2e": {"value": round(value, 3), "unit": "GB/s", "h2d_bytes_per_step": 0,
                 "d2h_bytes_per_step": 0},
@@ -1337,7 +1354,7 @@ def run_reference_flat(args, spec: dict, kind: str, threads: int) -> None:
         "scaling": "weak", "vs_baseline": None, "dtype": "e4m3 in; fp16 out",
         "data": "synthetic (seeded N(0,1), quantize_reference)",
         "config": static_config(args.workload, world),
-        "cpu_baseline": {"value": round(value, 3), "unit": "GB/s", "cores": threads, "kind": kind,
+        "cpu_baseline": {"value": round(value, 3), "unit": "GB/s", "cores": threads, "cpu_model": cpu_model(), "kind": kind,
                          "sample": f"the whole array ({n} values) per step"},
         "e2e": {"value": round(value, 3), "unit": "GB/s", "h2d_bytes_per_step": 0,
                 "d2h_bytes_per_step": 0},
@@ -1376,7 +1393,7 @@ def run_reference_decode(args, spec: dict, kind: str, threads: int) -> None:
         "scaling": "strong", "vs_baseline": None, "dtype": "fp16 in; e4m3/int4 out",
         "data": "synthetic (seeded N(0,1) tokens, formats .5/.5)",
         "config": static_config(args.workload, world),
-        "cpu_baseline": {"value": round(value, 3), "unit": "GB/s", "cores": threads, "kind": kind,
+        "cpu_baseline": {"value": round(value, 3), "unit": "GB/s", "cores": threads, "cpu_model": cpu_model(), "kind": kind,
                          "sample": f"one full step: {n} appended tokens ({x.shape[0]} rows of {D})"},
         "e2e": {"value": round(value, 3), "unit": "GB/s", "h2d_bytes_per_step": 0,
                 "d2h_bytes_per_step": 0},
